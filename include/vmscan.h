@@ -1,0 +1,206 @@
+/*
+ * vmscan.h — C ABI of the B200 (sm_100a) selective-scan library `libvmscan.so`.
+ *
+ * This is the drop-in boundary for the selective-scan (S6) hot path of
+ * mlx-vision-mamba.  Every entry point takes plain device pointers, element
+ * strides, sizes and a CUDA stream; none allocates memory, none synchronises
+ * the stream, and none holds state between calls (thread-safe).  Each returns
+ * an `int` status (VMSCAN_OK == 0) that `vmscan_strerror` turns into text.
+ *
+ * Reference interfaces replaced (paths inside the mlx-vision-mamba project):
+ *   - scan forward  : `selective_scan(x, delta, A, B, C, D) -> y`
+ *                     mlx_vision_mamba/mamba_block.py:20-74 (semantics), and the fused
+ *                     Metal launch `_launch_fused_fwd`
+ *                     mlx_vision_mamba/mamba_metal_fused.py:148-179 (kernel :21-63)
+ *   - scan VJP      : `_fused_scan_core_vjp` + `_launch_fused_bwd`
+ *                     mlx_vision_mamba/mamba_metal_fused.py:182-250 (kernel :66-145,
+ *                     reductions :213-224)
+ *   - gate          : `y * silu(z)` in MambaBlock.__call__, mamba_block.py:190
+ *   - directions    : permute/flip/unpermute helpers mamba_block.py:244-338 and
+ *                     `MultiDirectionalMambaBlock._apply_direction` :407-534, folded
+ *                     into the scan's (and the conv's) index maths
+ *   - conv1d + SiLU : `self.conv1d(x)[:, :L]` then `nn.silu`, mamba_block.py:129-132,170-171
+ *
+ * Layouts.  Sequence tensors are (batch, seq, channel) views with channel
+ * stride 1 and element strides {batch, seq} given by `vmscan_strides`;
+ * B, C, dB, dC are (batch, seq, d_state) views of the same kind.  A / dA are
+ * contiguous (d_inner, d_state); D / dD are contiguous (d_inner).  All data is
+ * fp32.  Sequence views must start on a 16-byte boundary and have strides that
+ * are multiples of 4 elements (TMA tensor-map rules); otherwise the call
+ * returns VMSCAN_ERR_ALIGN.  d_state must be 16 (the reference hard-codes a
+ * 16-float state, mamba_metal_fused.py:28).
+ */
+#ifndef VMSCAN_H
+#define VMSCAN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL means the legacy default stream. */
+typedef struct CUstream_st* vmscan_stream_t;
+
+enum vmscan_status {
+  VMSCAN_OK = 0,
+  VMSCAN_ERR_NULL = 1,       /* a required pointer is NULL */
+  VMSCAN_ERR_SHAPE = 2,      /* a size is <= 0 or out of range */
+  VMSCAN_ERR_DSTATE = 3,     /* d_state != 16 */
+  VMSCAN_ERR_ALIGN = 4,      /* pointer / stride breaks the 16-byte TMA rules */
+  VMSCAN_ERR_DIRECTION = 5,  /* bad direction descriptor */
+  VMSCAN_ERR_WORKSPACE = 6,  /* workspace missing or too small */
+  VMSCAN_ERR_DRIVER = 7,     /* tensor-map encoding refused by the driver */
+  VMSCAN_ERR_LAUNCH = 8,     /* kernel launch failed */
+  VMSCAN_ERR_TIMEOUT = 9,    /* a device-side wait ran out (see vmscan_device_status) */
+  VMSCAN_ERR_CONV = 10       /* conv kernel size unsupported (1..8) */
+};
+
+/*
+ * Scan direction.  The sequence of `seqlen` tokens is laid out row-major on
+ * `grid[0..ndim)`.  The scan visits tokens in the order of
+ * `transpose(grid, axes)` flattened row-major, reversed when `reverse` != 0.
+ * ndim == 0 means plain sequence order (grid/axes ignored).  This is the
+ * reference's `_permute_*` + `[:, ::-1, :]` pair (mamba_block.py:244-338,
+ * :443-534) without moving any data.
+ */
+typedef struct vmscan_direction {
+  int32_t ndim;
+  int32_t grid[4];
+  int32_t axes[4];
+  int32_t reverse;
+} vmscan_direction;
+
+/* Element strides of a (batch, seq, channel) view; channel stride is 1. */
+typedef struct vmscan_strides {
+  int64_t batch;
+  int64_t seq;
+} vmscan_strides;
+
+/* Library ABI version (major*100 + minor). */
+int vmscan_version(void);
+
+/* Static text for a status code. */
+const char* vmscan_strerror(int status);
+
+/*
+ * Number of fp32 elements of the checkpoint buffer written by vmscan_fwd and
+ * read by vmscan_bwd: the recurrent state (d_state floats per channel) at the
+ * end of every scan box of at most 16 steps.  Negative on a bad argument.
+ */
+int64_t vmscan_ckpt_elems(int64_t batch, int64_t seqlen, int64_t d_inner,
+                          int64_t d_state, const vmscan_direction* dir);
+
+/*
+ * Fused forward: y = (selective_scan(u, delta, A, B, C, D)) * silu(z).
+ * z == NULL drops the gate (plain reference `selective_scan` output).
+ * ckpt == NULL skips the checkpoints (inference); otherwise ckpt must hold
+ * vmscan_ckpt_elems(...) floats.
+ * Replaces mamba_metal_fused.py:148-179 (+ the gate at mamba_block.py:190).
+ */
+int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+               const float* u, vmscan_strides su,
+               const float* delta, vmscan_strides sdelta,
+               const float* A,
+               const float* B, vmscan_strides sB,
+               const float* C, vmscan_strides sC,
+               const float* D,
+               const float* z, vmscan_strides sz,
+               float* y, vmscan_strides sy,
+               float* ckpt,
+               const vmscan_direction* dir,
+               vmscan_stream_t stream);
+
+/*
+ * Workspace bytes needed by vmscan_bwd.  With recompute_ckpt != 0 the
+ * workspace also holds checkpoints that vmscan_bwd rebuilds itself (call
+ * vmscan_bwd with ckpt == NULL), matching the reference VJP, which recomputes
+ * the forward (mamba_metal_fused.py:241-244).  Negative on a bad argument.
+ */
+int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner,
+                                   int64_t d_state, const vmscan_direction* dir,
+                                   int recompute_ckpt);
+
+/*
+ * Fused VJP.  dy is the cotangent of the forward output (gated if z != NULL).
+ * Writes du, ddelta, dA, dB, dC, dD and (when z != NULL) dz; all outputs are
+ * overwritten, not accumulated.  Replaces mamba_metal_fused.py:182-250,
+ * including the host-side reductions at :213-224, which run on the device in
+ * a fixed order (deterministic).
+ */
+int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+               const float* u, vmscan_strides su,
+               const float* delta, vmscan_strides sdelta,
+               const float* A,
+               const float* B, vmscan_strides sB,
+               const float* C, vmscan_strides sC,
+               const float* D,
+               const float* z, vmscan_strides sz,
+               const float* ckpt,
+               const float* dy, vmscan_strides sdy,
+               float* du, vmscan_strides sdu,
+               float* ddelta, vmscan_strides sddelta,
+               float* dA,
+               float* dB, vmscan_strides sdB,
+               float* dC, vmscan_strides sdC,
+               float* dD,
+               float* dz, vmscan_strides sdz,
+               const vmscan_direction* dir,
+               void* workspace, size_t workspace_bytes,
+               vmscan_stream_t stream);
+
+/*
+ * Depthwise causal conv1d along the scan order, fused with SiLU:
+ *   out[tok(p)] = silu(bias + sum_k w[c, k] * x[tok(p - K + 1 + k)])
+ * where p is the scan position and tok() the direction's token map.  The
+ * weight uses MLX's Conv1d layout (channels, K, 1).  Replaces
+ * `silu(conv1d(x)[:, :L])`, mamba_block.py:129-132,170-171, on the permuted
+ * sequence of mamba_block.py:443-534.  K in 1..8; channels % 4 == 0.
+ */
+int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize,
+                           const float* x, vmscan_strides sx,
+                           const float* weight, const float* bias,
+                           float* out, vmscan_strides sout,
+                           const vmscan_direction* dir,
+                           vmscan_stream_t stream);
+
+int64_t vmscan_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t channels,
+                                          int64_t ksize);
+
+/* VJP of vmscan_conv1d_silu_fwd.  dweight / dbias are overwritten. */
+int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize,
+                           const float* x, vmscan_strides sx,
+                           const float* weight, const float* bias,
+                           const float* dout, vmscan_strides sdout,
+                           float* dx, vmscan_strides sdx,
+                           float* dweight, float* dbias,
+                           const vmscan_direction* dir,
+                           void* workspace, size_t workspace_bytes,
+                           vmscan_stream_t stream);
+
+/*
+ * Host-only introspection (no CUDA call): writes the token index visited at
+ * every scan step of `dir` into tokens[0..seqlen), computed the way the
+ * kernels compute it.  mode 0 enumerates the TMA boxes (box coordinates +
+ * row -> token, as the scan kernels and the dB/dC scatter do); mode 1 maps
+ * each scan position directly (as the conv kernels do).  geom (may be NULL)
+ * receives 16 int64 values: nsd, size[3], tstride[3], j, bj, nj, P, T,
+ * nboxes, reverse, 0, 0.  No reference counterpart: it exists so the index
+ * arithmetic of the direction fold is testable without a GPU.
+ */
+int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int64_t* tokens,
+                      int64_t* geom);
+
+/*
+ * Synchronises `stream` and returns the sticky device-side status (0 or
+ * VMSCAN_ERR_TIMEOUT, set when a kernel's bounded wait ran out and the kernel
+ * returned early); clears it when `clear` != 0.
+ */
+int vmscan_device_status(vmscan_stream_t stream, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VMSCAN_H */

@@ -1,0 +1,464 @@
+// vmscan.cu — C ABI of libvmscan.so (declared in include/vmscan.h).
+//
+// Host side of the selective-scan hot path: argument validation, the scan
+// geometry of a direction, TMA tensor-map encoding (the direction lives in
+// the maps' dims and strides) and kernel launches.  No allocation, no stream
+// synchronisation (except vmscan_device_status), no global state besides the
+// driver entry point and the sticky device status word.
+#include <cudaTypedefs.h>
+#include <mutex>
+
+#include "../../include/vmscan.h"
+#include "vmscan_bwd.cuh"
+#include "vmscan_common.cuh"
+#include "vmscan_conv.cuh"
+#include "vmscan_fwd.cuh"
+
+using namespace vmscan;
+
+// Sticky device status: kernels set it when a bounded wait gives up.
+__device__ int g_vmscan_status = 0;
+
+namespace {
+
+constexpr int kFwdNCW = 4;
+constexpr int kBwdNCW = 4;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int* status_ptr() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_vmscan_status) != cudaSuccess) return nullptr;
+  return static_cast<int*>(p);
+}
+
+struct ScanDim {
+  int64_t size;
+  int64_t tstride;
+};
+
+// Builds the scan geometry of `dir` for a sequence of `seqlen` tokens.
+int make_geom(int64_t batch, int64_t seqlen, int64_t d_inner, const vmscan_direction* dir, ScanGeom& g) {
+  if (batch <= 0 || seqlen <= 0 || d_inner <= 0) return VMSCAN_ERR_SHAPE;
+  if (batch > 65535 || seqlen > (int64_t(1) << 30) || d_inner > (int64_t(1) << 24)) return VMSCAN_ERR_SHAPE;
+  ScanDim dims[4];
+  int nd = 0;
+  if (dir == nullptr || dir->ndim == 0) {
+    dims[nd++] = {seqlen, 1};
+  } else {
+    const int n = dir->ndim;
+    if (n < 1 || n > 4) return VMSCAN_ERR_DIRECTION;
+    int64_t prod = 1;
+    bool seen[4] = {false, false, false, false};
+    for (int i = 0; i < n; ++i) {
+      if (dir->grid[i] < 1) return VMSCAN_ERR_DIRECTION;
+      prod *= dir->grid[i];
+      const int a = dir->axes[i];
+      if (a < 0 || a >= n || seen[a]) return VMSCAN_ERR_DIRECTION;
+      seen[a] = true;
+    }
+    if (prod != seqlen) return VMSCAN_ERR_DIRECTION;
+    int64_t ts[4];
+    int64_t acc = 1;
+    for (int i = n - 1; i >= 0; --i) {
+      ts[i] = acc;
+      acc *= dir->grid[i];
+    }
+    // fastest scan dim first; drop unit dims; merge dims contiguous in token order
+    for (int q = n - 1; q >= 0; --q) {
+      const int a = dir->axes[q];
+      const ScanDim sd = {dir->grid[a], ts[a]};
+      if (sd.size == 1) continue;
+      if (nd > 0 && sd.tstride == dims[nd - 1].tstride * dims[nd - 1].size) {
+        dims[nd - 1].size *= sd.size;
+      } else {
+        dims[nd++] = sd;
+      }
+    }
+    if (nd == 0) dims[nd++] = {1, 1};
+  }
+  if (nd > 3) return VMSCAN_ERR_DIRECTION;
+  g.nsd = nd;
+  for (int i = 0; i < 3; ++i) {
+    g.size[i] = i < nd ? int32_t(dims[i].size) : 1;
+    g.tstride[i] = i < nd ? dims[i].tstride : 0;
+  }
+  int64_t P = 1;
+  int j = nd - 1;
+  for (int i = 0; i < nd; ++i) {
+    if (i < nd - 1 && P * g.size[i] <= TMAX) {
+      P *= g.size[i];
+      continue;
+    }
+    j = i;
+    break;
+  }
+  const int64_t bj = std::min<int64_t>(g.size[j], TMAX / P);
+  g.j = j;
+  g.bj = int32_t(bj);
+  g.nj = int32_t((g.size[j] + bj - 1) / bj);
+  g.P = int32_t(P);
+  g.T = int32_t(P * bj);
+  int64_t nb = g.nj;
+  for (int i = j + 1; i < nd; ++i) nb *= g.size[i];
+  if (nb > (int64_t(1) << 30)) return VMSCAN_ERR_SHAPE;
+  g.nboxes = int32_t(nb);
+  g.reverse = (dir != nullptr && dir->reverse) ? 1 : 0;
+  g.batch = int32_t(batch);
+  g.d_inner = int32_t(d_inner);
+  g.seqlen = int32_t(seqlen);
+  return VMSCAN_OK;
+}
+
+void box_extent(const ScanGeom& g, cuuint32_t box[3]) {
+  for (int i = 0; i < 3; ++i) box[i] = (i < g.j) ? cuuint32_t(g.size[i]) : (i == g.j ? cuuint32_t(g.bj) : 1u);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Tensor map of a (batch, seq, inner) fp32 view seen in scan order:
+// dims {inner, scan0, scan1, scan2, batch}, box {box_inner, box...}.
+int encode_map(CUtensorMap* m, const void* ptr, int64_t inner, int box_inner, vmscan_strides st,
+               const ScanGeom& g) {
+  if (ptr == nullptr) return VMSCAN_ERR_NULL;
+  if (!aligned16(ptr)) return VMSCAN_ERR_ALIGN;
+  if ((g.seqlen > 1 && (st.seq <= 0 || st.seq % 4 != 0)) || (g.batch > 1 && (st.batch <= 0 || st.batch % 4 != 0)))
+    return VMSCAN_ERR_ALIGN;
+  auto fn = encode_fn();
+  if (fn == nullptr) return VMSCAN_ERR_DRIVER;
+  cuuint64_t dims[5];
+  cuuint64_t strides[4];
+  dims[0] = cuuint64_t(inner);
+  for (int i = 0; i < 3; ++i) {
+    dims[1 + i] = cuuint64_t(g.size[i]);
+    int64_t s = (i < g.nsd && g.size[i] > 1) ? g.tstride[i] * st.seq * 4 : 16;
+    strides[i] = cuuint64_t(s);
+  }
+  dims[4] = cuuint64_t(g.batch);
+  strides[3] = cuuint64_t(g.batch > 1 ? st.batch * 4 : 16);
+  for (int i = 0; i < 4; ++i)
+    if (strides[i] == 0 || strides[i] % 16 != 0 || strides[i] >= (cuuint64_t(1) << 40)) return VMSCAN_ERR_ALIGN;
+  cuuint32_t box3[3];
+  box_extent(g, box3);
+  cuuint32_t box[5] = {cuuint32_t(box_inner), box3[0], box3[1], box3[2], 1u};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VMSCAN_OK : VMSCAN_ERR_DRIVER;
+}
+
+#define VM_TRY(expr)                 \
+  do {                               \
+    const int _rc = (expr);          \
+    if (_rc != VMSCAN_OK) return _rc; \
+  } while (0)
+
+int check_launch() { return cudaGetLastError() == cudaSuccess ? VMSCAN_OK : VMSCAN_ERR_LAUNCH; }
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct BwdWorkspace {
+  size_t part, wA, wD, ck, total;
+};
+
+BwdWorkspace bwd_layout(const ScanGeom& g, int ndt, bool with_ck) {
+  BwdWorkspace w;
+  w.part = 0;
+  const size_t part_bytes = size_t(g.batch) * g.nboxes * ndt * TMAX * kPartRow * 4;
+  w.wA = align256(w.part + part_bytes);
+  w.wD = align256(w.wA + size_t(g.batch) * g.d_inner * NS * 4);
+  w.ck = align256(w.wD + size_t(g.batch) * g.d_inner * 4);
+  const size_t ck_bytes = with_ck ? size_t(g.batch) * g.nboxes * g.d_inner * NS * 4 : 0;
+  w.total = align256(w.ck + ck_bytes);
+  return w;
+}
+
+template <bool HAS_Z, bool SAVE_CK, bool STORE_Y>
+int launch_fwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
+               const CUtensorMap& mC, const CUtensorMap& my, const float* A, const float* D, float* ckpt,
+               const ScanGeom& g, cudaStream_t stream) {
+  using Cfg = FwdCfg<kFwdNCW>;
+  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
+    return VMSCAN_ERR_LAUNCH;
+  int* st = status_ptr();
+  if (st == nullptr) return VMSCAN_ERR_LAUNCH;
+  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, st);
+  return check_launch();
+}
+
+template <bool HAS_Z>
+int launch_bwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
+               const CUtensorMap& mB, const CUtensorMap& mC, const CUtensorMap& mdu, const CUtensorMap& mddt,
+               const CUtensorMap& mdz, const float* A, const float* D, const float* ckpt, float* wpart, float* wA,
+               float* wD, const ScanGeom& g, cudaStream_t stream) {
+  using Cfg = BwdCfg<kBwdNCW>;
+  auto kern = scan_bwd_kernel<kBwdNCW, HAS_Z>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
+    return VMSCAN_ERR_LAUNCH;
+  int* st = status_ptr();
+  if (st == nullptr) return VMSCAN_ERR_LAUNCH;
+  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ckpt, wpart, wA,
+                                                   wD, g, st);
+  return check_launch();
+}
+
+int check_common(int64_t d_state, const float* A, const float* D) {
+  if (d_state != NS) return VMSCAN_ERR_DSTATE;
+  if (A == nullptr || D == nullptr) return VMSCAN_ERR_NULL;
+  return VMSCAN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int vmscan_version(void) { return 100; }
+
+const char* vmscan_strerror(int status) {
+  switch (status) {
+    case VMSCAN_OK: return "ok";
+    case VMSCAN_ERR_NULL: return "a required pointer is NULL";
+    case VMSCAN_ERR_SHAPE: return "a size is out of range";
+    case VMSCAN_ERR_DSTATE: return "d_state must be 16";
+    case VMSCAN_ERR_ALIGN: return "pointer or stride breaks the 16-byte TMA alignment rules (channel stride 1, "
+                                  "16-byte base, strides multiple of 4 elements)";
+    case VMSCAN_ERR_DIRECTION: return "bad direction descriptor (grid product != seqlen, axes not a permutation, "
+                                      "or more than 3 non-mergeable scan dims)";
+    case VMSCAN_ERR_WORKSPACE: return "workspace missing or too small";
+    case VMSCAN_ERR_DRIVER: return "the CUDA driver refused the tensor map";
+    case VMSCAN_ERR_LAUNCH: return "kernel launch failed";
+    case VMSCAN_ERR_TIMEOUT: return "a device-side wait ran out; the kernel returned early";
+    case VMSCAN_ERR_CONV: return "conv kernel size must be 1..8 and channels a multiple of 4";
+    default: return "unknown vmscan status";
+  }
+}
+
+int64_t vmscan_ckpt_elems(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                          const vmscan_direction* dir) {
+  if (d_state != NS) return -VMSCAN_ERR_DSTATE;
+  ScanGeom g;
+  const int rc = make_geom(batch, seqlen, d_inner, dir, g);
+  if (rc != VMSCAN_OK) return -rc;
+  return int64_t(batch) * g.nboxes * d_inner * NS;
+}
+
+int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const float* u, vmscan_strides su,
+               const float* delta, vmscan_strides sdelta, const float* A, const float* B, vmscan_strides sB,
+               const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz, float* y,
+               vmscan_strides sy, float* ckpt, const vmscan_direction* dir, vmscan_stream_t stream) {
+  VM_TRY(check_common(d_state, A, D));
+  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
+  if (ckpt != nullptr && !aligned16(ckpt)) return VMSCAN_ERR_ALIGN;
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
+  using Cfg = FwdCfg<kFwdNCW>;
+  CUtensorMap mu, mdt, mz, mB, mC, my;
+  VM_TRY(encode_map(&mu, u, d_inner, Cfg::DT, su, g));
+  VM_TRY(encode_map(&mdt, delta, d_inner, Cfg::DT, sdelta, g));
+  if (z != nullptr) {
+    VM_TRY(encode_map(&mz, z, d_inner, Cfg::DT, sz, g));
+  } else {
+    mz = mu;
+  }
+  VM_TRY(encode_map(&mB, B, NS, NS, sB, g));
+  VM_TRY(encode_map(&mC, C, NS, NS, sC, g));
+  VM_TRY(encode_map(&my, y, d_inner, Cfg::DT, sy, g));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool hz = z != nullptr, ck = ckpt != nullptr;
+  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
+  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
+  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
+  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
+}
+
+int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                                   const vmscan_direction* dir, int recompute_ckpt) {
+  if (d_state != NS) return -VMSCAN_ERR_DSTATE;
+  ScanGeom g;
+  const int rc = make_geom(batch, seqlen, d_inner, dir, g);
+  if (rc != VMSCAN_OK) return -rc;
+  const int ndt = int((d_inner + BwdCfg<kBwdNCW>::DT - 1) / BwdCfg<kBwdNCW>::DT);
+  return int64_t(bwd_layout(g, ndt, recompute_ckpt != 0).total);
+}
+
+int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const float* u, vmscan_strides su,
+               const float* delta, vmscan_strides sdelta, const float* A, const float* B, vmscan_strides sB,
+               const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz,
+               const float* ckpt, const float* dy, vmscan_strides sdy, float* du, vmscan_strides sdu,
+               float* ddelta, vmscan_strides sddelta, float* dA, float* dB, vmscan_strides sdB, float* dC,
+               vmscan_strides sdC, float* dD, float* dz, vmscan_strides sdz, const vmscan_direction* dir,
+               void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
+  VM_TRY(check_common(d_state, A, D));
+  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || dy == nullptr || du == nullptr ||
+      ddelta == nullptr || dA == nullptr || dB == nullptr || dC == nullptr || dD == nullptr)
+    return VMSCAN_ERR_NULL;
+  if (z != nullptr && dz == nullptr) return VMSCAN_ERR_NULL;
+  if (ckpt != nullptr && !aligned16(ckpt)) return VMSCAN_ERR_ALIGN;
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
+  using Cfg = BwdCfg<kBwdNCW>;
+  static_assert(Cfg::DT == FwdCfg<kFwdNCW>::DT, "forward and backward channel tiles must agree");
+  const int ndt = int((d_inner + Cfg::DT - 1) / Cfg::DT);
+  const BwdWorkspace wl = bwd_layout(g, ndt, ckpt == nullptr);
+  if (workspace == nullptr || workspace_bytes < wl.total || !aligned16(workspace)) return VMSCAN_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  float* wpart = reinterpret_cast<float*>(ws + wl.part);
+  float* wA = reinterpret_cast<float*>(ws + wl.wA);
+  float* wD = reinterpret_cast<float*>(ws + wl.wD);
+  CUtensorMap mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz;
+  VM_TRY(encode_map(&mu, u, d_inner, Cfg::DT, su, g));
+  VM_TRY(encode_map(&mdt, delta, d_inner, Cfg::DT, sdelta, g));
+  if (z != nullptr) {
+    VM_TRY(encode_map(&mz, z, d_inner, Cfg::DT, sz, g));
+    VM_TRY(encode_map(&mdz, dz, d_inner, Cfg::DT, sdz, g));
+  } else {
+    mz = mu;
+    mdz = mu;
+  }
+  VM_TRY(encode_map(&mdy, dy, d_inner, Cfg::DT, sdy, g));
+  VM_TRY(encode_map(&mB, B, NS, NS, sB, g));
+  VM_TRY(encode_map(&mC, C, NS, NS, sC, g));
+  VM_TRY(encode_map(&mdu, du, d_inner, Cfg::DT, sdu, g));
+  VM_TRY(encode_map(&mddt, ddelta, d_inner, Cfg::DT, sddelta, g));
+  if (!aligned16(dB) || !aligned16(dC)) return VMSCAN_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float* ck = ckpt;
+  if (ck == nullptr) {
+    // Rebuild the checkpoints (the reference VJP also recomputes the forward).
+    float* ckw = reinterpret_cast<float*>(ws + wl.ck);
+    VM_TRY((launch_fwd<false, true, false>(mu, mdt, mu, mB, mC, mu, A, D, ckw, g, s)));
+    ck = ckw;
+  }
+  if (z != nullptr) {
+    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ck, wpart, wA, wD, g, s));
+  } else {
+    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ck, wpart, wA, wD, g, s));
+  }
+  reduce_dbc_kernel<<<dim3(unsigned(g.nboxes), unsigned(g.batch)), TMAX * kPartRow, 0, s>>>(
+      wpart, dB, sdB.batch, sdB.seq, dC, sdC.batch, sdC.seq, g, ndt);
+  VM_TRY(check_launch());
+  const int nA = int(d_inner * NS);
+  reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch), int(d_inner));
+  return check_launch();
+}
+
+int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,
+                           vmscan_strides sx, const float* weight, const float* bias, float* out,
+                           vmscan_strides sout, const vmscan_direction* dir, vmscan_stream_t stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr) return VMSCAN_ERR_NULL;
+  if (ksize < 1 || ksize > CONV_KMAX || channels % 4 != 0) return VMSCAN_ERR_CONV;
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, channels, dir, g));
+  if (!aligned16(x) || !aligned16(out) || !aligned16(bias) || sx.seq % 4 || sx.batch % 4 || sout.seq % 4 ||
+      sout.batch % 4)
+    return VMSCAN_ERR_ALIGN;
+  const dim3 grid(unsigned((channels / 4 + CONV_THREADS - 1) / CONV_THREADS),
+                  unsigned((seqlen + CONV_CHUNK - 1) / CONV_CHUNK), unsigned(batch));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (ksize <= 4)
+    conv_silu_fwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
+                                                         sout.seq, int(channels), int(ksize), g);
+  else
+    conv_silu_fwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
+                                                         sout.seq, int(channels), int(ksize), g);
+  return check_launch();
+}
+
+int64_t vmscan_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize) {
+  if (batch <= 0 || seqlen <= 0 || channels <= 0) return -VMSCAN_ERR_SHAPE;
+  if (ksize < 1 || ksize > CONV_KMAX) return -VMSCAN_ERR_CONV;
+  const int64_t nchunk = (seqlen + CONV_CHUNK - 1) / CONV_CHUNK;
+  return int64_t(align256(size_t(batch) * nchunk * channels * (CONV_KMAX + 1) * 4));
+}
+
+int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,
+                           vmscan_strides sx, const float* weight, const float* bias, const float* dout,
+                           vmscan_strides sdout, float* dx, vmscan_strides sdx, float* dweight, float* dbias,
+                           const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
+                           vmscan_stream_t stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || dout == nullptr || dx == nullptr ||
+      dweight == nullptr || dbias == nullptr)
+    return VMSCAN_ERR_NULL;
+  if (ksize < 1 || ksize > CONV_KMAX || channels % 4 != 0) return VMSCAN_ERR_CONV;
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, channels, dir, g));
+  if (!aligned16(x) || !aligned16(dout) || !aligned16(dx) || !aligned16(bias) || sx.seq % 4 || sx.batch % 4 ||
+      sdout.seq % 4 || sdout.batch % 4 || sdx.seq % 4 || sdx.batch % 4)
+    return VMSCAN_ERR_ALIGN;
+  const int64_t need = vmscan_conv1d_bwd_workspace_bytes(batch, seqlen, channels, ksize);
+  if (workspace == nullptr || int64_t(workspace_bytes) < need) return VMSCAN_ERR_WORKSPACE;
+  const int nchunk = int((seqlen + CONV_CHUNK - 1) / CONV_CHUNK);
+  const dim3 grid(unsigned((channels / 4 + CONV_THREADS - 1) / CONV_THREADS), unsigned(nchunk), unsigned(batch));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float* wpart = static_cast<float*>(workspace);
+  if (ksize <= 4)
+    conv_silu_bwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
+                                                         sdout.seq, dx, sdx.batch, sdx.seq, wpart, int(channels),
+                                                         int(ksize), g);
+  else
+    conv_silu_bwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
+                                                         sdout.seq, dx, sdx.batch, sdx.seq, wpart, int(channels),
+                                                         int(ksize), g);
+  VM_TRY(check_launch());
+  const int n = int(channels * (ksize + 1));
+  conv_reduce_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(wpart, dweight, dbias, int(batch) * nchunk,
+                                                                int(channels), int(ksize));
+  return check_launch();
+}
+
+int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int64_t* tokens, int64_t* geom) {
+  if (tokens == nullptr) return VMSCAN_ERR_NULL;
+  ScanGeom g;
+  VM_TRY(make_geom(1, seqlen, 1, dir, g));
+  if (geom != nullptr) {
+    const int64_t v[16] = {g.nsd,  g.size[0], g.size[1], g.size[2], g.tstride[0], g.tstride[1],
+                           g.tstride[2], g.j, g.bj, g.nj, g.P, g.T, g.nboxes, g.reverse, 0, 0};
+    for (int i = 0; i < 16; ++i) geom[i] = v[i];
+  }
+  if (mode == 1) {
+    for (int64_t p = 0; p < seqlen; ++p) tokens[p] = scan_pos_token(g, int(p));
+    return VMSCAN_OK;
+  }
+  int64_t q = 0;
+  for (int i = 0; i < g.nboxes; ++i) {
+    const int k = g.reverse ? g.nboxes - 1 - i : i;
+    int c[3], nv;
+    box_coords(g, k, c, nv);
+    for (int s = 0; s < nv; ++s) {
+      const int r = g.reverse ? nv - 1 - s : s;
+      if (q >= seqlen) return VMSCAN_ERR_SHAPE;
+      tokens[q++] = box_row_token(g, c, r);
+    }
+  }
+  return q == seqlen ? VMSCAN_OK : VMSCAN_ERR_SHAPE;
+}
+
+int vmscan_device_status(vmscan_stream_t stream, int clear) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return VMSCAN_ERR_LAUNCH;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_vmscan_status, sizeof(int)) != cudaSuccess) return VMSCAN_ERR_LAUNCH;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_vmscan_status, &zero, sizeof(int)) != cudaSuccess) return VMSCAN_ERR_LAUNCH;
+  }
+  return v;
+}
+
+}  // extern "C"

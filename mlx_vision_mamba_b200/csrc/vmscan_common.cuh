@@ -1,0 +1,243 @@
+// vmscan_common.cuh — PTX helpers (mbarrier, TMA, MUFU ex2, named barriers),
+// the scan-box geometry shared by every kernel, and the sticky device status.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vmscan {
+
+constexpr int NS = 16;     // d_state; the reference hard-codes 16 (mamba_metal_fused.py:28)
+constexpr int TMAX = 16;   // scan steps per box (one TMA box, one checkpoint interval)
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Bounded waits: each try_wait may suspend at most kSuspendNs; after kWaitLimit
+// tries (about one second) the wait gives up, sets the device status and the
+// CTA's abort flag, and the kernel drains and returns.
+constexpr uint32_t kSuspendNs = 1000;
+constexpr uint32_t kWaitLimit = 1u << 20;
+
+constexpr int kStatusTimeout = 9;  // == VMSCAN_ERR_TIMEOUT
+
+// ---------------------------------------------------------------------------
+// Scan geometry.  The scan order of a direction is described by up to three
+// "scan dims" (fastest first) with a size and a token stride each.  A box is
+// `T = P * bj` consecutive scan steps: the full extent of dims < j (product P)
+// times `bj` steps of dim j.  Boxes are numbered in scan order; the last box
+// along dim j may be ragged, in which case only its first `nvalid` rows exist.
+// ---------------------------------------------------------------------------
+struct ScanGeom {
+  int32_t nsd;            // number of scan dims (1..3)
+  int32_t size[3];        // scan dim sizes, fastest first (unused dims: 1)
+  int64_t tstride[3];     // token stride of each scan dim
+  int32_t j;              // the dim the box is partial along
+  int32_t bj;             // box extent along dim j
+  int32_t nj;             // ceil(size[j] / bj)
+  int32_t P;              // product of size[i] for i < j
+  int32_t T;              // rows per box = P * bj (<= TMAX)
+  int32_t nboxes;         // boxes per sequence
+  int32_t reverse;        // scan runs last -> first
+  int32_t batch;
+  int32_t d_inner;
+  int32_t seqlen;
+};
+
+// Box k -> TMA coordinates of scan dims 0..2 and the number of valid rows.
+__host__ __device__ __forceinline__ void box_coords(const ScanGeom& g, int k, int c[3], int& nvalid) {
+  int rest = k;
+  const int cj = (rest % g.nj) * g.bj;
+  rest /= g.nj;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (i < g.j) {
+      c[i] = 0;
+    } else if (i == g.j) {
+      c[i] = cj;
+    } else if (i < g.nsd) {
+      c[i] = rest % g.size[i];
+      rest /= g.size[i];
+    } else {
+      c[i] = 0;
+    }
+  }
+  const int sj = g.j == 0 ? g.size[0] : (g.j == 1 ? g.size[1] : g.size[2]);
+  const int left = sj - cj;
+  nvalid = g.P * (left < g.bj ? left : g.bj);
+}
+
+// Token index of row r of a box with coordinates c.
+__host__ __device__ __forceinline__ int64_t box_row_token(const ScanGeom& g, const int c[3], int r) {
+  int64_t tok = 0;
+  int rem = r;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (i >= g.nsd) break;
+    int x;
+    if (i < g.j) {
+      x = rem % g.size[i];
+      rem /= g.size[i];
+    } else if (i == g.j) {
+      x = c[i] + rem;
+    } else {
+      x = c[i];
+    }
+    tok += (int64_t)x * g.tstride[i];
+  }
+  return tok;
+}
+
+// Scan position p (0 = first step taken) -> token index.
+__host__ __device__ __forceinline__ int64_t scan_pos_token(const ScanGeom& g, int p) {
+  if (g.reverse) p = g.seqlen - 1 - p;
+  int64_t tok = 0;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    if (i >= g.nsd) break;
+    const int x = p % g.size[i];
+    p /= g.size[i];
+    tok += (int64_t)x * g.tstride[i];
+  }
+  return tok;
+}
+
+#if defined(__CUDACC__)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// silu(z) = z / (1 + 2^(-z*log2 e))
+__device__ __forceinline__ float silu_f(float z) {
+  return __fdividef(z, 1.0f + ex2_approx(-kLog2e * z));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity.  Returns false (after setting the
+// CTA abort flag and the device status) when the wait ran out or another
+// thread of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+  }
+  *abort_flag = 1;
+  atomicExch(status, kStatusTimeout);
+  return false;
+}
+
+// 5-D tiled TMA load into shared memory, completing on an mbarrier.
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 5-D tiled TMA store from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
+                                             int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Make generic-proxy shared-memory writes visible to the TMA (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+// Four lanes of a quad each hold v[0..3] (partials for four consecutive scan
+// steps).  Returns, in lane q of the quad, the quad-wide sum for step q.
+__device__ __forceinline__ float quad_transpose_sum(const float v[4], int q) {
+  const bool hi2 = (q & 2) != 0;
+  float keep0 = hi2 ? v[2] : v[0];
+  float keep1 = hi2 ? v[3] : v[1];
+  const float send0 = hi2 ? v[0] : v[2];
+  const float send1 = hi2 ? v[1] : v[3];
+  keep0 += __shfl_xor_sync(0xffffffffu, send0, 2);
+  keep1 += __shfl_xor_sync(0xffffffffu, send1, 2);
+  const bool hi1 = (q & 1) != 0;
+  const float keep = hi1 ? keep1 : keep0;
+  const float send = hi1 ? keep0 : keep1;
+  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
+__device__ __forceinline__ unsigned char* align_up_1024(unsigned char* p) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+#endif  // __CUDACC__
+
+}  // namespace vmscan

@@ -1,0 +1,226 @@
+// vmscan_conv.cuh — depthwise causal conv1d along a scan direction, fused
+// with SiLU, and its VJP.
+//
+// Reference: MambaBlock applies `nn.Conv1d(d_inner, d_inner, kernel_size=K,
+// padding=K-1, groups=d_inner)` to the (possibly permuted / reversed)
+// sequence, keeps the first L outputs and applies SiLU
+// (mlx_vision_mamba/mamba_block.py:129-132,170-171; permutations :443-534):
+//   out[p] = silu(bias + sum_{k<K} w[c, k] * x[p - K + 1 + k])   (zero for p-K+1+k < 0)
+// where p runs over scan positions.  Here p is mapped to its token through the
+// direction, so the permuted copy of the reference never exists.
+//
+// Layout: a CTA covers 128 float4 channel groups x CONV_CHUNK scan positions
+// of one batch row; the tokens of those positions are computed once into
+// shared memory; every thread slides a register window along the chunk, so
+// each x element is read once (plus a K-1 halo per chunk).
+#pragma once
+
+#include "vmscan_common.cuh"
+
+namespace vmscan {
+
+constexpr int CONV_CHUNK = 32;
+constexpr int CONV_KMAX = 8;
+constexpr int CONV_THREADS = 128;
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+__device__ __forceinline__ void fma4(float4& a, float w, const float4& x) {
+  a.x = fmaf(w, x.x, a.x);
+  a.y = fmaf(w, x.y, a.y);
+  a.z = fmaf(w, x.z, a.z);
+  a.w = fmaf(w, x.w, a.w);
+}
+
+__device__ __forceinline__ float dsilu_f(float pre) {
+  const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * pre));
+  return sig * fmaf(pre, 1.0f - sig, 1.0f);
+}
+
+// Window KW (4 or 8) >= K; the K real taps sit at the newest end of the window.
+template <int KW>
+__global__ void __launch_bounds__(CONV_THREADS)
+    conv_silu_fwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
+                         const float* __restrict__ bias, float* __restrict__ out, int64_t sob, int64_t sos, int C,
+                         int K, const ScanGeom g) {
+  __shared__ int64_t tok[CONV_CHUNK + CONV_KMAX];
+  const int p0 = blockIdx.y * CONV_CHUNK;
+  const int b = blockIdx.z;
+  const int L = g.seqlen;
+  const int span = CONV_CHUNK + K - 1;
+  for (int t = threadIdx.x; t < span; t += blockDim.x) {
+    const int p = p0 - (K - 1) + t;
+    tok[t] = (p >= 0 && p < L) ? scan_pos_token(g, p) : int64_t(-1);
+  }
+  __syncthreads();
+  const int c4 = blockIdx.x * CONV_THREADS + threadIdx.x;
+  if (c4 * 4 >= C) return;
+  float wv[KW][4];
+#pragma unroll
+  for (int m = 0; m < KW; ++m) {
+    const int k = m - (KW - K);  // tap index of window slot m
+#pragma unroll
+    for (int q = 0; q < 4; ++q) wv[m][q] = (k >= 0) ? w[size_t(c4 * 4 + q) * K + k] : 0.f;
+  }
+  const float4 bv = ldg4(bias + c4 * 4);
+  float4 win[KW];
+#pragma unroll
+  for (int m = 0; m < KW; ++m) win[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* xb = x + b * sxb + c4 * 4;
+  float* ob = out + b * sob + c4 * 4;
+  for (int t = 0; t < span; ++t) {
+    const int64_t tk = tok[t];
+#pragma unroll
+    for (int m = 0; m < KW - 1; ++m) win[m] = win[m + 1];
+    win[KW - 1] = (tk >= 0) ? ldg4(xb + tk * sxs) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (t >= K - 1 && tk >= 0) {
+      float4 acc = bv;
+#pragma unroll
+      for (int m = 0; m < KW; ++m) {
+        acc.x = fmaf(wv[m][0], win[m].x, acc.x);
+        acc.y = fmaf(wv[m][1], win[m].y, acc.y);
+        acc.z = fmaf(wv[m][2], win[m].z, acc.z);
+        acc.w = fmaf(wv[m][3], win[m].w, acc.w);
+      }
+      float4 o;
+      o.x = silu_f(acc.x);
+      o.y = silu_f(acc.y);
+      o.z = silu_f(acc.z);
+      o.w = silu_f(acc.w);
+      *reinterpret_cast<float4*>(ob + tk * sos) = o;
+    }
+  }
+}
+
+// VJP.  For the chunk [p0, p0+CHUNK) it recomputes the pre-activation on
+// [p0, p0+CHUNK+K-1), forms dpre = dout * silu'(pre), emits
+//   dx[p'] = sum_k w[k] dpre[p' + K - 1 - k]
+// and per-thread partial sums of dw[k] = sum_p dpre[p] x[p-K+1+k] and
+// dbias = sum_p dpre[p] over the chunk, written to wpart[b][chunk][c][KMAX+1].
+template <int KW>
+__global__ void __launch_bounds__(CONV_THREADS)
+    conv_silu_bwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
+                         const float* __restrict__ bias, const float* __restrict__ dout, int64_t sdb, int64_t sds,
+                         float* __restrict__ dx, int64_t sxgb, int64_t sxgs, float* __restrict__ wpart, int C,
+                         int K, const ScanGeom g) {
+  __shared__ int64_t tok[CONV_CHUNK + 2 * CONV_KMAX];
+  const int p0 = blockIdx.y * CONV_CHUNK;
+  const int nchunk = gridDim.y;
+  const int b = blockIdx.z;
+  const int L = g.seqlen;
+  const int span = CONV_CHUNK + 2 * K - 2;
+  for (int t = threadIdx.x; t < span; t += blockDim.x) {
+    const int p = p0 - (K - 1) + t;
+    tok[t] = (p >= 0 && p < L) ? scan_pos_token(g, p) : int64_t(-1);
+  }
+  __syncthreads();
+  const int c4 = blockIdx.x * CONV_THREADS + threadIdx.x;
+  if (c4 * 4 >= C) return;
+  float wv[KW][4];
+#pragma unroll
+  for (int m = 0; m < KW; ++m) {
+    const int k = m - (KW - K);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) wv[m][q] = (k >= 0) ? w[size_t(c4 * 4 + q) * K + k] : 0.f;
+  }
+  const float4 bv = ldg4(bias + c4 * 4);
+  float4 xw[KW], dw_acc[KW], dpw[KW];
+#pragma unroll
+  for (int m = 0; m < KW; ++m) {
+    xw[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dw_acc[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dpw[m] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float4 db_acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* xb = x + b * sxb + c4 * 4;
+  const float* gb = dout + b * sdb + c4 * 4;
+  float* dxb = dx + b * sxgb + c4 * 4;
+  for (int t = 0; t < span; ++t) {
+    const int p = p0 - (K - 1) + t;
+    const int64_t tk = tok[t];
+#pragma unroll
+    for (int m = 0; m < KW - 1; ++m) xw[m] = xw[m + 1];
+    xw[KW - 1] = (tk >= 0) ? ldg4(xb + tk * sxs) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 dp = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p >= p0 && tk >= 0) {
+      float4 pre = bv;
+#pragma unroll
+      for (int m = 0; m < KW; ++m) {
+        pre.x = fmaf(wv[m][0], xw[m].x, pre.x);
+        pre.y = fmaf(wv[m][1], xw[m].y, pre.y);
+        pre.z = fmaf(wv[m][2], xw[m].z, pre.z);
+        pre.w = fmaf(wv[m][3], xw[m].w, pre.w);
+      }
+      const float4 go = ldg4(gb + tk * sds);
+      dp.x = go.x * dsilu_f(pre.x);
+      dp.y = go.y * dsilu_f(pre.y);
+      dp.z = go.z * dsilu_f(pre.z);
+      dp.w = go.w * dsilu_f(pre.w);
+      if (p < p0 + CONV_CHUNK) {
+#pragma unroll
+        for (int m = 0; m < KW; ++m) {
+          dw_acc[m].x = fmaf(dp.x, xw[m].x, dw_acc[m].x);
+          dw_acc[m].y = fmaf(dp.y, xw[m].y, dw_acc[m].y);
+          dw_acc[m].z = fmaf(dp.z, xw[m].z, dw_acc[m].z);
+          dw_acc[m].w = fmaf(dp.w, xw[m].w, dw_acc[m].w);
+        }
+        db_acc.x += dp.x;
+        db_acc.y += dp.y;
+        db_acc.z += dp.z;
+        db_acc.w += dp.w;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < KW - 1; ++m) dpw[m] = dpw[m + 1];
+    dpw[KW - 1] = dp;
+    // dx at p' = p - (K - 1): taps k read dpre[p - k] = dpw[KW - 1 - k]
+    const int pp = p - (K - 1);
+    if (pp >= p0 && pp < p0 + CONV_CHUNK && pp < L) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < KW; ++k) {
+        const int m = KW - K + k;  // window slot of tap k
+        if (k < K) {
+          acc.x = fmaf(wv[m][0], dpw[KW - 1 - k].x, acc.x);
+          acc.y = fmaf(wv[m][1], dpw[KW - 1 - k].y, acc.y);
+          acc.z = fmaf(wv[m][2], dpw[KW - 1 - k].z, acc.z);
+          acc.w = fmaf(wv[m][3], dpw[KW - 1 - k].w, acc.w);
+        }
+      }
+      const int64_t tkp = tok[t - (K - 1)];
+      *reinterpret_cast<float4*>(dxb + tkp * sxgs) = acc;
+    }
+  }
+  // partials: slot k < K holds dw[k] (window slot KW-K+k), slot CONV_KMAX holds dbias
+  float* wp = wpart + ((size_t(b) * nchunk + blockIdx.y) * C + c4 * 4) * (CONV_KMAX + 1);
+  const float dbq[4] = {db_acc.x, db_acc.y, db_acc.z, db_acc.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      if (k < K) {
+        const float4 v = dw_acc[KW - K + k];
+        const float vq = q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
+        wp[q * (CONV_KMAX + 1) + k] = vq;
+      }
+    }
+    wp[q * (CONV_KMAX + 1) + CONV_KMAX] = dbq[q];
+  }
+}
+
+// dweight (C, K) and dbias (C): sum partials over (batch, chunk) in order.
+__global__ void conv_reduce_kernel(const float* __restrict__ wpart, float* __restrict__ dw, float* __restrict__ db,
+                                   int nrows, int C, int K) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= C * (K + 1)) return;
+  const int c = idx / (K + 1), k = idx % (K + 1);
+  const int slot = (k < K) ? k : CONV_KMAX;
+  float acc = 0.f;
+  for (int r = 0; r < nrows; ++r) acc += wpart[(size_t(r) * C + c) * (CONV_KMAX + 1) + slot];
+  if (k < K)
+    dw[size_t(c) * K + k] = acc;
+  else
+    db[c] = acc;
+}
+
+}  // namespace vmscan

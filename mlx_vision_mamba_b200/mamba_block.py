@@ -1,0 +1,208 @@
+"""Mamba blocks for B200: the host-side mirror of mlx_vision_mamba/mamba_block.py.
+
+Class names, constructor arguments, parameter names and parameter shapes follow
+the reference (MLX layouts, e.g. conv1d.weight is (d_inner, d_conv, 1)), so an
+MLX checkpoint's arrays load by name.  The selective scan, its SiLU gate and the
+causal conv1d+SiLU run in the sm_100a kernels of libvmscan.so; the projections
+are cuBLAS GEMMs.  Multi-directional scans never build permuted copies: each
+direction is a descriptor passed to the kernels (direction.py).
+
+Deliberate deviations from the reference, all documented:
+  * `scan_mode` defaults to "cuda_fused" and is threaded through every wrapper
+    (the reference never forwards it, mamba_block.py:202,223-224,402-405).
+  * The reference's Metal modes ("metal", "metal_train", "metal_fused") select
+    the CUDA kernels; the CPU Python scans ("sequential", "chunked",
+    "parallel") are not part of this package and unknown modes raise instead of
+    silently falling back (mamba_block.py:121-122).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .direction import BACKWARD, ScanDirection, directions_for
+from .scan import conv1d_silu_cuda, selective_scan_cuda
+
+GPU_SCAN_MODES = ("cuda_fused", "metal_fused", "metal_train", "metal")
+CPU_SCAN_MODES = ("sequential", "chunked", "parallel")
+
+
+def _mlx_uniform_(t: torch.Tensor, scale: float) -> torch.Tensor:
+    with torch.no_grad():
+        return t.uniform_(-scale, scale)
+
+
+class Linear(nn.Linear):
+    """nn.Linear with MLX's default init: U(-1/sqrt(in), 1/sqrt(in)) for weight and bias."""
+
+    def reset_parameters(self) -> None:
+        scale = math.sqrt(1.0 / self.in_features)
+        _mlx_uniform_(self.weight, scale)
+        if self.bias is not None:
+            _mlx_uniform_(self.bias, scale)
+
+
+class LayerNorm(nn.LayerNorm):
+    """MLX nn.LayerNorm defaults: eps 1e-5, weight 1, bias 0."""
+
+
+class DepthwiseConv1d(nn.Module):
+    """Parameters of MLX's nn.Conv1d(C, C, K, padding=K-1, groups=C) in MLX layout.
+
+    weight (C, K, 1) ~ U(-s, s) with s = sqrt(1 / (C * K)) and bias zeros, the
+    MLX Conv1d initialisation.  The computation itself (causal, along the
+    scan order, fused with SiLU) is `conv1d_silu_cuda`.
+    """
+
+    def __init__(self, channels: int, kernel_size: int):
+        super().__init__()
+        self.channels = channels
+        self.kernel_size = kernel_size
+        self.weight = nn.Parameter(torch.empty(channels, kernel_size, 1))
+        self.bias = nn.Parameter(torch.zeros(channels))
+        _mlx_uniform_(self.weight, math.sqrt(1.0 / (channels * kernel_size)))
+
+    def silu_along(self, x: torch.Tensor, direction: Optional[ScanDirection]) -> torch.Tensor:
+        return conv1d_silu_cuda(x, self.weight, self.bias, direction)
+
+
+class MambaBlock(nn.Module):
+    """in_proj -> causal depthwise conv1d -> SiLU -> x_proj -> dt_proj -> softplus
+    -> selective scan -> y * SiLU(z) -> out_proj (mamba_block.py:77-192).
+
+    `forward(x, direction=None)`: x is (B, L, d_model) in token order; with a
+    direction the conv and the scan run along that order and the output comes
+    back in token order, i.e. `unpermute(block(permute(x)))` of the reference
+    without the copies.
+    """
+
+    def __init__(
+        self,
+        d_model: int = 384,
+        d_state: int = 16,
+        d_conv: int = 4,
+        expand_factor: int = 2,
+        scan_mode: str = "cuda_fused",
+    ):
+        super().__init__()
+        if scan_mode in CPU_SCAN_MODES:
+            raise ValueError(
+                f"scan_mode={scan_mode!r} is a CPU Python scan of the reference; this package only "
+                "implements the CUDA path (scan_mode='cuda_fused')"
+            )
+        if scan_mode not in GPU_SCAN_MODES:
+            raise ValueError(f"unknown scan_mode {scan_mode!r}; expected one of {GPU_SCAN_MODES}")
+        self.d_model = d_model
+        self.d_state = d_state
+        self.d_inner = d_model * expand_factor
+        self.d_conv = d_conv
+        self.scan_mode = scan_mode
+        self.dt_rank = math.ceil(d_model / 16)
+
+        self.in_proj = Linear(d_model, 2 * self.d_inner, bias=False)
+        self.conv1d = DepthwiseConv1d(self.d_inner, d_conv)
+        self.x_proj = Linear(self.d_inner, self.dt_rank + 2 * d_state, bias=False)
+        self.dt_proj = Linear(self.dt_rank, self.d_inner, bias=True)
+        a = torch.arange(1, d_state + 1, dtype=torch.float32).unsqueeze(0).repeat(self.d_inner, 1)
+        self.A_log = nn.Parameter(torch.log(a))
+        self.D = nn.Parameter(torch.ones(self.d_inner))
+        self.out_proj = Linear(self.d_inner, d_model, bias=False)
+
+    def forward(self, x: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
+        dn, r, n = self.d_inner, self.dt_rank, self.d_state
+        xz = self.in_proj(x)
+        x_branch = xz[:, :, :dn]
+        z = xz[:, :, dn:]
+        x_branch = self.conv1d.silu_along(x_branch, direction)
+        x_dbc = self.x_proj(x_branch)
+        dt = x_dbc[:, :, :r]
+        B_proj = x_dbc[:, :, r : r + n]
+        C_proj = x_dbc[:, :, r + n :]
+        delta = self.dt_proj(dt)
+        delta = torch.log(1.0 + torch.exp(delta))  # softplus written as in mamba_block.py:181
+        A = -torch.exp(self.A_log)
+        y = selective_scan_cuda(x_branch, delta, A, B_proj, C_proj, self.D, z=z, direction=direction)
+        return self.out_proj(y)
+
+
+class ResidualMambaBlock(nn.Module):
+    """x + mamba(norm(x)) (mamba_block.py:195-205)."""
+
+    def __init__(self, d_model=384, d_state=16, d_conv=4, expand_factor=2, scan_mode="cuda_fused"):
+        super().__init__()
+        self.norm = LayerNorm(d_model)
+        self.mamba = MambaBlock(d_model, d_state, d_conv, expand_factor, scan_mode)
+
+    def forward(self, x):
+        return x + self.mamba(self.norm(x))
+
+
+class BidirectionalMambaBlock(nn.Module):
+    """x + fwd(norm(x)) + flip(bwd(flip(norm(x)))) (mamba_block.py:208-237); the flips
+    are the BACKWARD direction of the kernels."""
+
+    def __init__(self, d_model=384, d_state=16, d_conv=4, expand_factor=2, scan_mode="cuda_fused"):
+        super().__init__()
+        self.norm = LayerNorm(d_model)
+        self.forward_mamba = MambaBlock(d_model, d_state, d_conv, expand_factor, scan_mode)
+        self.backward_mamba = MambaBlock(d_model, d_state, d_conv, expand_factor, scan_mode)
+
+    def forward(self, x):
+        h = self.norm(x)
+        y_fwd = self.forward_mamba(h)
+        y_bwd = self.backward_mamba(h, BACKWARD)
+        return x + y_fwd + y_bwd
+
+
+class MultiDirectionalMambaBlock(nn.Module):
+    """K independent MambaBlocks, one per scan direction, summed plus residual
+    (mamba_block.py:341-566).  Directions follow `_apply_direction` (:407-534);
+    when the sequence is not the full grid only blocks 0 and 1 run, forward and
+    reversed (:550-559)."""
+
+    def __init__(
+        self,
+        d_model: int = 384,
+        d_state: int = 16,
+        d_conv: int = 4,
+        expand_factor: int = 2,
+        num_directions: int = 2,
+        grid_shape: Optional[Tuple[int, ...]] = None,
+        scan_mode: str = "cuda_fused",
+    ):
+        super().__init__()
+        if num_directions not in (2, 4, 6, 8):
+            raise ValueError(f"num_directions must be 2, 4, 6, or 8, got {num_directions}")
+        need = {4: 2, 6: 3, 8: 4}
+        if num_directions > 2:
+            if grid_shape is None:
+                raise ValueError("grid_shape is required when num_directions > 2")
+            if len(grid_shape) != need[num_directions]:
+                raise ValueError(
+                    f"K={num_directions} requires a {need[num_directions]}-D grid_shape, got {grid_shape}"
+                )
+        self.num_directions = num_directions
+        self.grid_shape = tuple(grid_shape) if grid_shape is not None else None
+        self.norm = LayerNorm(d_model)
+        self.mamba_blocks = nn.ModuleList(
+            [MambaBlock(d_model, d_state, d_conv, expand_factor, scan_mode) for _ in range(num_directions)]
+        )
+        self.directions = directions_for(num_directions, self.grid_shape)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        n = x.shape[1]
+        h = self.norm(x)
+        expected = math.prod(self.grid_shape) if self.grid_shape is not None else n
+        if n != expected and self.num_directions > 2:
+            y_fwd = self.mamba_blocks[0](h)
+            y_bwd = self.mamba_blocks[1](h, BACKWARD)
+            return x + y_fwd + y_bwd
+        y = self.mamba_blocks[0](h, self.directions[0])
+        for k in range(1, self.num_directions):
+            y = y + self.mamba_blocks[k](h, self.directions[k])
+        return x + y

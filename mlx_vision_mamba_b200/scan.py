@@ -1,0 +1,280 @@
+"""Selective scan and direction-aware conv1d+SiLU as autograd functions over libvmscan.so.
+
+`selective_scan_cuda(x, delta, A, B, C, D, z=None, direction=None)` is the
+drop-in for the reference's scan functions, which share the positional
+signature `scan(x, delta, A, B, C, D) -> y` (mlx_vision_mamba/mamba_block.py:20-74,
+mamba_metal_fused.py:253-267).  Two keyword extensions: `z` fuses the gate
+`y * silu(z)` of MambaBlock (mamba_block.py:190) into the kernel, and
+`direction` folds a multi-directional scan order into the kernel's indexing.
+
+The custom VJP mirrors `_fused_scan_core.vjp` (mamba_metal_fused.py:236-250):
+it returns gradients for all primals (and dz), reducing dA, dB, dC and dD on
+the device.  Instead of recomputing the full forward and storing h for every
+step (a (B, L, D, N) buffer in the reference), the forward saves the state at
+the end of every 16-step box and the VJP recomputes each box from it.
+
+There is no CPU path: inputs must be CUDA tensors and libvmscan.so must load.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _native
+from .direction import ScanDirection
+
+D_STATE = 16
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _strides(t: Optional[torch.Tensor]) -> _native.Strides:
+    if t is None:
+        return _native.Strides(0, 0)
+    return _native.Strides(t.stride(0), t.stride(1))
+
+
+def _tma_compatible(t: torch.Tensor) -> bool:
+    """True when the (B, L, C) view meets the TMA rules of include/vmscan.h."""
+    if t.dtype != torch.float32 or t.dim() != 3 or t.stride(2) != 1 and t.size(2) > 1:
+        return False
+    if t.data_ptr() % 16:
+        return False
+    b, l, _ = t.shape
+    if l > 1 and (t.stride(1) <= 0 or t.stride(1) % 4):
+        return False
+    if b > 1 and (t.stride(0) <= 0 or t.stride(0) % 4):
+        return False
+    return True
+
+
+def _prepare(t: torch.Tensor) -> torch.Tensor:
+    """Return a TMA-compatible fp32 view of t, copying only when needed.
+
+    Strided views such as the reference's `xz[:, :, :d_inner]` slices pass
+    through untouched; a copy is made only for other dtypes, a non-unit
+    channel stride, or strides that are not multiples of 4 elements (then the
+    channel dim is padded to a multiple of 4 in storage).
+    """
+    if t.dtype != torch.float32:
+        t = t.float()
+    if _tma_compatible(t):
+        return t
+    b, l, c = t.shape
+    cp = (c + 3) // 4 * 4
+    buf = torch.empty((b, l, cp), dtype=torch.float32, device=t.device)
+    out = buf[:, :, :c]
+    out.copy_(t)
+    return out
+
+
+def _dir_ptr(direction: Optional[ScanDirection]):
+    if direction is None:
+        return None
+    return ctypes.byref(direction.to_native())
+
+
+def _check_inputs(x, delta, A, B, C, D, z):
+    for name, t in (("x", x), ("delta", delta), ("A", A), ("B", B), ("C", C), ("D", D)):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError(f"selective_scan_cuda: `{name}` must be a CUDA tensor (there is no CPU path)")
+    if z is not None and not z.is_cuda:
+        raise RuntimeError("selective_scan_cuda: `z` must be a CUDA tensor")
+    if x.dim() != 3:
+        raise ValueError(f"x must be (B, L, D_inner), got {tuple(x.shape)}")
+    bt, l, dn = x.shape
+    if A.dim() != 2 or A.shape[0] != dn:
+        raise ValueError(f"A must be (D_inner, N), got {tuple(A.shape)}")
+    n = A.shape[1]
+    if n != D_STATE:
+        raise ValueError(f"d_state must be {D_STATE} (the kernel holds a 16-float state), got {n}")
+    if tuple(delta.shape) != (bt, l, dn):
+        raise ValueError(f"delta must be {(bt, l, dn)}, got {tuple(delta.shape)}")
+    for name, t in (("B", B), ("C", C)):
+        if tuple(t.shape) != (bt, l, n):
+            raise ValueError(f"{name} must be {(bt, l, n)}, got {tuple(t.shape)}")
+    if tuple(D.shape) != (dn,):
+        raise ValueError(f"D must be ({dn},), got {tuple(D.shape)}")
+    if z is not None and tuple(z.shape) != (bt, l, dn):
+        raise ValueError(f"z must be {(bt, l, dn)}, got {tuple(z.shape)}")
+
+
+class _SelectiveScanFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, delta, A, B, C, D, z, direction):
+        lib = _native.load()
+        bt, l, dn = x.shape
+        u_ = _prepare(x)
+        dt_ = _prepare(delta)
+        B_ = _prepare(B)
+        C_ = _prepare(C)
+        z_ = _prepare(z) if z is not None else None
+        A_ = A.detach().float().contiguous()
+        D_ = D.detach().float().contiguous()
+        y = torch.empty((bt, l, dn), dtype=torch.float32, device=x.device)
+        need_grad = any(ctx.needs_input_grad[:7])
+        dptr = _dir_ptr(direction)
+        ckpt = None
+        if need_grad:
+            n_ck = lib.vmscan_ckpt_elems(bt, l, dn, D_STATE, dptr)
+            if n_ck < 0:
+                _native.check(-n_ck, "vmscan_ckpt_elems")
+            ckpt = torch.empty(n_ck, dtype=torch.float32, device=x.device)
+        st = lib.vmscan_fwd(
+            bt, l, dn, D_STATE,
+            _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
+            _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
+            _ptr(z_), _strides(z_), _ptr(y), _strides(y), _ptr(ckpt), dptr, _stream(x),
+        )
+        _native.check(st, "vmscan_fwd")
+        if need_grad:
+            ctx.save_for_backward(u_, dt_, A_, B_, C_, D_, z_, ckpt)
+        ctx.direction = direction
+        ctx.has_z = z is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        lib = _native.load()
+        u_, dt_, A_, B_, C_, D_, z_, ckpt = ctx.saved_tensors
+        bt, l, dn = u_.shape
+        dev = u_.device
+        dy_ = _prepare(dy)
+        f32 = dict(dtype=torch.float32, device=dev)
+        du = torch.empty((bt, l, dn), **f32)
+        ddelta = torch.empty((bt, l, dn), **f32)
+        dA = torch.empty((dn, D_STATE), **f32)
+        dB = torch.empty((bt, l, D_STATE), **f32)
+        dC = torch.empty((bt, l, D_STATE), **f32)
+        dD = torch.empty((dn,), **f32)
+        dz = torch.empty((bt, l, dn), **f32) if ctx.has_z else None
+        dptr = _dir_ptr(ctx.direction)
+        ws_bytes = lib.vmscan_bwd_workspace_bytes(bt, l, dn, D_STATE, dptr, 0)
+        if ws_bytes < 0:
+            _native.check(-ws_bytes, "vmscan_bwd_workspace_bytes")
+        ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
+        st = lib.vmscan_bwd(
+            bt, l, dn, D_STATE,
+            _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
+            _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
+            _ptr(z_), _strides(z_), _ptr(ckpt),
+            _ptr(dy_), _strides(dy_),
+            _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta),
+            _ptr(dA), _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD),
+            _ptr(dz), _strides(dz),
+            dptr, _ptr(ws), ws.numel(), _stream(u_),
+        )
+        _native.check(st, "vmscan_bwd")
+        return du, ddelta, dA, dB, dC, dD, dz, None
+
+
+def selective_scan_cuda(
+    x: torch.Tensor,
+    delta: torch.Tensor,
+    A: torch.Tensor,
+    B: torch.Tensor,
+    C: torch.Tensor,
+    D: torch.Tensor,
+    z: Optional[torch.Tensor] = None,
+    direction: Optional[ScanDirection] = None,
+) -> torch.Tensor:
+    """Fused selective scan (S6) on sm_100a.
+
+    Args (shapes as in mlx_vision_mamba/mamba_block.py:35-40):
+        x:     (B, L, D_inner)   input after conv1d + SiLU
+        delta: (B, L, D_inner)   discretisation steps
+        A:     (D_inner, 16)     state matrix (negative)
+        B, C:  (B, L, 16)        input / output projections
+        D:     (D_inner,)        skip
+        z:     optional (B, L, D_inner) gate; returns y * silu(z)
+        direction: optional ScanDirection; tokens are visited in that order
+            and y is returned in token order.
+    Returns y (B, L, D_inner), fp32.
+    """
+    _check_inputs(x, delta, A, B, C, D, z)
+    return _SelectiveScanFn.apply(x, delta, A, B, C, D, z, direction)
+
+
+# Reference entry-point names (mlx_vision_mamba/__init__.py:14-19) bound to the
+# CUDA implementation, so code importing them keeps working.
+def selective_scan(x, delta, A, B, C, D):
+    return selective_scan_cuda(x, delta, A, B, C, D)
+
+
+selective_scan_metal = selective_scan
+selective_scan_metal_trainable = selective_scan
+selective_scan_metal_fused = selective_scan
+
+
+class _ConvSiluFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, direction):
+        lib = _native.load()
+        bt, l, c = x.shape
+        k = weight.shape[1]
+        x_ = _prepare(x)
+        w_ = weight.detach().float().contiguous()
+        b_ = bias.detach().float().contiguous()
+        out = torch.empty((bt, l, c), dtype=torch.float32, device=x.device)
+        st = lib.vmscan_conv1d_silu_fwd(
+            bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(out), _strides(out),
+            _dir_ptr(direction), _stream(x),
+        )
+        _native.check(st, "vmscan_conv1d_silu_fwd")
+        ctx.save_for_backward(x_, w_, b_)
+        ctx.direction = direction
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        lib = _native.load()
+        x_, w_, b_ = ctx.saved_tensors
+        bt, l, c = x_.shape
+        k = w_.shape[1]
+        dout_ = _prepare(dout)
+        dx = torch.empty((bt, l, c), dtype=torch.float32, device=x_.device)
+        dw = torch.empty_like(w_)
+        db = torch.empty_like(b_)
+        ws_bytes = lib.vmscan_conv1d_bwd_workspace_bytes(bt, l, c, k)
+        if ws_bytes < 0:
+            _native.check(-ws_bytes, "vmscan_conv1d_bwd_workspace_bytes")
+        ws = torch.empty(int(ws_bytes), dtype=torch.uint8, device=x_.device)
+        st = lib.vmscan_conv1d_silu_bwd(
+            bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(dout_), _strides(dout_),
+            _ptr(dx), _strides(dx), _ptr(dw), _ptr(db), _dir_ptr(ctx.direction), _ptr(ws), ws.numel(),
+            _stream(x_),
+        )
+        _native.check(st, "vmscan_conv1d_silu_bwd")
+        return dx, dw, db, None
+
+
+def conv1d_silu_cuda(
+    x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, direction: Optional[ScanDirection] = None
+) -> torch.Tensor:
+    """silu(causal depthwise conv1d(x)) along the scan order of `direction`.
+
+    x: (B, L, C) CUDA fp32, channel-last as in MLX; weight: (C, K, 1) in MLX's
+    Conv1d layout; bias: (C,).  Equivalent to `silu(conv1d(x_perm)[:, :L])`
+    un-permuted (mlx_vision_mamba/mamba_block.py:129-132,170-171).
+    """
+    if not (x.is_cuda and weight.is_cuda and bias.is_cuda):
+        raise RuntimeError("conv1d_silu_cuda: inputs must be CUDA tensors (there is no CPU path)")
+    if x.dim() != 3 or weight.dim() != 3 or weight.shape[0] != x.shape[2] or weight.shape[2] != 1:
+        raise ValueError(f"bad shapes x={tuple(x.shape)} weight={tuple(weight.shape)}")
+    return _ConvSiluFn.apply(x, weight, bias, direction)
+
+
+def device_status(device: Optional[torch.device] = None, clear: bool = True) -> int:
+    """Synchronise the current stream and return the sticky device status (0 = ok)."""
+    lib = _native.load()
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return int(lib.vmscan_device_status(ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream), int(clear)))

@@ -1,0 +1,192 @@
+"""CUDA selective scan (forward + VJP, gate, directions) against the CPU oracle."""
+
+import ctypes
+
+import pytest
+import torch
+
+from golden_cases import SCAN_CASES, load
+from mlx_vision_mamba_b200 import ScanDirection, _native, device_status, directions_for, selective_scan_cuda
+from oracle import scan_ref
+from parity import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+NAMES = ["u", "delta", "A", "B", "C", "D"]
+
+
+def cuda_vjp(inp, gated, direction=None, dev="cuda"):
+    keys = NAMES + (["z"] if gated else [])
+    lv = {k: inp[k].to(dev).float().clone().requires_grad_(True) for k in keys}
+    y = selective_scan_cuda(lv["u"], lv["delta"], lv["A"], lv["B"], lv["C"], lv["D"],
+                            z=lv.get("z"), direction=direction)
+    y.backward(inp["dy"].to(dev).float())
+    torch.cuda.synchronize()
+    return y.detach().cpu(), {"d" + k: lv[k].grad.detach().cpu() for k in keys}
+
+
+def oracle_vjp(inp, gated, direction=None, dtype=torch.float64):
+    """Oracle on the direction-permuted sequence, results returned in token order."""
+    if direction is None:
+        return scan_ref.scan_vjp(inp, gated, dtype)
+    L = inp["u"].shape[1]
+    idx = torch.tensor(direction.scan_order(L))
+    inv = torch.empty_like(idx)
+    inv[idx] = torch.arange(L)
+    p = dict(inp)
+    for k in ("u", "delta", "B", "C", "z", "dy"):
+        p[k] = inp[k][:, idx]
+    y, g = scan_ref.scan_vjp(p, gated, dtype)
+    y = y[:, inv]
+    for k in ("du", "ddelta", "dB", "dC", "dz"):
+        if k in g:
+            g[k] = g[k][:, inv]
+    return y, g
+
+
+def check_all(inp, gated, direction=None, tag=""):
+    y, g = cuda_vjp(inp, gated, direction)
+    y64, g64 = oracle_vjp(inp, gated, direction, torch.float64)
+    y32, g32 = oracle_vjp(inp, gated, direction, torch.float32)
+    assert_parity(f"{tag} y", y, y64, y32)
+    for k in g64:
+        assert_parity(f"{tag} {k}", g[k], g64[k], g32[k])
+
+
+SHAPES = [
+    (1, 1, 4, True),
+    (2, 2, 8, True),
+    (1, 15, 12, False),
+    (1, 16, 32, True),
+    (2, 17, 40, True),
+    (2, 31, 36, False),
+    (1, 33, 64, True),
+    (3, 100, 40, True),
+    (2, 196, 768, True),
+    (1, 1024, 32, True),
+    (1, 4096, 24, False),
+]
+
+
+@pytest.mark.parametrize("b,l,dn,gated", SHAPES)
+def test_scan_matches_oracle(b, l, dn, gated):
+    inp = scan_ref.sweep_inputs(b, l, dn, seed=l * 7 + dn)
+    check_all(inp, gated, tag=f"({b},{l},{dn},{gated})")
+
+
+def test_scan_random_A_and_large_delta():
+    inp = scan_ref.sweep_inputs(2, 77, 48, seed=5)
+    g = torch.Generator().manual_seed(9)
+    inp["A"] = -torch.exp(torch.randn(48, 16, generator=g))
+    inp["delta"] = torch.nn.functional.softplus(torch.randn(2, 77, 48, generator=g))
+    inp["D"] = torch.randn(48, generator=g)
+    check_all(inp, True, tag="randA")
+
+
+@pytest.mark.parametrize(
+    "K,grid",
+    [(2, None), (4, (14, 14)), (4, (3, 5)), (6, (8, 8, 8)), (6, (2, 3, 5)), (8, (8, 4, 4, 4)), (8, (2, 3, 2, 2))],
+)
+def test_directions_match_permuted_oracle(K, grid):
+    L = 1
+    for gdim in grid or (45,):
+        L *= gdim
+    inp = scan_ref.sweep_inputs(2, L, 32, seed=K * 100 + L)
+    for k, d in enumerate(directions_for(K, grid)):
+        check_all(inp, True, d, tag=f"K{K} dir{k}")
+
+
+def test_strided_views_match_contiguous():
+    """MambaBlock passes slices of xz and x_dbc; the kernels read them in place."""
+    b, l, dn, r = 2, 50, 64, 24
+    inp = scan_ref.sweep_inputs(b, l, dn, seed=3)
+    xz = torch.cat([inp["u"], inp["z"]], dim=-1).cuda()
+    xdbc = torch.cat([torch.randn(b, l, r), inp["B"], inp["C"]], dim=-1).cuda()
+    u, z = xz[:, :, :dn], xz[:, :, dn:]
+    B, C = xdbc[:, :, r:r + 16], xdbc[:, :, r + 16:]
+    dev = {k: inp[k].cuda() for k in ("delta", "A", "D")}
+    y1 = selective_scan_cuda(u, dev["delta"], dev["A"], B, C, dev["D"], z=z)
+    y2 = selective_scan_cuda(u.contiguous(), dev["delta"], dev["A"], B.contiguous(), C.contiguous(), dev["D"],
+                             z=z.contiguous())
+    torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+
+
+def test_unaligned_channel_count_is_padded():
+    inp = scan_ref.sweep_inputs(2, 21, 10, seed=4)  # 10 channels: strides not multiples of 4
+    check_all(inp, True, tag="dn10")
+
+
+def test_backward_is_deterministic():
+    inp = scan_ref.sweep_inputs(2, 300, 96, seed=11)
+    y1, g1 = cuda_vjp(inp, True)
+    y2, g2 = cuda_vjp(inp, True)
+    assert torch.equal(y1, y2)
+    for k in g1:
+        assert torch.equal(g1[k], g2[k]), k
+
+
+def test_bwd_without_checkpoints_recomputes_them():
+    """vmscan_bwd(ckpt=NULL) rebuilds the checkpoints like the reference VJP."""
+    lib = _native.load()
+    b, l, dn = 2, 70, 64
+    inp = scan_ref.sweep_inputs(b, l, dn, seed=6)
+    t = {k: v.cuda().contiguous() for k, v in inp.items()}
+    S = lambda x: _native.Strides(x.stride(0), x.stride(1))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def bwd(ckpt):
+        outs = {k: torch.empty_like(t["u"]) for k in ("du", "ddelta", "dz")}
+        outs["dA"] = torch.empty(dn, 16, device="cuda")
+        outs["dB"] = torch.empty(b, l, 16, device="cuda")
+        outs["dC"] = torch.empty(b, l, 16, device="cuda")
+        outs["dD"] = torch.empty(dn, device="cuda")
+        ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, 16, None, int(ckpt is None))
+        ws = torch.empty(ws_n, dtype=torch.uint8, device="cuda")
+        st = lib.vmscan_bwd(
+            b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]), t["A"].data_ptr(),
+            t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]), t["D"].data_ptr(), t["z"].data_ptr(),
+            S(t["z"]), None if ckpt is None else ckpt.data_ptr(), t["dy"].data_ptr(), S(t["dy"]),
+            outs["du"].data_ptr(), S(outs["du"]), outs["ddelta"].data_ptr(), S(outs["ddelta"]),
+            outs["dA"].data_ptr(), outs["dB"].data_ptr(), S(outs["dB"]), outs["dC"].data_ptr(), S(outs["dC"]),
+            outs["dD"].data_ptr(), outs["dz"].data_ptr(), S(outs["dz"]), None, ws.data_ptr(), ws_n, stream)
+        assert st == 0, lib.vmscan_strerror(st)
+        torch.cuda.synchronize()
+        return outs
+
+    n_ck = lib.vmscan_ckpt_elems(b, l, dn, 16, None)
+    ck = torch.empty(n_ck, device="cuda")
+    y = torch.empty_like(t["u"])
+    st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
+                        t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
+                        t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), ck.data_ptr(), None,
+                        stream)
+    assert st == 0
+    a = bwd(ck)
+    r = bwd(None)
+    for k in a:
+        assert torch.equal(a[k], r[k]), k
+
+
+@pytest.mark.parametrize("name", SCAN_CASES)
+def test_golden_scan_fixtures(name):
+    rec = load(name)
+    y, g = cuda_vjp(rec["inputs"], rec["gated"])
+    y64, g64 = scan_ref.scan_vjp(rec["inputs"], rec["gated"], torch.float64)
+    assert_parity(f"{name} y", y, y64, rec["y"])
+    for k in rec["grads"]:
+        assert_parity(f"{name} {k}", g[k], g64[k], rec["grads"][k])
+
+
+def test_errors_are_raised_not_hidden():
+    inp = scan_ref.sweep_inputs(1, 8, 8, seed=0)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        selective_scan_cuda(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"])
+    t = {k: v.cuda() for k, v in inp.items()}
+    with pytest.raises(ValueError, match="d_state"):
+        selective_scan_cuda(t["u"], t["delta"], t["A"][:, :8], t["B"][..., :8], t["C"][..., :8], t["D"])
+
+
+def test_device_status_is_clean():
+    inp = scan_ref.sweep_inputs(2, 64, 64, seed=1)
+    cuda_vjp(inp, True, ScanDirection(reverse=True))
+    assert device_status() == 0
