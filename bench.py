@@ -259,7 +259,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--batch", type=int, default=WORKLOAD["batch"], help="per-GPU batch (profiling runs)")
+    ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
+    ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
     args = ap.parse_args()
+    WORKLOAD.update(batch=args.batch, seqlen=args.seqlen, d_inner=args.dinner)
     if args.impl == "reference":
         run_reference(args)
         return
@@ -353,7 +357,7 @@ def main():
                 "workload": workload_name(),
                 "batch_per_gpu": b, "global_batch": b * world, "seq_len": l, "d_inner": d, "d_state": N_STATE,
                 "gated": True, "parallelism": f"weak x{world} (independent batch shards, no collective)",
-                "l2": "inputs 6.4 GB per GPU >> 126 MB L2; no flush",
+                "l2": f"inputs {4 * 4 * b * l * d / 1e9:.2f} GB per GPU vs 126 MB L2; no flush",
             },
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
             "fwd_gbs": fwd_gbs, "bwd_gbs": bwd_gbs,

@@ -85,6 +85,12 @@ int vmscan_version(void);
 const char* vmscan_strerror(int status);
 
 /*
+ * Detail of the last failed call on this thread (which argument, the driver's
+ * CUresult, the tensor-map dims/strides...); "" if none.  Thread-local.
+ */
+const char* vmscan_last_error(void);
+
+/*
  * Number of fp32 elements of the checkpoint buffer written by vmscan_fwd and
  * read by vmscan_bwd: the recurrent state (d_state floats per channel) at the
  * end of every scan box of at most 16 steps.  Negative on a bad argument.

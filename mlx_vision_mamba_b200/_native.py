@@ -45,6 +45,7 @@ _D = ctypes.POINTER(Direction)
 SIGNATURES = {
     "vmscan_version": (ctypes.c_int, []),
     "vmscan_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "vmscan_last_error": (ctypes.c_char_p, []),
     "vmscan_ckpt_elems": (_i64, [_i64, _i64, _i64, _i64, _D]),
     "vmscan_fwd": (
         ctypes.c_int,
@@ -104,7 +105,8 @@ class VmscanError(RuntimeError):
     def __init__(self, status: int, where: str):
         lib = load()
         msg = lib.vmscan_strerror(int(status)).decode()
-        super().__init__(f"{where}: vmscan status {status}: {msg}")
+        detail = lib.vmscan_last_error().decode()
+        super().__init__(f"{where}: vmscan status {status}: {msg}" + (f" ({detail})" if detail else ""))
         self.status = int(status)
 
 

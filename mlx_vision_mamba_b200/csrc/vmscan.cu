@@ -6,6 +6,9 @@
 // synchronisation (except vmscan_device_status), no global state besides the
 // driver entry point and the sticky device status word.
 #include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
 #include <mutex>
 
 #include "../../include/vmscan.h"
@@ -22,20 +25,67 @@ __device__ int g_vmscan_status = 0;
 namespace {
 
 constexpr int kFwdNCW = 4;
-constexpr int kBwdNCW = 4;
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+
+// Driver entry points, resolved once through the runtime (no link-time libcuda).
+struct DriverFns {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  PFN_cuCtxGetCurrent_v4000 ctx_get = nullptr;
+  PFN_cuCtxSetCurrent_v4000 ctx_set = nullptr;
+  PFN_cuPointerGetAttribute_v4000 ptr_attr = nullptr;
+};
+
+template <typename F>
+void resolve(const char* name, int version, F& out) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion(name, &p, version, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    out = reinterpret_cast<F>(p);
+}
+
+const DriverFns& driver() {
+  static DriverFns fns;
   static std::once_flag once;
   std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    resolve("cuTensorMapEncodeTiled", 12000, fns.encode);
+    resolve("cuCtxGetCurrent", 4000, fns.ctx_get);
+    resolve("cuCtxSetCurrent", 4000, fns.ctx_set);
+    resolve("cuPointerGetAttribute", 4000, fns.ptr_attr);
   });
-  return fn;
+  return fns;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return driver().encode; }
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// The C ABI can be called from a thread on which no CUDA context is current
+// yet (e.g. PyTorch's autograd worker thread).  Driver calls such as the
+// tensor-map encoder need one, so bind the context that owns the caller's
+// device buffer when the thread has none.  A context that is already current
+// is left untouched.
+int ensure_context(const void* devptr) {
+  const DriverFns& d = driver();
+  if (d.ctx_get == nullptr || d.ctx_set == nullptr || d.ptr_attr == nullptr)
+    return fail(VMSCAN_ERR_DRIVER, "CUDA driver entry points unavailable");
+  CUcontext cur = nullptr;
+  if (d.ctx_get(&cur) == CUDA_SUCCESS && cur != nullptr) return VMSCAN_OK;
+  CUcontext owner = nullptr;
+  const CUresult r = d.ptr_attr(&owner, CU_POINTER_ATTRIBUTE_CONTEXT, reinterpret_cast<CUdeviceptr>(devptr));
+  if (r != CUDA_SUCCESS || owner == nullptr)
+    return fail(VMSCAN_ERR_DRIVER, "no current CUDA context and buffer %p has no owning context (CUresult %d)",
+                devptr, int(r));
+  if (d.ctx_set(owner) != CUDA_SUCCESS) return fail(VMSCAN_ERR_DRIVER, "cuCtxSetCurrent failed");
+  return VMSCAN_OK;
 }
 
 int* status_ptr() {
@@ -130,14 +180,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Tensor map of a (batch, seq, inner) fp32 view seen in scan order:
 // dims {inner, scan0, scan1, scan2, batch}, box {box_inner, box...}.
-int encode_map(CUtensorMap* m, const void* ptr, int64_t inner, int box_inner, vmscan_strides st,
-               const ScanGeom& g) {
-  if (ptr == nullptr) return VMSCAN_ERR_NULL;
-  if (!aligned16(ptr)) return VMSCAN_ERR_ALIGN;
+int encode_map(CUtensorMap* m, const char* what, const void* ptr, int64_t inner, int box_inner,
+               vmscan_strides st, const ScanGeom& g) {
+  if (ptr == nullptr) return fail(VMSCAN_ERR_NULL, "%s is NULL", what);
+  if (!aligned16(ptr)) return fail(VMSCAN_ERR_ALIGN, "%s base %p is not 16-byte aligned", what, ptr);
   if ((g.seqlen > 1 && (st.seq <= 0 || st.seq % 4 != 0)) || (g.batch > 1 && (st.batch <= 0 || st.batch % 4 != 0)))
-    return VMSCAN_ERR_ALIGN;
+    return fail(VMSCAN_ERR_ALIGN, "%s strides {batch %lld, seq %lld} must be positive multiples of 4", what,
+                (long long)st.batch, (long long)st.seq);
   auto fn = encode_fn();
-  if (fn == nullptr) return VMSCAN_ERR_DRIVER;
+  if (fn == nullptr) return fail(VMSCAN_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[5];
   cuuint64_t strides[4];
   dims[0] = cuuint64_t(inner);
@@ -149,7 +200,9 @@ int encode_map(CUtensorMap* m, const void* ptr, int64_t inner, int box_inner, vm
   dims[4] = cuuint64_t(g.batch);
   strides[3] = cuuint64_t(g.batch > 1 ? st.batch * 4 : 16);
   for (int i = 0; i < 4; ++i)
-    if (strides[i] == 0 || strides[i] % 16 != 0 || strides[i] >= (cuuint64_t(1) << 40)) return VMSCAN_ERR_ALIGN;
+    if (strides[i] == 0 || strides[i] % 16 != 0 || strides[i] >= (cuuint64_t(1) << 40))
+      return fail(VMSCAN_ERR_ALIGN, "%s byte stride %llu of dim %d is invalid", what, (unsigned long long)strides[i],
+                  i + 1);
   cuuint32_t box3[3];
   box_extent(g, box3);
   cuuint32_t box[5] = {cuuint32_t(box_inner), box3[0], box3[1], box3[2], 1u};
@@ -157,7 +210,15 @@ int encode_map(CUtensorMap* m, const void* ptr, int64_t inner, int box_inner, vm
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? VMSCAN_OK : VMSCAN_ERR_DRIVER;
+  if (r != CUDA_SUCCESS)
+    return fail(VMSCAN_ERR_DRIVER,
+                "cuTensorMapEncodeTiled(%s) -> CUresult %d; dims {%llu,%llu,%llu,%llu,%llu} strides "
+                "{%llu,%llu,%llu,%llu} box {%u,%u,%u,%u,%u}",
+                what, int(r), (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2],
+                (unsigned long long)dims[3], (unsigned long long)dims[4], (unsigned long long)strides[0],
+                (unsigned long long)strides[1], (unsigned long long)strides[2], (unsigned long long)strides[3],
+                box[0], box[1], box[2], box[3], box[4]);
+  return VMSCAN_OK;
 }
 
 #define VM_TRY(expr)                 \
@@ -166,7 +227,11 @@ int encode_map(CUtensorMap* m, const void* ptr, int64_t inner, int box_inner, vm
     if (_rc != VMSCAN_OK) return _rc; \
   } while (0)
 
-int check_launch() { return cudaGetLastError() == cudaSuccess ? VMSCAN_OK : VMSCAN_ERR_LAUNCH; }
+int check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return VMSCAN_OK;
+  return fail(VMSCAN_ERR_LAUNCH, "kernel launch failed: %s", cudaGetErrorString(e));
+}
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -186,36 +251,61 @@ BwdWorkspace bwd_layout(const ScanGeom& g, int ndt, bool with_ck) {
   return w;
 }
 
+template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
+int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
+                 const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
+                 const ScanGeom& g, cudaStream_t stream) {
+  using Cfg = FwdCfg<kFwdNCW>;
+  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y, REV>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
+    return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_fwd_kernel) failed");
+  int* st = status_ptr();
+  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sy.seq, A, D, ckpt, g, st);
+  return check_launch();
+}
+
 template <bool HAS_Z, bool SAVE_CK, bool STORE_Y>
 int launch_fwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-               const CUtensorMap& mC, const CUtensorMap& my, const float* A, const float* D, float* ckpt,
+               const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
                const ScanGeom& g, cudaStream_t stream) {
-  using Cfg = FwdCfg<kFwdNCW>;
-  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y>;
+  if (g.reverse) return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, stream);
+  return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, stream);
+}
+
+struct BwdOut {
+  float* du;
+  vmscan_strides sdu;
+  float* ddt;
+  vmscan_strides sddt;
+  float* dz;
+  vmscan_strides sdz;
+};
+
+template <bool HAS_Z, bool REV>
+int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
+                 const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
+                 const float* ckpt, float* wpart, float* wA, float* wD, const ScanGeom& g, cudaStream_t stream) {
+  using Cfg = BwdCfg;
+  auto kern = scan_bwd_kernel<HAS_Z, REV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
-    return VMSCAN_ERR_LAUNCH;
+    return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_kernel) failed");
   int* st = status_ptr();
-  if (st == nullptr) return VMSCAN_ERR_LAUNCH;
+  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
   const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, st);
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, o.du, o.sdu.batch, o.sdu.seq, o.ddt,
+                                                   o.sddt.batch, o.sddt.seq, o.dz, o.sdz.batch, o.sdz.seq, A, D,
+                                                   ckpt, wpart, wA, wD, g, st);
   return check_launch();
 }
 
 template <bool HAS_Z>
 int launch_bwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
-               const CUtensorMap& mB, const CUtensorMap& mC, const CUtensorMap& mdu, const CUtensorMap& mddt,
-               const CUtensorMap& mdz, const float* A, const float* D, const float* ckpt, float* wpart, float* wA,
-               float* wD, const ScanGeom& g, cudaStream_t stream) {
-  using Cfg = BwdCfg<kBwdNCW>;
-  auto kern = scan_bwd_kernel<kBwdNCW, HAS_Z>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
-    return VMSCAN_ERR_LAUNCH;
-  int* st = status_ptr();
-  if (st == nullptr) return VMSCAN_ERR_LAUNCH;
-  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ckpt, wpart, wA,
-                                                   wD, g, st);
-  return check_launch();
+               const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
+               const float* ckpt, float* wpart, float* wA, float* wD, const ScanGeom& g, cudaStream_t stream) {
+  if (g.reverse) return launch_bwd_t<HAS_Z, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, g, stream);
+  return launch_bwd_t<HAS_Z, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, g, stream);
 }
 
 int check_common(int64_t d_state, const float* A, const float* D) {
@@ -264,27 +354,27 @@ int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
                vmscan_strides sy, float* ckpt, const vmscan_direction* dir, vmscan_stream_t stream) {
   VM_TRY(check_common(d_state, A, D));
   if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
-  if (ckpt != nullptr && !aligned16(ckpt)) return VMSCAN_ERR_ALIGN;
+  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
+  VM_TRY(ensure_context(u));
   using Cfg = FwdCfg<kFwdNCW>;
-  CUtensorMap mu, mdt, mz, mB, mC, my;
-  VM_TRY(encode_map(&mu, u, d_inner, Cfg::DT, su, g));
-  VM_TRY(encode_map(&mdt, delta, d_inner, Cfg::DT, sdelta, g));
+  CUtensorMap mu, mdt, mz, mB, mC;
+  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g));
+  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g));
   if (z != nullptr) {
-    VM_TRY(encode_map(&mz, z, d_inner, Cfg::DT, sz, g));
+    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g));
   } else {
     mz = mu;
   }
-  VM_TRY(encode_map(&mB, B, NS, NS, sB, g));
-  VM_TRY(encode_map(&mC, C, NS, NS, sC, g));
-  VM_TRY(encode_map(&my, y, d_inner, Cfg::DT, sy, g));
+  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g));
+  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool hz = z != nullptr, ck = ckpt != nullptr;
-  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
-  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
-  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
-  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, my, A, D, ckpt, g, s);
+  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
+  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
+  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
+  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
 }
 
 int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
@@ -293,7 +383,7 @@ int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inne
   ScanGeom g;
   const int rc = make_geom(batch, seqlen, d_inner, dir, g);
   if (rc != VMSCAN_OK) return -rc;
-  const int ndt = int((d_inner + BwdCfg<kBwdNCW>::DT - 1) / BwdCfg<kBwdNCW>::DT);
+  const int ndt = int((d_inner + BwdCfg::DT - 1) / BwdCfg::DT);
   return int64_t(bwd_layout(g, ndt, recompute_ckpt != 0).total);
 }
 
@@ -309,11 +399,11 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
       ddelta == nullptr || dA == nullptr || dB == nullptr || dC == nullptr || dD == nullptr)
     return VMSCAN_ERR_NULL;
   if (z != nullptr && dz == nullptr) return VMSCAN_ERR_NULL;
-  if (ckpt != nullptr && !aligned16(ckpt)) return VMSCAN_ERR_ALIGN;
+  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
-  using Cfg = BwdCfg<kBwdNCW>;
-  static_assert(Cfg::DT == FwdCfg<kFwdNCW>::DT, "forward and backward channel tiles must agree");
+  VM_TRY(ensure_context(u));
+  using Cfg = BwdCfg;
   const int ndt = int((d_inner + Cfg::DT - 1) / Cfg::DT);
   const BwdWorkspace wl = bwd_layout(g, ndt, ckpt == nullptr);
   if (workspace == nullptr || workspace_bytes < wl.total || !aligned16(workspace)) return VMSCAN_ERR_WORKSPACE;
@@ -321,34 +411,36 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
   float* wpart = reinterpret_cast<float*>(ws + wl.part);
   float* wA = reinterpret_cast<float*>(ws + wl.wA);
   float* wD = reinterpret_cast<float*>(ws + wl.wD);
-  CUtensorMap mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz;
-  VM_TRY(encode_map(&mu, u, d_inner, Cfg::DT, su, g));
-  VM_TRY(encode_map(&mdt, delta, d_inner, Cfg::DT, sdelta, g));
+  CUtensorMap mu, mdt, mz, mdy, mB, mC;
+  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g));
+  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g));
   if (z != nullptr) {
-    VM_TRY(encode_map(&mz, z, d_inner, Cfg::DT, sz, g));
-    VM_TRY(encode_map(&mdz, dz, d_inner, Cfg::DT, sdz, g));
+    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g));
   } else {
     mz = mu;
-    mdz = mu;
   }
-  VM_TRY(encode_map(&mdy, dy, d_inner, Cfg::DT, sdy, g));
-  VM_TRY(encode_map(&mB, B, NS, NS, sB, g));
-  VM_TRY(encode_map(&mC, C, NS, NS, sC, g));
-  VM_TRY(encode_map(&mdu, du, d_inner, Cfg::DT, sdu, g));
-  VM_TRY(encode_map(&mddt, ddelta, d_inner, Cfg::DT, sddelta, g));
-  if (!aligned16(dB) || !aligned16(dC)) return VMSCAN_ERR_ALIGN;
+  VM_TRY(encode_map(&mdy, "dy", dy, d_inner, Cfg::DT, sdy, g));
+  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g));
+  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const float* ck = ckpt;
   if (ck == nullptr) {
     // Rebuild the checkpoints (the reference VJP also recomputes the forward).
+    // The forward's channel tile differs from the VJP's, so it gets its own maps.
+    using FC = FwdCfg<kFwdNCW>;
+    CUtensorMap fu, fdt, fB;
+    VM_TRY(encode_map(&fu, "u", u, d_inner, FC::DT, su, g));
+    VM_TRY(encode_map(&fdt, "delta", delta, d_inner, FC::DT, sdelta, g));
+    VM_TRY(encode_map(&fB, "B", B, NS, NS, sB, g));
     float* ckw = reinterpret_cast<float*>(ws + wl.ck);
-    VM_TRY((launch_fwd<false, true, false>(mu, mdt, mu, mB, mC, mu, A, D, ckw, g, s)));
+    VM_TRY((launch_fwd<false, true, false>(fu, fdt, fu, fB, fB, nullptr, vmscan_strides{0, 0}, A, D, ckw, g, s)));
     ck = ckw;
   }
+  const BwdOut o{du, sdu, ddelta, sddelta, dz, sdz};
   if (z != nullptr) {
-    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ck, wpart, wA, wD, g, s));
+    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, g, s));
   } else {
-    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, mdu, mddt, mdz, A, D, ck, wpart, wA, wD, g, s));
+    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, g, s));
   }
   reduce_dbc_kernel<<<dim3(unsigned(g.nboxes), unsigned(g.batch)), TMAX * kPartRow, 0, s>>>(
       wpart, dB, sdB.batch, sdB.seq, dC, sdC.batch, sdC.seq, g, ndt);
@@ -365,6 +457,7 @@ int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   if (ksize < 1 || ksize > CONV_KMAX || channels % 4 != 0) return VMSCAN_ERR_CONV;
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, channels, dir, g));
+  VM_TRY(ensure_context(x));
   if (!aligned16(x) || !aligned16(out) || !aligned16(bias) || sx.seq % 4 || sx.batch % 4 || sout.seq % 4 ||
       sout.batch % 4)
     return VMSCAN_ERR_ALIGN;
@@ -398,6 +491,7 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   if (ksize < 1 || ksize > CONV_KMAX || channels % 4 != 0) return VMSCAN_ERR_CONV;
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, channels, dir, g));
+  VM_TRY(ensure_context(x));
   if (!aligned16(x) || !aligned16(dout) || !aligned16(dx) || !aligned16(bias) || sx.seq % 4 || sx.batch % 4 ||
       sdout.seq % 4 || sdout.batch % 4 || sdx.seq % 4 || sdx.batch % 4)
     return VMSCAN_ERR_ALIGN;
@@ -448,6 +542,8 @@ int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int
   }
   return q == seqlen ? VMSCAN_OK : VMSCAN_ERR_SHAPE;
 }
+
+const char* vmscan_last_error(void) { return g_last_error; }
 
 int vmscan_device_status(vmscan_stream_t stream, int clear) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

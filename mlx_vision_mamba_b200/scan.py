@@ -57,6 +57,14 @@ def _tma_compatible(t: torch.Tensor) -> bool:
     return True
 
 
+def _empty_seq(b: int, l: int, c: int, device) -> torch.Tensor:
+    """Uninitialised (b, l, c) fp32 view whose storage rows are padded to a
+    multiple of 4 channels, as the TMA rules of include/vmscan.h require."""
+    cp = (c + 3) // 4 * 4
+    buf = torch.empty((b, l, cp), dtype=torch.float32, device=device)
+    return buf if cp == c else buf[:, :, :c]
+
+
 def _prepare(t: torch.Tensor) -> torch.Tensor:
     """Return a TMA-compatible fp32 view of t, copying only when needed.
 
@@ -70,9 +78,7 @@ def _prepare(t: torch.Tensor) -> torch.Tensor:
     if _tma_compatible(t):
         return t
     b, l, c = t.shape
-    cp = (c + 3) // 4 * 4
-    buf = torch.empty((b, l, cp), dtype=torch.float32, device=t.device)
-    out = buf[:, :, :c]
+    out = _empty_seq(b, l, c, t.device)
     out.copy_(t)
     return out
 
@@ -120,7 +126,7 @@ class _SelectiveScanFn(torch.autograd.Function):
         z_ = _prepare(z) if z is not None else None
         A_ = A.detach().float().contiguous()
         D_ = D.detach().float().contiguous()
-        y = torch.empty((bt, l, dn), dtype=torch.float32, device=x.device)
+        y = _empty_seq(bt, l, dn, x.device)
         need_grad = any(ctx.needs_input_grad[:7])
         dptr = _dir_ptr(direction)
         ckpt = None
@@ -150,13 +156,13 @@ class _SelectiveScanFn(torch.autograd.Function):
         dev = u_.device
         dy_ = _prepare(dy)
         f32 = dict(dtype=torch.float32, device=dev)
-        du = torch.empty((bt, l, dn), **f32)
-        ddelta = torch.empty((bt, l, dn), **f32)
+        du = _empty_seq(bt, l, dn, dev)
+        ddelta = _empty_seq(bt, l, dn, dev)
         dA = torch.empty((dn, D_STATE), **f32)
         dB = torch.empty((bt, l, D_STATE), **f32)
         dC = torch.empty((bt, l, D_STATE), **f32)
         dD = torch.empty((dn,), **f32)
-        dz = torch.empty((bt, l, dn), **f32) if ctx.has_z else None
+        dz = _empty_seq(bt, l, dn, dev) if ctx.has_z else None
         dptr = _dir_ptr(ctx.direction)
         ws_bytes = lib.vmscan_bwd_workspace_bytes(bt, l, dn, D_STATE, dptr, 0)
         if ws_bytes < 0:
@@ -224,7 +230,7 @@ class _ConvSiluFn(torch.autograd.Function):
         x_ = _prepare(x)
         w_ = weight.detach().float().contiguous()
         b_ = bias.detach().float().contiguous()
-        out = torch.empty((bt, l, c), dtype=torch.float32, device=x.device)
+        out = _empty_seq(bt, l, c, x.device)
         st = lib.vmscan_conv1d_silu_fwd(
             bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(out), _strides(out),
             _dir_ptr(direction), _stream(x),
@@ -241,7 +247,7 @@ class _ConvSiluFn(torch.autograd.Function):
         bt, l, c = x_.shape
         k = w_.shape[1]
         dout_ = _prepare(dout)
-        dx = torch.empty((bt, l, c), dtype=torch.float32, device=x_.device)
+        dx = _empty_seq(bt, l, c, x_.device)
         dw = torch.empty_like(w_)
         db = torch.empty_like(b_)
         ws_bytes = lib.vmscan_conv1d_bwd_workspace_bytes(bt, l, c, k)
