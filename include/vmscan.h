@@ -54,7 +54,8 @@ enum vmscan_status {
   VMSCAN_ERR_DRIVER = 7,     /* tensor-map encoding refused by the driver */
   VMSCAN_ERR_LAUNCH = 8,     /* kernel launch failed */
   VMSCAN_ERR_TIMEOUT = 9,    /* a device-side wait ran out (see vmscan_device_status) */
-  VMSCAN_ERR_CONV = 10       /* conv kernel size unsupported (1..8) */
+  VMSCAN_ERR_CONV = 10,      /* conv kernel size unsupported (1..8) */
+  VMSCAN_ERR_SCRATCH = 11    /* problem too large for vmscan_bwd_noalloc's static scratch */
 };
 
 /*
@@ -155,6 +156,52 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
                const vmscan_direction* dir,
                void* workspace, size_t workspace_bytes,
                vmscan_stream_t stream);
+
+/*
+ * Size of the device array behind vmscan_bwd_noalloc: 32 MiB, reserved on
+ * every GPU that loads libvmscan.so, for as long as the library stays loaded.
+ */
+#define VMSCAN_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/*
+ * vmscan_bwd without a workspace argument, for callers that cannot allocate
+ * device memory: for example a C or FFI binding that is handed raw input and
+ * output buffers by a host framework and has no device allocator of its own,
+ * or a serving process that budgets all device memory at start-up and forbids
+ * allocator calls afterwards.  It has no counterpart in the reference, whose
+ * VJP lets MLX allocate its outputs and (B, L, D, N) partials.
+ *
+ * The scratch is a file-scope device array of VMSCAN_NOALLOC_SCRATCH_BYTES;
+ * a problem whose vmscan_bwd_workspace_bytes(..., recompute_ckpt = (ckpt ==
+ * NULL)) exceeds it returns VMSCAN_ERR_SCRATCH without launching anything.
+ * Inputs and outputs are the caller's, exactly as for vmscan_bwd.  The call
+ * allocates and frees nothing.  The first call on a device looks up that
+ * device's address of the array (once per device, cached); make that first
+ * call before any stream capture.  All calls on a device share the one array
+ * and it keeps the previous call's contents; nothing in it needs to start at
+ * zero (every byte read is written earlier in the same call), but calls whose
+ * kernels overlap on the GPU (different streams, or another thread) race on
+ * it and corrupt each other's results: serialise them.
+ */
+int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                       const float* u, vmscan_strides su,
+                       const float* delta, vmscan_strides sdelta,
+                       const float* A,
+                       const float* B, vmscan_strides sB,
+                       const float* C, vmscan_strides sC,
+                       const float* D,
+                       const float* z, vmscan_strides sz,
+                       const float* ckpt,
+                       const float* dy, vmscan_strides sdy,
+                       float* du, vmscan_strides sdu,
+                       float* ddelta, vmscan_strides sddelta,
+                       float* dA,
+                       float* dB, vmscan_strides sdB,
+                       float* dC, vmscan_strides sdC,
+                       float* dD,
+                       float* dz, vmscan_strides sdz,
+                       const vmscan_direction* dir,
+                       vmscan_stream_t stream);
 
 /*
  * Depthwise causal conv1d along the scan order, fused with SiLU:

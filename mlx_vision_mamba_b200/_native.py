@@ -67,6 +67,21 @@ SIGNATURES = {
             _D, _p, _sz, _p,
         ],
     ),
+    "vmscan_bwd_noalloc": (
+        ctypes.c_int,
+        [
+            _i64, _i64, _i64, _i64,
+            _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S,  # u delta A B C D z
+            _p,  # ckpt
+            _p, _S,  # dy
+            _p, _S, _p, _S,  # du ddelta
+            _p,  # dA
+            _p, _S, _p, _S,  # dB dC
+            _p,  # dD
+            _p, _S,  # dz
+            _D, _p,
+        ],
+    ),
     "vmscan_conv1d_silu_fwd": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _D, _p]),
     "vmscan_conv1d_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vmscan_conv1d_silu_bwd": (

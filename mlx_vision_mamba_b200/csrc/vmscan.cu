@@ -22,6 +22,10 @@ using namespace vmscan;
 // Sticky device status: kernels set it when a bounded wait gives up.
 __device__ int g_vmscan_status = 0;
 
+// Scratch of vmscan_bwd_noalloc (see include/vmscan.h).  Host code only ever
+// uses its per-device address from cudaGetSymbolAddress, never the symbol.
+static __device__ __align__(256) unsigned char g_vmscan_noalloc_scratch[VMSCAN_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 constexpr int kFwdNCW = 4;
@@ -335,6 +339,8 @@ const char* vmscan_strerror(int status) {
     case VMSCAN_ERR_LAUNCH: return "kernel launch failed";
     case VMSCAN_ERR_TIMEOUT: return "a device-side wait ran out; the kernel returned early";
     case VMSCAN_ERR_CONV: return "conv kernel size must be 1..8 and channels a multiple of 4";
+    case VMSCAN_ERR_SCRATCH: return "problem needs more scratch than vmscan_bwd_noalloc's static 32 MiB array; "
+                                    "use vmscan_bwd with a caller-provided workspace";
     default: return "unknown vmscan status";
   }
 }
@@ -544,6 +550,55 @@ int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int
 }
 
 const char* vmscan_last_error(void) { return g_last_error; }
+
+namespace {
+// Per-device address of g_vmscan_noalloc_scratch, looked up once per device
+// with that device current.
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+int noalloc_scratch_addr(const void* devbuf, void** out) {
+  VM_TRY(ensure_context(devbuf));
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(VMSCAN_ERR_LAUNCH, "cudaGetDevice failed");
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, devbuf) != cudaSuccess || attr.device != dev)
+    return fail(VMSCAN_ERR_LAUNCH, "the current device (%d) does not own the input buffers", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_vmscan_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(VMSCAN_ERR_LAUNCH, "cudaGetSymbolAddress(scratch) on device %d failed: %s", dev,
+                  cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return VMSCAN_OK;
+}
+}  // namespace
+
+int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const float* u,
+                       vmscan_strides su, const float* delta, vmscan_strides sdelta, const float* A, const float* B,
+                       vmscan_strides sB, const float* C, vmscan_strides sC, const float* D, const float* z,
+                       vmscan_strides sz, const float* ckpt, const float* dy, vmscan_strides sdy, float* du,
+                       vmscan_strides sdu, float* ddelta, vmscan_strides sddelta, float* dA, float* dB,
+                       vmscan_strides sdB, float* dC, vmscan_strides sdC, float* dD, float* dz, vmscan_strides sdz,
+                       const vmscan_direction* dir, vmscan_stream_t stream) {
+  if (u == nullptr) return VMSCAN_ERR_NULL;
+  const int64_t need = vmscan_bwd_workspace_bytes(batch, seqlen, d_inner, d_state, dir, ckpt == nullptr ? 1 : 0);
+  if (need < 0) return int(-need);
+  if (need > int64_t(VMSCAN_NOALLOC_SCRATCH_BYTES))
+    return fail(VMSCAN_ERR_SCRATCH, "needs %lld bytes of scratch, the static array holds %u", (long long)need,
+                VMSCAN_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  VM_TRY(noalloc_scratch_addr(u, &scratch));
+  return vmscan_bwd(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy, sdy,
+                    du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, scratch,
+                    size_t(VMSCAN_NOALLOC_SCRATCH_BYTES), stream);
+}
 
 int vmscan_device_status(vmscan_stream_t stream, int clear) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -38,7 +38,7 @@ def test_every_header_function_is_exported_and_bound():
 
 def test_strerror_covers_codes():
     lib = _native.load()
-    for code in range(0, 11):
+    for code in range(0, 12):
         assert lib.vmscan_strerror(code) != b"unknown vmscan status"
     assert lib.vmscan_strerror(99) == b"unknown vmscan status"
 
