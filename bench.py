@@ -259,6 +259,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the VisionMamba-2D training measurement")
     ap.add_argument("--batch", type=int, default=WORKLOAD["batch"], help="per-GPU batch (profiling runs)")
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
@@ -333,7 +334,13 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(t, dev, K=max(2, min(K, 4)), warmup=1, world=world, barrier=barrier)
-    del runner
+    del runner, t
+    torch.cuda.empty_cache()
+
+    # ---- VisionMamba-2D training throughput (second half of the metric) ----
+    model_line = None
+    if not args.no_model:
+        model_line = run_model(dev, rank, world, steps=max(3, min(K, 10)), warmup=3, barrier=barrier)
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -374,10 +381,52 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": base,
+            "vision_mamba_2d_train": model_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def run_model(dev, rank, world, steps, warmup, barrier):
+    """VisionMamba-2D (K=4, 224x224x1, patch 16, E 384, depth 6) training steps:
+    forward, MSE, backward (DDP all-reduce over NCCL when world > 1), AdamW.
+    Global batch 64 split over the ranks (strong scaling), fp32 (TF32 off)."""
+    import torch
+    import torch.distributed as dist
+
+    from mlx_vision_mamba_b200 import train
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    cfg = train.VISION_MAMBA_2D
+    a, b = train.shard(cfg.global_batch, rank, world)
+    model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+    opt = train.make_optimizer(model)
+    x, tgt = train.synthetic_batch(cfg, b - a, dev, seed=100 + rank)
+    for _ in range(warmup):
+        train.train_step(model, opt, x, tgt)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = train.train_step(model, opt, x, tgt)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    tm = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms = float(tm.item())
+    n_params = sum(p.numel() for p in model.parameters())
+    del model, opt
+    torch.cuda.empty_cache()
+    return {"img_per_s": cfg.global_batch * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
+            "warmup": warmup, "global_batch": cfg.global_batch, "per_gpu_batch": b - a, "scaling": "strong",
+            "dtype": "f32 (TF32 off)", "params": n_params, "loss": float(loss.item()),
+            "parallelism": f"DDP NCCL all-reduce x{world}" if world > 1 else "single GPU",
+            "config": "img 224x224x1, patch 16, embed 384, depth 6, d_state 16, K=4 directions, MSE vs N(0,1)"}
 
 
 def run_e2e(t, dev, K, warmup, world, barrier):

@@ -44,12 +44,12 @@ struct BwdCfg {
   static constexpr int DT = 16 * NCW;      // channels per CTA (2 per quad)
   static constexpr int NCT = NCW * 32;
   static constexpr int NT = NCT;
-  static constexpr int NST = 3;
+  static constexpr int NST = 2;
   static constexpr int TILE = TMAX * DT;
   static constexpr int BCT = TMAX * NS;
   static constexpr int CKT = DT * NS;
   static constexpr int TOKF = 32;             // 16 row tokens + row count
-  static constexpr uint32_t TMEM_COLS = 256;  // 16 steps x 2 channels x (4 exp + 4 h)
+  static constexpr uint32_t TMEM_COLS = 128;  // 16 steps x 2 channels x 4 states of h_{t-1}
   // stage: u, delta, z, dy tiles, B, C tiles, checkpoint, token table
   static constexpr int OFF_DT = TILE, OFF_Z = 2 * TILE, OFF_DY = 3 * TILE, OFF_B = 4 * TILE,
                        OFF_C = 4 * TILE + BCT, OFF_CK = 4 * TILE + 2 * BCT, OFF_TOK = 4 * TILE + 2 * BCT + CKT;
@@ -166,6 +166,9 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
           const float2 du2 = mul2(t2, u2);
           const float2 dl2 = mul2(t2, log2e2);
           const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
+          const float hist[8] = {h[0][0].x, h[0][0].y, h[0][1].x, h[0][1].y,
+                                 h[1][0].x, h[1][0].y, h[1][1].x, h[1][1].y};
+          tmem_st8(taddr + 8 * s, hist);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float2 dlb = bcast2(dlc[c]), dub = bcast2(duc[c]);
@@ -173,8 +176,6 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
             const float2 a1 = fma2(dlb, L.Ar[c][1], off2);
             const float2 e0 = make_float2(ex2_approx(a0.x), ex2_approx(a0.y));
             const float2 e1 = make_float2(ex2_approx(a1.x), ex2_approx(a1.y));
-            const float hist[8] = {e0.x, e0.y, e1.x, e1.y, h[c][0].x, h[c][0].y, h[c][1].x, h[c][1].y};
-            tmem_st8(taddr + 16 * s + 8 * c, hist);
             h[c][0] = fma2(e0, h[c][0], mul2(dub, B2[0]));
             h[c][1] = fma2(e1, h[c][1], mul2(dub, B2[1]));
           }
@@ -215,28 +216,22 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
   for (int c = 0; c < 2; ++c) dAbox[c][0] = dAbox[c][1] = make_float2(0.f, 0.f);
   float dDbox = 0.f;
   float2 hs[2][2] = {{h[0][0], h[0][1]}, {h[1][0], h[1][1]}};
-  uint32_t X[2][16];  // two alternating history buffers: slot s in X[s & 1]
+  uint32_t X[2][8];  // two alternating history buffers: h_{s-1} of slot s in X[s & 1]
   {
     const int s = FULL ? TMAX - 1 : nv - 1;
     if (FULL || (s & 1)) {
-      tmem_ld8(taddr + 16 * s, X[1]);
-      tmem_ld8(taddr + 16 * s + 8, X[1] + 8);
-      tmem_wait_ld16(X[1]);
+      tmem_ld8(taddr + 8 * s, X[1]);
+      tmem_wait_ld8(X[1]);
     } else {
-      tmem_ld8(taddr + 16 * s, X[0]);
-      tmem_ld8(taddr + 16 * s + 8, X[0] + 8);
-      tmem_wait_ld16(X[0]);
+      tmem_ld8(taddr + 8 * s, X[0]);
+      tmem_wait_ld8(X[0]);
     }
   }
 #pragma unroll
   for (int s = TMAX - 1; s >= 0; --s) {
     if (FULL || s < nv) {
       uint32_t* cur = X[s & 1];
-      if (s > 0) {
-        uint32_t* nxt = X[(s - 1) & 1];
-        tmem_ld8(taddr + 16 * (s - 1), nxt);
-        tmem_ld8(taddr + 16 * (s - 1) + 8, nxt + 8);
-      }
+      if (s > 0) tmem_ld8(taddr + 8 * (s - 1), X[(s - 1) & 1]);
       const int r = REV ? nv - 1 - s : s;
       const float2 dy2 = lds2(sdy + r * DT);
       const float2 u2 = lds2(su + r * DT);
@@ -246,17 +241,22 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
       const float2 B2[2] = {make_float2(Bv.x, Bv.y), make_float2(Bv.z, Bv.w)};
       const float2 C2[2] = {make_float2(Cv.x, Cv.y), make_float2(Cv.z, Cv.w)};
       const float2 du2 = mul2(t2, u2);
+      const float2 dl2 = mul2(t2, log2e2);
       const float dyc[2] = {dy2.x, dy2.y}, duc[2] = {du2.x, du2.y}, dtc[2] = {t2.x, t2.y},
-                  uc[2] = {u2.x, u2.y};
+                  uc[2] = {u2.x, u2.y}, dlc[2] = {dl2.x, dl2.y};
       float2 vb[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       float2 vc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       float red4[4];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const float2 e[2] = {make_float2(__uint_as_float(cur[8 * c + 0]), __uint_as_float(cur[8 * c + 1])),
-                             make_float2(__uint_as_float(cur[8 * c + 2]), __uint_as_float(cur[8 * c + 3]))};
-        const float2 hp[2] = {make_float2(__uint_as_float(cur[8 * c + 4]), __uint_as_float(cur[8 * c + 5])),
-                              make_float2(__uint_as_float(cur[8 * c + 6]), __uint_as_float(cur[8 * c + 7]))};
+        // exp(delta*A) recomputed exactly as in the forward pass (same operations)
+        const float2 dlb = bcast2(dlc[c]);
+        const float2 a0 = fma2(dlb, L.Ar[c][0], off2);
+        const float2 a1 = fma2(dlb, L.Ar[c][1], off2);
+        const float2 e[2] = {make_float2(ex2_approx(a0.x), ex2_approx(a0.y)),
+                             make_float2(ex2_approx(a1.x), ex2_approx(a1.y))};
+        const float2 hp[2] = {make_float2(__uint_as_float(cur[4 * c + 0]), __uint_as_float(cur[4 * c + 1])),
+                              make_float2(__uint_as_float(cur[4 * c + 2]), __uint_as_float(cur[4 * c + 3]))};
         const float2 dyb = bcast2(dyc[c]), dub = bcast2(duc[c]), dtb = bcast2(dtc[c]);
         float2 sB2 = make_float2(0.f, 0.f), sAg2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -288,7 +288,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
       const float vbs[4] = {vb[0].x, vb[0].y, vb[1].x, vb[1].y};
       const float vcs[4] = {vc[0].x, vc[0].y, vc[1].x, vc[1].y};
       part[(r * Cfg::NCW + warp) * 32 + part_slot(lane)] = warp_reduce8_scatter(vbs, vcs, lane);
-      if (s > 0) tmem_wait_ld16(X[(s - 1) & 1]);
+      if (s > 0) tmem_wait_ld8(X[(s - 1) & 1]);
     }
   }
 #pragma unroll
@@ -300,7 +300,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
 }
 
 template <bool HAS_Z, bool REV>
-__global__ void __launch_bounds__(BwdCfg::NT, 2)
+__global__ void __launch_bounds__(BwdCfg::NT, 3)
     scan_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_dy,
                     const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
   // (one row per lane) and the row count, then lane 0 issues the stage's TMA
   // loads and the checkpoint bulk copy.  A stage is reused once all warps
   // released it.
-  auto issue = [&](int i) {
+  auto issue = [&](int i) {  // called by one whole warp
     const int st = i % NST;
     const uint32_t ph = uint32_t(i / NST) & 1u;
     int ok = 1;
@@ -419,8 +419,9 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     const uint32_t ph = uint32_t(i / NST) & 1u;
     const int ib = g.nboxes - 1 - i;
     // the stage of box i-1 was released by every warp before the barrier that
-    // closed box i-1, so this wait does not stall
-    if (warp == 0 && alive && i + NST - 1 < g.nboxes) issue(i + NST - 1);
+    // closed box i-1, so this wait does not stall; the producer role rotates
+    // over the warps so the per-box barrier does not wait on one busy warp
+    if (warp == (i % NCW) && alive && i + NST - 1 < g.nboxes) issue(i + NST - 1);
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles and tcgen05 below need the whole warp
     float* part = sm + Cfg::OFF_PART + (i & 1) * (TMAX * NCW * 32);

@@ -1,0 +1,102 @@
+"""Data-parallel training step for the VisionMamba encoders.
+
+The reference has no training loop or distributed code (it runs one MLX
+device); this is the harness of the BASELINE configs 3-5: a VisionMamba
+forward, an MSE loss against a target of the feature shape, backward and an
+AdamW update, with the global batch split across one process per GPU and the
+gradients averaged by DistributedDataParallel (bucketed NCCL all-reduce over
+NVLink, overlapped with the backward).  Every function here is model-agnostic
+so the data-parallel logic can be exercised on CPU ranks (gloo).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+
+@dataclass(frozen=True)
+class EncoderConfig:
+    """A VisionMamba training configuration."""
+
+    name: str
+    input_shape: Tuple[int, ...]  # per-sample input, channel-last
+    img_size: int
+    patch_size: int
+    embed_dim: int = 384
+    depth: int = 6
+    d_state: int = 16
+    input_dim: int = 2
+    num_temporal_frames: int = 1
+    temporal_patch_size: int = 1
+    global_batch: int = 64
+
+    @property
+    def num_tokens(self) -> int:
+        g = self.img_size // self.patch_size
+        if self.input_dim == 4:
+            return (self.num_temporal_frames // self.temporal_patch_size) * g ** 3
+        return g ** self.input_dim
+
+
+VISION_MAMBA_2D = EncoderConfig("VisionMamba-2D K=4", (224, 224, 1), 224, 16, input_dim=2, global_batch=64)
+VISION_MAMBA_3D = EncoderConfig("VisionMamba-3D K=6", (128, 128, 128, 1), 128, 16, input_dim=3, global_batch=16)
+VISION_MAMBA_4D = EncoderConfig(
+    "VisionMamba-4D K=8", (8, 64, 64, 64, 1), 64, 16, input_dim=4, num_temporal_frames=8, global_batch=8
+)
+
+
+def shard(global_batch: int, rank: int, world: int) -> Tuple[int, int]:
+    """[start, stop) of this rank's slice of the global batch (contiguous, balanced)."""
+    if global_batch < world:
+        raise ValueError(f"global batch {global_batch} smaller than world size {world}")
+    base, extra = divmod(global_batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def synthetic_batch(cfg: EncoderConfig, batch: int, device, seed: int):
+    """Seeded N(0,1) inputs and MSE targets of the config's shapes."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn((batch, *cfg.input_shape), generator=g, device=device)
+    target = torch.randn((batch, cfg.num_tokens, cfg.embed_dim), generator=g, device=device)
+    return x, target
+
+
+def build_encoder(cfg: EncoderConfig, device, seed: int = 0):
+    from .vision_mamba import VisionMamba
+
+    torch.manual_seed(seed)
+    return VisionMamba(
+        img_size=cfg.img_size, patch_size=cfg.patch_size, in_channels=cfg.input_shape[-1],
+        embed_dim=cfg.embed_dim, depth=cfg.depth, d_state=cfg.d_state, input_dim=cfg.input_dim,
+        num_temporal_frames=cfg.num_temporal_frames, temporal_patch_size=cfg.temporal_patch_size,
+    ).to(device)
+
+
+def wrap_data_parallel(model: torch.nn.Module, device: Optional[torch.device] = None):
+    """DDP when a process group with more than one rank is active, else the model itself."""
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        ids = [device.index] if device is not None and device.type == "cuda" else None
+        return torch.nn.parallel.DistributedDataParallel(model, device_ids=ids, bucket_cap_mb=25)
+    return model
+
+
+def train_step(model, optimizer, x, target) -> torch.Tensor:
+    """One step: forward, MSE against the target, backward (gradients averaged
+    across ranks by DDP), AdamW update.  Returns the detached loss."""
+    out = model(x)
+    loss = F.mse_loss(out, target)
+    optimizer.zero_grad(set_to_none=True)
+    loss.backward()
+    optimizer.step()
+    return loss.detach()
+
+
+def make_optimizer(model, lr: float = 1e-4):
+    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=0.05)

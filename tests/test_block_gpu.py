@@ -67,3 +67,20 @@ def test_mamba_block_config1_shape():
     assert_parity("cfg1 dx", dx.cpu(), dx64, dx32)
     for k in g64:
         assert_parity(f"cfg1 d[{k}]", g[k].cpu(), g64[k], g32[k])
+
+
+def test_vision_mamba_training_step_updates_parameters():
+    """One data-parallel-ready training step (single process) on a small config."""
+    from mlx_vision_mamba_b200 import train
+
+    cfg = train.EncoderConfig("tiny 2D", (32, 32, 1), 32, 8, embed_dim=32, depth=2, input_dim=2, global_batch=4)
+    dev = torch.device("cuda", 0)
+    model = train.wrap_data_parallel(train.build_encoder(cfg, dev), dev)
+    opt = train.make_optimizer(model, lr=1e-3)
+    x, tgt = train.synthetic_batch(cfg, 4, dev, seed=0)
+    before = {k: p.detach().clone() for k, p in model.named_parameters()}
+    losses = [train.train_step(model, opt, x, tgt).item() for _ in range(3)]
+    assert all(torch.isfinite(torch.tensor(losses)))
+    assert losses[-1] < losses[0]
+    changed = sum(not torch.equal(before[k], p.detach()) for k, p in model.named_parameters())
+    assert changed == len(before)
