@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <mutex>
 
@@ -182,6 +183,16 @@ void box_extent(const ScanGeom& g, cuuint32_t box[3]) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Output tensors are written with plain stores at (token * seq stride); the
+// kernels take that stride as a 32-bit int so the address is one wide
+// multiply-add.
+int seq_stride32(const char* what, vmscan_strides s, int64_t seqlen, int& out) {
+  if (seqlen > 1 && (s.seq <= 0 || s.seq > INT32_MAX))
+    return fail(VMSCAN_ERR_SHAPE, "%s seq stride %lld must be in 1..2^31-1", what, (long long)s.seq);
+  out = int(seqlen > 1 ? s.seq : 0);
+  return VMSCAN_OK;
+}
+
 // Tensor map of a (batch, seq, inner) fp32 view seen in scan order:
 // dims {inner, scan0, scan1, scan2, batch}, box {box_inner, box...}.
 int encode_map(CUtensorMap* m, const char* what, const void* ptr, int64_t inner, int box_inner,
@@ -265,8 +276,10 @@ int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_fwd_kernel) failed");
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  int sys = 0;
+  if (STORE_Y) VM_TRY(seq_stride32("y", sy, g.seqlen, sys));
   const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sy.seq, A, D, ckpt, g, st);
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sys, A, D, ckpt, g, st);
   return check_launch();
 }
 
@@ -297,10 +310,14 @@ int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_kernel) failed");
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  int sdus = 0, sdts = 0, sdzs = 0;
+  VM_TRY(seq_stride32("du", o.sdu, g.seqlen, sdus));
+  VM_TRY(seq_stride32("ddelta", o.sddt, g.seqlen, sdts));
+  if (HAS_Z) VM_TRY(seq_stride32("dz", o.sdz, g.seqlen, sdzs));
   const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, o.du, o.sdu.batch, o.sdu.seq, o.ddt,
-                                                   o.sddt.batch, o.sddt.seq, o.dz, o.sdz.batch, o.sdz.seq, A, D,
-                                                   ckpt, wpart, wA, wD, g, st);
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, o.du, o.sdu.batch, sdus, o.ddt,
+                                                   o.sddt.batch, sdts, o.dz, o.sdz.batch, sdzs, A, D, ckpt, wpart,
+                                                   wA, wD, g, st);
   return check_launch();
 }
 

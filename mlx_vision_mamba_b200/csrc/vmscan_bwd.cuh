@@ -13,23 +13,27 @@
 //   dD[d]     = sum_{b,t} dy'_t u_t
 //   dz_t      = dy_t * y_t * sigma(z_t) * (1 + z_t (1 - sigma(z_t)))
 //
-// Design.  One CTA (one warpgroup, 4 warps) owns one batch row and 64
+// Design.  One CTA (one warpgroup, 4 warps) owns one batch row and 128
 // channels for the whole sequence and visits its boxes (<= 16 steps)
-// last-to-first.  Warp 0 also acts as producer: per box it writes the row ->
-// token table and the row count into the stage, and lane 0 issues the TMA
-// loads of u, delta, z, dy, B, C and the bulk copy of the checkpointed state
-// that precedes the box.  A consumer quad owns two adjacent channels; each
-// lane holds 4 of the 16 states of both, so every shared-memory load, shuffle
-// and epilogue serves two channels and the sums over channels start inside
-// the lane.  The box's forward steps are recomputed once and exp(delta_t A),
-// h_{t-1} of every step are parked in Tensor Memory (256 columns of the
-// thread's TMEM lane), so the history costs neither registers nor
-// shared-memory bandwidth; the gate (y_pre, dy', dz) is evaluated in that same
-// pass.  The reverse pass streams the history back one step ahead of use from
-// two alternating register buffers.  State math runs on packed fp32 pairs.
-// du/ddelta come out of one quad reduce-scatter and go straight to global
-// memory through the token table; dB/dC are reduce-scattered over the warp's
-// 8 quads, summed over the 4 warps in a fixed order and written as one
+// last-to-first.  The producer role rotates over the warps: per box it writes
+// the row -> token table and the row count into the stage, and its lane 0
+// issues the TMA loads of u, delta, z, dy, B, C and the bulk copy of the
+// checkpointed state that precedes the box.  A lane pair owns two adjacent
+// channels; each lane of the pair holds 8 of the 16 states of both (lane bit
+// 0 picks the half), so a warp covers 32 channels, every per-channel sum
+// over states is one pair exchange, and the sums over channels for dB/dC
+// start with two channels inside the lane.  The box's forward steps are
+// recomputed once and h_{t-1} of every step (16 floats per lane) is parked in
+// Tensor Memory (256 columns of the thread's TMEM lane), so the history costs
+// neither registers nor shared-memory bandwidth; the gate (y_pre, dy', dz)
+// is evaluated in that same pass for the lane's own channel.  The reverse
+// pass streams the history back one step ahead of use from two alternating
+// register buffers and recomputes exp(delta A) with the forward's exact
+// operations.  State math runs on packed fp32 pairs.  du/ddelta of the own
+// channel go straight to global memory through the token table; dB/dC are
+// reduce-scattered over the 16 lanes holding the same state half (the state
+// groups are stored in lane-dependent order so the first stage needs no
+// selects), summed over the 4 warps in a fixed order and written as one
 // partial per (CTA, step); dA/dD partials are kept per thread.  Two small
 // kernels finish dB/dC (sum over channel tiles, scattered to token order) and
 // dA/dD (sum over the batch) in a fixed order: the result is deterministic.
@@ -41,7 +45,7 @@ namespace vmscan {
 
 struct BwdCfg {
   static constexpr int NCW = 4;            // one warpgroup: the 4 TMEM lane quarters
-  static constexpr int DT = 16 * NCW;      // channels per CTA (2 per quad)
+  static constexpr int DT = 32 * NCW;      // channels per CTA (32 per warp, 2 per lane pair)
   static constexpr int NCT = NCW * 32;
   static constexpr int NT = NCT;
   static constexpr int NST = 2;
@@ -49,7 +53,7 @@ struct BwdCfg {
   static constexpr int BCT = TMAX * NS;
   static constexpr int CKT = DT * NS;
   static constexpr int TOKF = 32;             // 16 row tokens + row count
-  static constexpr uint32_t TMEM_COLS = 128;  // 16 steps x 2 channels x 4 states of h_{t-1}
+  static constexpr uint32_t TMEM_COLS = 256;  // 16 steps x 2 channels x 8 states of h_{t-1}
   // stage: u, delta, z, dy tiles, B, C tiles, checkpoint, token table
   static constexpr int OFF_DT = TILE, OFF_Z = 2 * TILE, OFF_DY = 3 * TILE, OFF_B = 4 * TILE,
                        OFF_C = 4 * TILE + BCT, OFF_CK = 4 * TILE + 2 * BCT, OFF_TOK = 4 * TILE + 2 * BCT + CKT;
@@ -63,147 +67,252 @@ struct BwdCfg {
 // Rows of the per-(CTA, step) dB/dC partial: 16 dB values then 16 dC values.
 constexpr int kPartRow = 2 * NS;
 
-// Reduce-scatter of 8 values (vb = dB partials of states 4q..4q+3, vc = dC
-// partials of the same states) over the 8 lanes that share q = lane & 3.
-// Returns one fully reduced value; its slot is part_slot(lane).
-__device__ __forceinline__ float warp_reduce8_scatter(const float vb[4], const float vc[4], int lane) {
-  const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-  float w[4];
-#pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const float keep = b4 ? vc[m] : vb[m];
-    const float send = b4 ? vb[m] : vc[m];
-    w[m] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-  float x[2];
-#pragma unroll
-  for (int m = 0; m < 2; ++m) {
-    const float keep = b3 ? w[2 + m] : w[m];
-    const float send = b3 ? w[m] : w[2 + m];
-    x[m] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  const float keep = b2 ? x[1] : x[0];
-  const float send = b2 ? x[0] : x[1];
-  return keep + __shfl_xor_sync(0xffffffffu, send, 4);
+// Lane roles.  Lane l of a warp: pair l >> 1 owns channels 2(l >> 1) and
+// 2(l >> 1) + 1 of the warp; the lane's own channel (epilogue) is l.  The
+// lane holds states 8 hb .. 8 hb + 7 (hb = l & 1) of both channels, in slot
+// order: slot group g (4 states) holds state group g ^ b4 (b4 = bit 4 of l).
+struct PairLane {
+  int hb, b4, b3, b2, b1;
+  __device__ __forceinline__ explicit PairLane(int lane)
+      : hb(lane & 1), b4((lane >> 4) & 1), b3((lane >> 3) & 1), b2((lane >> 2) & 1), b1((lane >> 1) & 1) {}
+  // first state of slot group g
+  __device__ __forceinline__ int group_state(int g) const { return 8 * hb + 4 * (g ^ b4); }
+  // slot of this lane's value in the 32-float dB/dC row after dbc_reduce_scatter
+  __device__ __forceinline__ int part_slot() const { return 16 * b1 + 8 * hb + 4 * b4 + 2 * b3 + b2; }
+};
+
+__device__ __forceinline__ float2 sel2(bool p, float2 a, float2 b) { return p ? a : b; }
+
+__device__ __forceinline__ float2 shfl_xor2(float2 v, int m) {
+  return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-__device__ __forceinline__ int part_slot(int lane) {
-  const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
-  return b4 * NS + 4 * (lane & 3) + 2 * b3 + b2;
+// Reduce-scatter of the lane's dB partials vb (8 states, slot order, pairs)
+// and dC partials vc over the 16 lanes that hold the same state half.
+// Returns one fully reduced value: dB (b1 == 0) or dC (b1 == 1) of state
+// 8 hb + 4 b4 + 2 b3 + b2, i.e. PairLane::part_slot().
+__device__ __forceinline__ float dbc_reduce_scatter(const float2 vb[4], const float2 vc[4], const PairLane& pl) {
+  // lanes l and l^16 hold opposite state groups in slot group 1: send it, keep slot group 0
+  const float2 xb0 = add2(vb[0], shfl_xor2(vb[2], 16));
+  const float2 xb1 = add2(vb[1], shfl_xor2(vb[3], 16));
+  const float2 xc0 = add2(vc[0], shfl_xor2(vc[2], 16));
+  const float2 xc1 = add2(vc[1], shfl_xor2(vc[3], 16));
+  // state bit 1
+  const bool p3 = pl.b3 != 0;
+  const float2 yb = add2(sel2(p3, xb1, xb0), shfl_xor2(sel2(p3, xb0, xb1), 8));
+  const float2 yc = add2(sel2(p3, xc1, xc0), shfl_xor2(sel2(p3, xc0, xc1), 8));
+  // state bit 0 (dB and dC exchanged as one pair)
+  const bool p2 = pl.b2 != 0;
+  const float2 keep = p2 ? make_float2(yb.y, yc.y) : make_float2(yb.x, yc.x);
+  const float2 send = p2 ? make_float2(yb.x, yc.x) : make_float2(yb.y, yc.y);
+  const float2 z = add2(keep, shfl_xor2(send, 4));
+  // dB or dC
+  const bool p1 = pl.b1 != 0;
+  return (p1 ? z.y : z.x) + __shfl_xor_sync(0xffffffffu, p1 ? z.x : z.y, 2);
 }
 
-// Quad reduce-scatter of v[0..3]: lane q of the quad receives the quad sum of v[q].
-__device__ __forceinline__ float quad_scatter(const float v[4], int q) {
-  const bool hi2 = (q & 2) != 0;
-  float k0 = hi2 ? v[2] : v[0];
-  float k1 = hi2 ? v[3] : v[1];
-  const float s0 = hi2 ? v[0] : v[2];
-  const float s1 = hi2 ? v[1] : v[3];
-  k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-  k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-  const bool hi1 = (q & 1) != 0;
-  const float keep = hi1 ? k1 : k0;
-  const float send = hi1 ? k0 : k1;
+// Sum over the lane pair: lane hb receives the pair sum of v[hb].
+__device__ __forceinline__ float pair_scatter(float v0, float v1, int hb) {
+  const float keep = hb ? v1 : v0;
+  const float send = hb ? v0 : v1;
   return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
 // Per-thread state of the VJP that lives across boxes.
 struct BwdLane {
-  float2 Ar[2][2];     // A of the lane's 4 states, per channel, as pairs
-  float2 P[2][2];      // dA_{t+1} * dh_{t+1} carried backwards
-  float2 dAacc[2][2];  // running dA partials
-  float dDacc;         // running dD partial (lanes gq < 2, channel gq)
+  float2 Ar[2][4];     // A of the lane's 8 states (slot order), per channel
+  float2 P[2][4];      // dA_{t+1} * dh_{t+1} carried backwards
+  float2 dAacc[2][4];  // running dA partials
+  float dDacc;         // running dD partial of the own channel
 };
 
-// One box of the VJP.  FULL: the box has all TMAX rows (no per-step guards).
-template <bool FULL, bool HAS_Z, bool REV>
-__device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uint32_t taddr, int nv, int warp, int lane,
-                                        int dl0, bool has_ck, bool v0, bool v1, const float (&Dd)[2], float* du_b,
-                                        float* dt_b,
-                                        float* dz_b, int64_t sdus, int64_t sdts, int64_t sdzs, bool ev) {
+// exp(delta A) of the lane's 8 states of one channel; the forward recompute
+// and the reverse pass call this with identical arguments.
+__device__ __forceinline__ void decay8(float dl, const float2 Ar[4], float2 e[4]) {
+  const float2 dlb = bcast2(dl), off2 = bcast2(kEx2ArgBias);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 a = fma2(dlb, Ar[j], off2);
+    e[j] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
+  }
+}
+
+__device__ __forceinline__ void load8(const float* p, const PairLane& pl, float2 v[4]) {
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const float4 q = lds4(p + pl.group_state(g));
+    v[2 * g] = make_float2(q.x, q.y);
+    v[2 * g + 1] = make_float2(q.z, q.w);
+  }
+}
+
+// Global store under a predicate (no branch, no reconvergence region).
+__device__ __forceinline__ void stg_if(float* p, float v, bool pred) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}" ::"l"(p), "f"(v),
+      "r"(int(pred)));
+}
+
+// What a reverse step hands to its epilogue.  The epilogue (cross-lane sums,
+// stores) of step s runs after the state math of step s - 1, so its shuffle
+// chains overlap independent work instead of stalling the in-order warp.
+struct RevCarry {
+  float2 vb[4], vc[4];  // dB / dC partials of the lane's 8 states (2 channels summed)
+  float sBc[2], sAc[2];  // per channel: sum_n dh B, sum_n A g over the lane's states
+  float dyo, uo, to;     // own channel: dy', u, delta
+  int r;                 // stage row
+};
+
+// State math of one reverse step (row r) with the history h_{s-1} in hp.
+__device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], float2 (&dAbox)[2][4], float& dDbox,
+                                             const uint32_t (&hp)[16], const float* __restrict__ stg, int r,
+                                             int c0l, const PairLane& pl, RevCarry& k) {
   using Cfg = BwdCfg;
   constexpr int DT = Cfg::DT;
-  const int gq = lane & 3;
-  const float* su = stg + dl0;
-  const float* sdt = stg + Cfg::OFF_DT + dl0;
-  const float* sz = stg + Cfg::OFF_Z + dl0;
-  float* sdy = stg + Cfg::OFF_DY + dl0;
-  const float* sB = stg + Cfg::OFF_B + 4 * gq;
-  const float* sC = stg + Cfg::OFF_C + 4 * gq;
-  const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
-  const int ech = gq & 1;       // epilogue channel of this lane
-  const int ekind = gq >> 1;    // gate pass: step parity; reverse pass: 0 du, 1 ddelta
+  const float2 dy2 = lds2(stg + Cfg::OFF_DY + r * DT + c0l);
+  const float2 u2 = lds2(stg + r * DT + c0l);
+  const float2 t2 = lds2(stg + Cfg::OFF_DT + r * DT + c0l);
+  float2 B2[4], C2[4];
+  load8(stg + Cfg::OFF_B + r * NS, pl, B2);
+  load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+  const float2 du2 = mul2(t2, u2);
+  const float2 dl2 = mul2(t2, bcast2(kLog2e));
+  const float dyc[2] = {dy2.x, dy2.y}, duc[2] = {du2.x, du2.y}, dtc[2] = {t2.x, t2.y}, dlc[2] = {dl2.x, dl2.y};
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    float2 e[4];
+    decay8(dlc[c], L.Ar[c], e);
+    const float2 dyb = bcast2(dyc[c]), dub = bcast2(duc[c]), dtb = bcast2(dtc[c]);
+    // two accumulators per sum keep the dependent chains short
+    float2 sB2[2], sA2[2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 h1 = make_float2(__uint_as_float(hp[8 * c + 2 * j]), __uint_as_float(hp[8 * c + 2 * j + 1]));
+      const float2 dh = fma2(C2[j], dyb, L.P[c][j]);
+      const float2 pn = mul2(e[j], dh);
+      const float2 gg = mul2(pn, h1);
+      sB2[j & 1] = j < 2 ? mul2(dh, B2[j]) : fma2(dh, B2[j], sB2[j & 1]);
+      sA2[j & 1] = j < 2 ? mul2(L.Ar[c][j], gg) : fma2(L.Ar[c][j], gg, sA2[j & 1]);
+      dAbox[c][j] = fma2(dtb, gg, dAbox[c][j]);
+      k.vb[j] = c ? fma2(dh, dub, k.vb[j]) : mul2(dh, dub);
+      k.vc[j] = c ? fma2(dyb, hs[c][j], k.vc[j]) : mul2(dyb, hs[c][j]);
+      L.P[c][j] = pn;
+      hs[c][j] = h1;
+    }
+    const float2 sB = add2(sB2[0], sB2[1]), sA = add2(sA2[0], sA2[1]);
+    k.sBc[c] = sB.x + sB.y;
+    k.sAc[c] = sA.x + sA.y;
+  }
+  k.dyo = pl.hb ? dy2.y : dy2.x;
+  k.uo = pl.hb ? u2.y : u2.x;
+  k.to = pl.hb ? t2.y : t2.x;
+  k.r = r;
+  dDbox = fmaf(k.dyo, k.uo, dDbox);
+}
 
-  float2 h[2][2];
+// Epilogue of a reverse step: du / ddelta of the own channel, dB / dC row partial.
+__device__ __forceinline__ void bwd_rev_epilogue(const RevCarry& k, const float* __restrict__ stg,
+                                                 float* __restrict__ part, int warp, const PairLane& pl, float Down,
+                                                 float* du_b, float* dt_b, int sdus, int sdts, bool ev) {
+  using Cfg = BwdCfg;
+  const int tk = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK)[k.r];
+  const float sB = pair_scatter(k.sBc[0], k.sBc[1], pl.hb);
+  const float sA = pair_scatter(k.sAc[0], k.sAc[1], pl.hb);
+  stg_if(du_b + int64_t(tk) * sdus, fmaf(k.dyo, Down, k.to * sB), ev);
+  stg_if(dt_b + int64_t(tk) * sdts, fmaf(k.uo, sB, sA), ev);
+  part[(k.r * Cfg::NCW + warp) * 32 + pl.part_slot()] = dbc_reduce_scatter(k.vb, k.vc, pl);
+}
+
+// What a recompute step hands to its gate epilogue.
+struct FwdCarry {
+  float yp[2];  // C . h over the lane's 8 states, per channel
+  float uo;     // own channel u
+  int r;
+};
+
+// One box of the VJP (nv rows).
+template <bool HAS_Z, bool REV>
+__device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, float* __restrict__ part, uint32_t taddr, int nv, int warp,
+                                        int lane, int c0l, const PairLane& pl, bool has_ck, bool v0, bool v1,
+                                        float Down, float* du_b, float* dt_b, float* dz_b, int sdus, int sdts,
+                                        int sdzs, bool ev) {
+  using Cfg = BwdCfg;
+  constexpr int DT = Cfg::DT;
+  const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
+  const int own = c0l + pl.hb;
+
+  float2 h[2][4];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     // the checkpoint copy only covers valid channels; other rows are stale
     if (has_ck && (c ? v1 : v0)) {
-      const float4 v = lds4(stg + Cfg::OFF_CK + (dl0 + c) * NS + 4 * gq);
-      h[c][0] = make_float2(v.x, v.y);
-      h[c][1] = make_float2(v.z, v.w);
+      load8(stg + Cfg::OFF_CK + (c0l + c) * NS, pl, h[c]);
     } else {
-      h[c][0] = h[c][1] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[c][j] = make_float2(0.f, 0.f);
     }
   }
-  const float2 log2e2 = bcast2(kLog2e), off2 = bcast2(kEx2ArgBias);
 
   // ---- forward pass: recompute, park history in TMEM, gate ----
+  auto fwd_math = [&](int s, FwdCarry& k) {
+    const int r = REV ? nv - 1 - s : s;
+    const float2 u2 = lds2(stg + r * DT + c0l);
+    const float2 t2 = lds2(stg + Cfg::OFF_DT + r * DT + c0l);
+    float2 B2[4];
+    load8(stg + Cfg::OFF_B + r * NS, pl, B2);
+    const float2 du2 = mul2(t2, u2);
+    const float2 dl2 = mul2(t2, bcast2(kLog2e));
+    const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
+    float hist[16];
 #pragma unroll
-  for (int s0 = 0; s0 < TMAX; s0 += 2) {
-    if (FULL || s0 < nv) {
-      float v[4];
+    for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int p2 = 0; p2 < 2; ++p2) {
-        const int s = s0 + p2;
-        v[2 * p2] = v[2 * p2 + 1] = 0.f;
-        if (FULL || s < nv) {
-          const int r = REV ? nv - 1 - s : s;
-          const float2 u2 = lds2(su + r * DT);
-          const float2 t2 = lds2(sdt + r * DT);
-          const float4 Bv = lds4(sB + r * NS);
-          const float2 B2[2] = {make_float2(Bv.x, Bv.y), make_float2(Bv.z, Bv.w)};
-          const float2 du2 = mul2(t2, u2);
-          const float2 dl2 = mul2(t2, log2e2);
-          const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
-          const float hist[8] = {h[0][0].x, h[0][0].y, h[0][1].x, h[0][1].y,
-                                 h[1][0].x, h[1][0].y, h[1][1].x, h[1][1].y};
-          tmem_st8(taddr + 8 * s, hist);
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const float2 dlb = bcast2(dlc[c]), dub = bcast2(duc[c]);
-            const float2 a0 = fma2(dlb, L.Ar[c][0], off2);
-            const float2 a1 = fma2(dlb, L.Ar[c][1], off2);
-            const float2 e0 = make_float2(ex2_approx(a0.x), ex2_approx(a0.y));
-            const float2 e1 = make_float2(ex2_approx(a1.x), ex2_approx(a1.y));
-            h[c][0] = fma2(e0, h[c][0], mul2(dub, B2[0]));
-            h[c][1] = fma2(e1, h[c][1], mul2(dub, B2[1]));
-          }
-          if (HAS_Z) {
-            const float4 Cv = lds4(sC + r * NS);
-            const float2 C01 = make_float2(Cv.x, Cv.y), C23 = make_float2(Cv.z, Cv.w);
-            const float2 y0 = fma2(h[0][1], C23, mul2(h[0][0], C01));
-            const float2 y1 = fma2(h[1][1], C23, mul2(h[1][0], C01));
-            v[2 * p2] = y0.x + y0.y;
-            v[2 * p2 + 1] = y1.x + y1.y;
-          }
-        }
+      for (int j = 0; j < 4; ++j) {
+        hist[8 * c + 2 * j] = h[c][j].x;
+        hist[8 * c + 2 * j + 1] = h[c][j].y;
       }
-      if (HAS_Z) {
-        // lane gq: step s0 + (gq >> 1), channel gq & 1
-        const float ys = quad_scatter(v, gq);
-        const int s = s0 + ekind;
-        if (FULL || s < nv) {
-          const int r = REV ? nv - 1 - s : s;
-          const float zz = sz[r * DT + ech];
-          const float dyv = sdy[r * DT + ech];
-          const float ypre = fmaf(su[r * DT + ech], ech ? Dd[1] : Dd[0], ys);
-          const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * zz));
-          if (ev) dz_b[ech + int64_t(tok[r]) * sdzs] = dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f);
-          sdy[r * DT + ech] = dyv * (zz * sig);
-        }
-      }
+    tmem_st16(taddr + 16 * s, hist);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float2 e[4];
+      decay8(dlc[c], L.Ar[c], e);
+      const float2 dub = bcast2(duc[c]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) h[c][j] = fma2(e[j], h[c][j], mul2(dub, B2[j]));
     }
+    if (HAS_Z) {
+      float2 C2[4];
+      load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float2 acc = add2(fma2(C2[1], h[c][1], mul2(C2[0], h[c][0])), fma2(C2[3], h[c][3], mul2(C2[2], h[c][2])));
+        k.yp[c] = acc.x + acc.y;
+      }
+      k.uo = pl.hb ? u2.y : u2.x;
+      k.r = r;
+    }
+  };
+  // gate of the own channel: y_pre, dy' (written over dy in the stage), dz
+  auto fwd_epilogue = [&](const FwdCarry& k) {
+    const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
+    const float zz = stg[Cfg::OFF_Z + k.r * DT + own];
+    float* sdy = stg + Cfg::OFF_DY + k.r * DT + own;
+    const float dyv = *sdy;
+    const float ypre = fmaf(k.uo, Down, ys);
+    const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * zz));
+    stg_if(dz_b + int64_t(tok[k.r]) * sdzs, dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f), ev);
+    *sdy = dyv * (zz * sig);
+  };
+  {
+    FwdCarry fa, fb;
+    fwd_math(0, fa);
+#pragma unroll 2
+    for (int s = 1; s < nv; ++s) {
+      fwd_math(s, fb);
+      if (HAS_Z) fwd_epilogue(fa);
+      fa = fb;
+    }
+    if (HAS_Z) fwd_epilogue(fa);
   }
   tmem_wait_st();
   __syncwarp();
@@ -211,108 +320,68 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* stg, float* part, uin
   // ---- reverse adjoint over the box ----
   // dA / dD are summed per box first and folded into the running totals
   // once per box: L/16 + 16 additions per total instead of L in a row.
-  float2 dAbox[2][2];
+  float2 dAbox[2][4];
 #pragma unroll
-  for (int c = 0; c < 2; ++c) dAbox[c][0] = dAbox[c][1] = make_float2(0.f, 0.f);
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dAbox[c][j] = make_float2(0.f, 0.f);
   float dDbox = 0.f;
-  float2 hs[2][2] = {{h[0][0], h[0][1]}, {h[1][0], h[1][1]}};
-  uint32_t X[2][8];  // two alternating history buffers: h_{s-1} of slot s in X[s & 1]
-  {
-    const int s = FULL ? TMAX - 1 : nv - 1;
-    if (FULL || (s & 1)) {
-      tmem_ld8(taddr + 8 * s, X[1]);
-      tmem_wait_ld8(X[1]);
-    } else {
-      tmem_ld8(taddr + 8 * s, X[0]);
-      tmem_wait_ld8(X[0]);
-    }
+  float2 hs[2][4];
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hs[c][j] = h[c][j];
+  // Two history buffers: the current step's h_{s-1} and the next one in
+  // flight.  Each step's epilogue runs after the next step's math.  The pair
+  // loop body has no branch; its look-ahead load is clamped to column 0
+  // (re-reading a valid column) on the last pair.
+  uint32_t XA[16], XB[16];
+  RevCarry ka, kb;
+  auto row = [&](int s) { return REV ? nv - 1 - s : s; };
+  int s = nv - 1;
+  tmem_ld16(taddr + 16 * s, XA);
+  tmem_wait_ld16(XA);
+  if (s > 0) tmem_ld16(taddr + 16 * (s - 1), XB);
+  bwd_rev_math(L, hs, dAbox, dDbox, XA, stg, row(s), c0l, pl, ka);
+  if (s > 0) tmem_wait_ld16(XB);
+  for (--s; s >= 1; s -= 2) {
+    tmem_ld16(taddr + 16 * (s - 1), XA);
+    bwd_rev_math(L, hs, dAbox, dDbox, XB, stg, row(s), c0l, pl, kb);
+    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    tmem_wait_ld16(XA);
+    tmem_ld16(taddr + 16 * max(s - 2, 0), XB);
+    bwd_rev_math(L, hs, dAbox, dDbox, XA, stg, row(s - 1), c0l, pl, ka);
+    bwd_rev_epilogue(kb, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    tmem_wait_ld16(XB);
+  }
+  if (s == 0) {
+    bwd_rev_math(L, hs, dAbox, dDbox, XB, stg, row(0), c0l, pl, kb);
+    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_epilogue(kb, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+  } else {
+    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
   }
 #pragma unroll
-  for (int s = TMAX - 1; s >= 0; --s) {
-    if (FULL || s < nv) {
-      uint32_t* cur = X[s & 1];
-      if (s > 0) tmem_ld8(taddr + 8 * (s - 1), X[(s - 1) & 1]);
-      const int r = REV ? nv - 1 - s : s;
-      const float2 dy2 = lds2(sdy + r * DT);
-      const float2 u2 = lds2(su + r * DT);
-      const float2 t2 = lds2(sdt + r * DT);
-      const float4 Bv = lds4(sB + r * NS);
-      const float4 Cv = lds4(sC + r * NS);
-      const float2 B2[2] = {make_float2(Bv.x, Bv.y), make_float2(Bv.z, Bv.w)};
-      const float2 C2[2] = {make_float2(Cv.x, Cv.y), make_float2(Cv.z, Cv.w)};
-      const float2 du2 = mul2(t2, u2);
-      const float2 dl2 = mul2(t2, log2e2);
-      const float dyc[2] = {dy2.x, dy2.y}, duc[2] = {du2.x, du2.y}, dtc[2] = {t2.x, t2.y},
-                  uc[2] = {u2.x, u2.y}, dlc[2] = {dl2.x, dl2.y};
-      float2 vb[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      float2 vc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      float red4[4];
+  for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        // exp(delta*A) recomputed exactly as in the forward pass (same operations)
-        const float2 dlb = bcast2(dlc[c]);
-        const float2 a0 = fma2(dlb, L.Ar[c][0], off2);
-        const float2 a1 = fma2(dlb, L.Ar[c][1], off2);
-        const float2 e[2] = {make_float2(ex2_approx(a0.x), ex2_approx(a0.y)),
-                             make_float2(ex2_approx(a1.x), ex2_approx(a1.y))};
-        const float2 hp[2] = {make_float2(__uint_as_float(cur[4 * c + 0]), __uint_as_float(cur[4 * c + 1])),
-                              make_float2(__uint_as_float(cur[4 * c + 2]), __uint_as_float(cur[4 * c + 3]))};
-        const float2 dyb = bcast2(dyc[c]), dub = bcast2(duc[c]), dtb = bcast2(dtc[c]);
-        float2 sB2 = make_float2(0.f, 0.f), sAg2 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const float2 dh = fma2(C2[p], dyb, L.P[c][p]);
-          const float2 gg = mul2(dh, mul2(e[p], hp[p]));
-          sB2 = fma2(dh, B2[p], sB2);
-          sAg2 = fma2(L.Ar[c][p], gg, sAg2);
-          dAbox[c][p] = fma2(dtb, gg, dAbox[c][p]);
-          vb[p] = fma2(dh, dub, vb[p]);
-          vc[p] = fma2(dyb, hs[c][p], vc[p]);
-          L.P[c][p] = mul2(e[p], dh);
-          hs[c][p] = hp[p];
-        }
-        const float sB = sB2.x + sB2.y;
-        red4[c] = dtc[c] * sB;                        // -> du (minus the skip term)
-        red4[2 + c] = fmaf(uc[c], sB, sAg2.x + sAg2.y);  // -> ddelta
-      }
-      // lane gq: gq < 2 -> du of channel gq, gq >= 2 -> ddelta of channel gq - 2
-      const float w = quad_scatter(red4, gq);
-      if (ev) {
-        const int64_t tk = tok[r];
-        if (ekind == 0)
-          du_b[ech + tk * sdus] = fmaf(ech ? dyc[1] : dyc[0], ech ? Dd[1] : Dd[0], w);
-        else
-          dt_b[ech + tk * sdts] = w;
-      }
-      if (ekind == 0) dDbox = fmaf(ech ? dyc[1] : dyc[0], ech ? uc[1] : uc[0], dDbox);
-      const float vbs[4] = {vb[0].x, vb[0].y, vb[1].x, vb[1].y};
-      const float vcs[4] = {vc[0].x, vc[0].y, vc[1].x, vc[1].y};
-      part[(r * Cfg::NCW + warp) * 32 + part_slot(lane)] = warp_reduce8_scatter(vbs, vcs, lane);
-      if (s > 0) tmem_wait_ld8(X[(s - 1) & 1]);
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    L.dAacc[c][0] = add2(L.dAacc[c][0], dAbox[c][0]);
-    L.dAacc[c][1] = add2(L.dAacc[c][1], dAbox[c][1]);
-  }
+    for (int j = 0; j < 4; ++j) L.dAacc[c][j] = add2(L.dAacc[c][j], dAbox[c][j]);
   L.dDacc += dDbox;
 }
 
 template <bool HAS_Z, bool REV>
-__global__ void __launch_bounds__(BwdCfg::NT, 3)
+__global__ void __launch_bounds__(BwdCfg::NT, 2)
     scan_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_dy,
                     const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
-                    float* __restrict__ du_out, int64_t sdub, int64_t sdus, float* __restrict__ ddt_out,
-                    int64_t sdtb, int64_t sdts, float* __restrict__ dz_out, int64_t sdzb, int64_t sdzs,
+                    float* __restrict__ du_out, int64_t sdub, int sdus, float* __restrict__ ddt_out,
+                    int64_t sdtb, int sdts, float* __restrict__ dz_out, int64_t sdzb, int sdzs,
                     const float* __restrict__ A, const float* __restrict__ Dskip, const float* __restrict__ ckpt,
                     float* __restrict__ wpart, float* __restrict__ wA, float* __restrict__ wD, const ScanGeom g,
                     int* __restrict__ status) {
   using Cfg = BwdCfg;
   constexpr int DT = Cfg::DT, NST = Cfg::NST, NCT = Cfg::NCT, NCW = Cfg::NCW;
   extern __shared__ unsigned char smem_raw[];
-  float* sm = reinterpret_cast<float*>(align_up_1024(smem_raw));
+  float* sm = smem_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::OFF_BAR);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
@@ -342,10 +411,10 @@ __global__ void __launch_bounds__(BwdCfg::NT, 3)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t taddr = tmem_base + (uint32_t(warp * 32) << 16);  // this warp's lane quarter
 
-  // Warp 0 doubles as the producer: for box i it writes the row -> token table
-  // (one row per lane) and the row count, then lane 0 issues the stage's TMA
-  // loads and the checkpoint bulk copy.  A stage is reused once all warps
-  // released it.
+  // The producer (warp 0 for the first stages, then warp i % NCW issuing box
+  // i + NST - 1) writes the row -> token table (one row per lane) and the row
+  // count, then its lane 0 issues the stage's TMA loads and the checkpoint
+  // bulk copy.  A stage is reused once all warps released it.
   auto issue = [&](int i) {  // called by one whole warp
     const int st = i % NST;
     const uint32_t ph = uint32_t(i / NST) & 1u;
@@ -390,28 +459,31 @@ __global__ void __launch_bounds__(BwdCfg::NT, 3)
     for (int i = 0; i < NST - 1 && i < g.nboxes; ++i) issue(i);
   }
 
-  const int q = lane >> 2;
-  const int gq = lane & 3;
-  const int dl0 = warp * 16 + 2 * q;  // the quad's two channels: dl0, dl0 + 1
-  const int dc = d0 + dl0;
+  const PairLane pl(lane);
+  const int c0l = warp * 32 + (lane & ~1);  // the pair's two channels: c0l, c0l + 1 (tile-local)
+  const int dc = d0 + c0l;
   const bool v0 = dc < g.d_inner, v1 = dc + 1 < g.d_inner;
+  const bool ev = pl.hb ? v1 : v0;  // the own channel d0 + c0l + hb exists
   BwdLane L;
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const bool vc = c ? v1 : v0;
-    const float4 a4 = vc ? *reinterpret_cast<const float4*>(A + size_t(dc + c) * NS + 4 * gq)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    L.Ar[c][0] = make_float2(a4.x, a4.y);
-    L.Ar[c][1] = make_float2(a4.z, a4.w);
-    L.P[c][0] = L.P[c][1] = make_float2(0.f, 0.f);
-    L.dAacc[c][0] = L.dAacc[c][1] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const float4 a4 = vc ? *reinterpret_cast<const float4*>(A + size_t(dc + c) * NS + pl.group_state(gi))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      L.Ar[c][2 * gi] = make_float2(a4.x, a4.y);
+      L.Ar[c][2 * gi + 1] = make_float2(a4.z, a4.w);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) L.P[c][j] = L.dAacc[c][j] = make_float2(0.f, 0.f);
   }
   L.dDacc = 0.f;
-  const float Dd[2] = {v0 ? Dskip[dc] : 0.f, v1 ? Dskip[dc + 1] : 0.f};
-  const bool ev = (gq & 1) ? v1 : v0;  // the epilogue channel of this lane exists
-  float* du_b = du_out + b * sdub + dc;
-  float* dt_b = ddt_out + b * sdtb + dc;
-  float* dz_b = HAS_Z ? dz_out + b * sdzb + dc : nullptr;
+  const int own = dc + pl.hb;
+  const float Down = ev ? Dskip[own] : 0.f;
+  float* du_b = du_out + b * sdub + own;
+  float* dt_b = ddt_out + b * sdtb + own;
+  float* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
   bool alive = true;
 
   for (int i = 0; i < g.nboxes; ++i) {
@@ -427,14 +499,9 @@ __global__ void __launch_bounds__(BwdCfg::NT, 3)
     float* part = sm + Cfg::OFF_PART + (i & 1) * (TMAX * NCW * 32);
     float* stg = sm + st * Cfg::STAGE_F;
     const int nv = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK)[TMAX];
-    if (alive) {
-      if (nv == TMAX)
-        bwd_box<true, HAS_Z, REV>(L, stg, part, taddr, nv, warp, lane, dl0, ib > 0, v0, v1, Dd, du_b, dt_b, dz_b,
-                                  sdus, sdts, sdzs, ev);
-      else
-        bwd_box<false, HAS_Z, REV>(L, stg, part, taddr, nv, warp, lane, dl0, ib > 0, v0, v1, Dd, du_b, dt_b, dz_b,
-                                   sdus, sdts, sdzs, ev);
-    }
+    if (alive)
+      bwd_box<HAS_Z, REV>(L, stg, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
+                          sdus, sdts, sdzs, ev);
     // dy' was written into the stage: order those generic-proxy writes before
     // the TMA load that will refill the stage
     fence_proxy_async_smem();
@@ -460,11 +527,15 @@ __global__ void __launch_bounds__(BwdCfg::NT, 3)
 
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
-    if (c ? v1 : v0)
-      *reinterpret_cast<float4*>(wA + (size_t(b) * g.d_inner + dc + c) * NS + 4 * gq) =
-          make_float4(L.dAacc[c][0].x, L.dAacc[c][0].y, L.dAacc[c][1].x, L.dAacc[c][1].y);
+    if (c ? v1 : v0) {
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi)
+        *reinterpret_cast<float4*>(wA + (size_t(b) * g.d_inner + dc + c) * NS + pl.group_state(gi)) =
+            make_float4(L.dAacc[c][2 * gi].x, L.dAacc[c][2 * gi].y, L.dAacc[c][2 * gi + 1].x,
+                        L.dAacc[c][2 * gi + 1].y);
+    }
   }
-  if ((gq >> 1) == 0 && ev) wD[size_t(b) * g.d_inner + dc + (gq & 1)] = L.dDacc;
+  if (ev) wD[size_t(b) * g.d_inner + own] = L.dDacc;
   tmem_fence_before_sync();
   __syncthreads();
   if (warp == 0) {

@@ -165,6 +165,33 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float v[8]) {
       : "memory");
 }
 
+// Store 16 consecutive columns of this thread's lane.  The 16-column TMEM
+// helpers carry no memory clobber: Tensor Memory is not reachable by ordinary
+// loads and stores, the tcgen05 statements stay ordered among themselves (all
+// volatile), and loaded registers are tied to the wait, so shared/global
+// accesses may be scheduled across them.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float v[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])));
+}
+
+// Issue a load of 16 consecutive columns; valid after tmem_wait_ld16 on the same array.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t r[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Issue a load of 8 consecutive columns.  The registers are not valid until
@@ -182,7 +209,7 @@ __device__ __forceinline__ void tmem_wait_ld16(uint32_t r[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
                  "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                 "+r"(r[15])::"memory");
+                 "+r"(r[15]));
 }
 
 __device__ __forceinline__ void tmem_wait_ld8(uint32_t r[8]) {
@@ -311,8 +338,13 @@ __device__ __forceinline__ float quad_transpose_sum(const float v[4], int q) {
   return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
-__device__ __forceinline__ unsigned char* align_up_1024(unsigned char* p) {
-  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+// First 1024-byte aligned float of the dynamic shared-memory window.  The
+// offset is added to the shared array itself (not through an integer cast),
+// so the compiler keeps the shared address space: accesses through the
+// result are LDS/STS with 32-bit addresses instead of generic loads.
+__device__ __forceinline__ float* smem_align1024(unsigned char* raw) {
+  const uint32_t a = smem_u32(raw);
+  return reinterpret_cast<float*>(raw + ((1024u - (a & 1023u)) & 1023u));
 }
 
 #endif  // __CUDACC__

@@ -94,14 +94,14 @@ template <int NCW, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
 __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 5)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
-                    const __grid_constant__ CUtensorMap tm_C, float* __restrict__ y, int64_t syb, int64_t sys,
+                    const __grid_constant__ CUtensorMap tm_C, float* __restrict__ y, int64_t syb, int sys,
                     const float* __restrict__ A, const float* __restrict__ Dskip, float* __restrict__ ckpt,
                     const ScanGeom g, int* __restrict__ status) {
   using Cfg = FwdCfg<NCW>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST;
   constexpr bool LOAD_Z = HAS_Z && STORE_Y;
   extern __shared__ unsigned char smem_raw[];
-  float* sm = reinterpret_cast<float*>(align_up_1024(smem_raw));
+  float* sm = smem_align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + NST * Cfg::STAGE_F);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
