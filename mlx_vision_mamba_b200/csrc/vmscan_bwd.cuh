@@ -67,26 +67,6 @@ struct BwdCfg {
 // Rows of the per-(CTA, step) dB/dC partial: 16 dB values then 16 dC values.
 constexpr int kPartRow = 2 * NS;
 
-// Lane roles.  Lane l of a warp: pair l >> 1 owns channels 2(l >> 1) and
-// 2(l >> 1) + 1 of the warp; the lane's own channel (epilogue) is l.  The
-// lane holds states 8 hb .. 8 hb + 7 (hb = l & 1) of both channels, in slot
-// order: slot group g (4 states) holds state group g ^ b4 (b4 = bit 4 of l).
-struct PairLane {
-  int hb, b4, b3, b2, b1;
-  __device__ __forceinline__ explicit PairLane(int lane)
-      : hb(lane & 1), b4((lane >> 4) & 1), b3((lane >> 3) & 1), b2((lane >> 2) & 1), b1((lane >> 1) & 1) {}
-  // first state of slot group g
-  __device__ __forceinline__ int group_state(int g) const { return 8 * hb + 4 * (g ^ b4); }
-  // slot of this lane's value in the 32-float dB/dC row after dbc_reduce_scatter
-  __device__ __forceinline__ int part_slot() const { return 16 * b1 + 8 * hb + 4 * b4 + 2 * b3 + b2; }
-};
-
-__device__ __forceinline__ float2 sel2(bool p, float2 a, float2 b) { return p ? a : b; }
-
-__device__ __forceinline__ float2 shfl_xor2(float2 v, int m) {
-  return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
-}
-
 // Reduce-scatter of the lane's dB partials vb (8 states, slot order, pairs)
 // and dC partials vc over the 16 lanes that hold the same state half.
 // Returns one fully reduced value: dB (b1 == 0) or dC (b1 == 1) of state
@@ -111,13 +91,6 @@ __device__ __forceinline__ float dbc_reduce_scatter(const float2 vb[4], const fl
   return (p1 ? z.y : z.x) + __shfl_xor_sync(0xffffffffu, p1 ? z.x : z.y, 2);
 }
 
-// Sum over the lane pair: lane hb receives the pair sum of v[hb].
-__device__ __forceinline__ float pair_scatter(float v0, float v1, int hb) {
-  const float keep = hb ? v1 : v0;
-  const float send = hb ? v0 : v1;
-  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
-}
-
 // Per-thread state of the VJP that lives across boxes.
 struct BwdLane {
   float2 Ar[2][4];     // A of the lane's 8 states (slot order), per channel
@@ -125,33 +98,6 @@ struct BwdLane {
   float2 dAacc[2][4];  // running dA partials
   float dDacc;         // running dD partial of the own channel
 };
-
-// exp(delta A) of the lane's 8 states of one channel; the forward recompute
-// and the reverse pass call this with identical arguments.
-__device__ __forceinline__ void decay8(float dl, const float2 Ar[4], float2 e[4]) {
-  const float2 dlb = bcast2(dl), off2 = bcast2(kEx2ArgBias);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 a = fma2(dlb, Ar[j], off2);
-    e[j] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-  }
-}
-
-__device__ __forceinline__ void load8(const float* p, const PairLane& pl, float2 v[4]) {
-#pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    const float4 q = lds4(p + pl.group_state(g));
-    v[2 * g] = make_float2(q.x, q.y);
-    v[2 * g + 1] = make_float2(q.z, q.w);
-  }
-}
-
-// Global store under a predicate (no branch, no reconvergence region).
-__device__ __forceinline__ void stg_if(float* p, float v, bool pred) {
-  asm volatile(
-      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}" ::"l"(p), "f"(v),
-      "r"(int(pred)));
-}
 
 // What a reverse step hands to its epilogue.  The epilogue (cross-lane sums,
 // stores) of step s runs after the state math of step s - 1, so its shuffle

@@ -7,18 +7,20 @@
 //   y_t      = sum_n h_t[n] * C_t[n] + u_t * D[d]
 //   out_t    = y_t * silu(z_t)            (when a gate is given)
 //
-// Design.  One CTA owns one batch row and DT = 16*NCW channels for the whole
+// Design.  One CTA owns one batch row and DT = 32*NCW channels for the whole
 // sequence.  A producer warp streams boxes of <= 16 scan steps of u, delta,
 // z (DT channels each) and B, C (16 states) through an NST-stage TMA ring;
 // the tensor maps carry the direction (token permutation), so the consumer
 // code only knows "row r of the box".  The producer also writes the token of
 // every row into the stage, which the consumers use to store y directly to
-// global memory (no output staging, no CTA barriers).  Each consumer quad (4
-// lanes) owns two adjacent channels; each lane holds 4 of the 16 states of
-// both channels in registers, so B/C loads and the quad shuffles serve two
-// channels.  The quad reduce-scatter of y leaves each lane one (step,
-// channel) pair per two steps, so the skip/gate epilogue runs once per output.
-// The state at the end of each box is stored as a checkpoint for the VJP.
+// global memory (no output staging, no CTA barriers).  A lane pair owns two
+// adjacent channels and each lane holds 8 of the 16 states of both (lane bit
+// 0 picks the half), so every B/C load serves two channels and the sum of
+// C.h over states is one pair exchange that leaves each lane the output of
+// its own channel.  Each step's epilogue (that exchange, the skip term, the
+// gate and the store) runs after the next step's state math so its latency
+// overlaps independent work.  The state at the end of each box is stored as
+// a checkpoint for the VJP.
 #pragma once
 
 #include "vmscan_common.cuh"
@@ -27,10 +29,10 @@ namespace vmscan {
 
 template <int NCW>
 struct FwdCfg {
-  static constexpr int DT = 16 * NCW;          // channels per CTA (2 per quad)
+  static constexpr int DT = 32 * NCW;          // channels per CTA (32 per warp, 2 per lane pair)
   static constexpr int NCT = NCW * 32;         // consumer threads
   static constexpr int NT = NCT + 32;          // + producer warp
-  static constexpr int NST = 3;                // TMA pipeline stages
+  static constexpr int NST = 2;                // TMA pipeline stages
   static constexpr int TILE = TMAX * DT;       // floats of one (step, channel) tile
   static constexpr int BCT = TMAX * NS;        // floats of one (step, state) tile
   static constexpr int TOKF = 32;              // row -> token table (int32), padded
@@ -39,59 +41,8 @@ struct FwdCfg {
   static constexpr size_t SMEM_BYTES = size_t(NST * STAGE_F) * 4 + 2 * NST * 8 + 16 + 1024;
 };
 
-// One forward step for the two channels of a lane: updates h, returns the
-// lane's partial of C.h for each channel.  Shared by the forward kernel and
-// the VJP's recompute so both produce bit-identical states.
-struct Step2 {
-  float y0, y1;
-};
-
-template <bool WANT_Y>
-__device__ __forceinline__ Step2 fwd_step2(float2 (&h)[2][2], const float2 (&Ar)[2][2], float u0, float u1,
-                                           float dt0, float dt1, const float4& Bv, const float4& Cv) {
-  const float du[2] = {dt0 * u0, dt1 * u1};
-  const float dl[2] = {dt0 * kLog2e, dt1 * kLog2e};
-  const float2 B2[2] = {make_float2(Bv.x, Bv.y), make_float2(Bv.z, Bv.w)};
-  Step2 out{0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const float2 du2 = bcast2(du[c]);
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const float2 a = fma2(bcast2(dl[c]), Ar[c][p], bcast2(kEx2ArgBias));
-      const float2 e = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-      h[c][p] = fma2(e, h[c][p], mul2(du2, B2[p]));
-    }
-  }
-  if (WANT_Y) {
-    const float2 C01 = make_float2(Cv.x, Cv.y), C23 = make_float2(Cv.z, Cv.w);
-    const float2 y0 = fma2(h[0][1], C23, mul2(h[0][0], C01));
-    const float2 y1 = fma2(h[1][1], C23, mul2(h[1][0], C01));
-    out.y0 = y0.x + y0.y;
-    out.y1 = y1.x + y1.y;
-  }
-  return out;
-}
-
-// Quad reduce-scatter of v = {ch0 step a, ch1 step a, ch0 step b, ch1 step b}:
-// lane q of the quad receives the quad sum of v[q], i.e. step (q >> 1),
-// channel (q & 1).
-__device__ __forceinline__ float quad_scatter4(const float v[4], int q) {
-  const bool hi2 = (q & 2) != 0;
-  float k0 = hi2 ? v[2] : v[0];
-  float k1 = hi2 ? v[3] : v[1];
-  const float s0 = hi2 ? v[0] : v[2];
-  const float s1 = hi2 ? v[1] : v[3];
-  k0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-  k1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-  const bool hi1 = (q & 1) != 0;
-  const float keep = hi1 ? k1 : k0;
-  const float send = hi1 ? k0 : k1;
-  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
-}
-
 template <int NCW, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
-__global__ void __launch_bounds__(FwdCfg<NCW>::NT, 5)
+__global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
                     const __grid_constant__ CUtensorMap tm_C, float* __restrict__ y, int64_t syb, int sys,
@@ -154,27 +105,34 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 5)
   }
 
   // ---------------- consumer warps ----------------
-  const int q = lane >> 2;                   // quad within the warp
-  const int gq = lane & 3;                   // state group: states 4*gq .. 4*gq+3
-  const int dl0 = warp * 16 + 2 * q;         // first of the quad's two channels
-  const int dc = d0 + dl0;
+  const PairLane pl(lane);
+  const int c0l = warp * 32 + (lane & ~1);  // the pair's two channels: c0l, c0l + 1 (tile-local)
+  const int dc = d0 + c0l;
   const bool v0 = dc < g.d_inner, v1 = dc + 1 < g.d_inner;
-  float2 Ar[2][2], h[2][2];
+  const bool ev = pl.hb ? v1 : v0;  // the own channel d0 + c0l + hb exists
+  float2 Ar[2][4], h[2][4];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const bool vc = c ? v1 : v0;
-    const float4 a4 = vc ? *reinterpret_cast<const float4*>(A + size_t(dc + c) * NS + 4 * gq)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-    Ar[c][0] = make_float2(a4.x, a4.y);
-    Ar[c][1] = make_float2(a4.z, a4.w);
-    h[c][0] = h[c][1] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const float4 a4 = vc ? *reinterpret_cast<const float4*>(A + size_t(dc + c) * NS + pl.group_state(gi))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      Ar[c][2 * gi] = make_float2(a4.x, a4.y);
+      Ar[c][2 * gi + 1] = make_float2(a4.z, a4.w);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[c][j] = make_float2(0.f, 0.f);
   }
-  // epilogue role of this lane: channel (gq & 1), step parity (gq >> 1)
-  const int ech = gq & 1;
-  const bool evalid = ech ? v1 : v0;
-  const float Dd = evalid ? Dskip[dc + ech] : 0.f;
-  float* ybase = y + b * syb + dc + ech;
+  const int own = c0l + pl.hb;
+  const float Down = ev ? Dskip[d0 + own] : 0.f;
+  float* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
   bool alive = true;
+
+  struct Carry {
+    float yp[2];  // C . h over the lane's 8 states, per channel
+    int r;
+  };
 
   for (int i = 0; i < g.nboxes; ++i) {
     const int st = i % NST;
@@ -188,52 +146,66 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 5)
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles below need the whole warp
     if (alive) {
-      const float* su = sm + st * Cfg::STAGE_F + dl0;
-      const float* sdt = su + Cfg::TILE;
-      const float* sz = su + Cfg::OFF_Z;
-      const float* sB = sm + st * Cfg::STAGE_F + Cfg::OFF_B + 4 * gq;
-      const float* sC = sm + st * Cfg::STAGE_F + Cfg::OFF_C + 4 * gq;
-      const int* tok = reinterpret_cast<const int*>(sm + st * Cfg::STAGE_F + Cfg::OFF_TOK);
-      // two steps at a time: the quad scatter needs a pair
+      const float* __restrict__ stg = sm + st * Cfg::STAGE_F;
+      const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
+      auto math = [&](int s, Carry& k) {
+        const int r = REV ? nv - 1 - s : s;
+        const float2 u2 = lds2(stg + r * DT + c0l);
+        const float2 t2 = lds2(stg + Cfg::TILE + r * DT + c0l);
+        float2 B2[4];
+        load8(stg + Cfg::OFF_B + r * NS, pl, B2);
+        const float2 du2 = mul2(t2, u2);
+        const float2 dl2 = mul2(t2, bcast2(kLog2e));
+        const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
 #pragma unroll
-      for (int s0 = 0; s0 < TMAX; s0 += 2) {
-        if (s0 < nv) {
-          float v[4];
+        for (int c = 0; c < 2; ++c) {
+          float2 e[4];
+          decay8(dlc[c], Ar[c], e);
+          const float2 dub = bcast2(duc[c]);
 #pragma unroll
-          for (int p = 0; p < 2; ++p) {
-            const int s = s0 + p;
-            v[2 * p] = 0.f;
-            v[2 * p + 1] = 0.f;
-            if (s < nv) {
-              const int r = REV ? nv - 1 - s : s;
-              const float2 u2 = lds2(su + r * DT);
-              const float2 t2 = lds2(sdt + r * DT);
-              const float4 Bv = lds4(sB + r * NS);
-              const float4 Cv = STORE_Y ? lds4(sC + r * NS) : make_float4(0.f, 0.f, 0.f, 0.f);
-              const Step2 o = fwd_step2<STORE_Y>(h, Ar, u2.x, u2.y, t2.x, t2.y, Bv, Cv);
-              v[2 * p] = o.y0;
-              v[2 * p + 1] = o.y1;
-            }
-          }
-          if (STORE_Y) {
-            const float ys = quad_scatter4(v, gq);
-            const int s = s0 + (gq >> 1);
-            if (s < nv && evalid) {
-              const int r = REV ? nv - 1 - s : s;
-              float yy = fmaf(su[r * DT + ech], Dd, ys);
-              if (HAS_Z) yy *= silu_f(sz[r * DT + ech]);
-              ybase[int64_t(tok[r]) * sys] = yy;
-            }
-          }
+          for (int j = 0; j < 4; ++j) h[c][j] = fma2(e[j], h[c][j], mul2(dub, B2[j]));
         }
+        if (STORE_Y) {
+          float2 C2[4];
+          load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const float2 acc =
+                add2(fma2(C2[1], h[c][1], mul2(C2[0], h[c][0])), fma2(C2[3], h[c][3], mul2(C2[2], h[c][2])));
+            k.yp[c] = acc.x + acc.y;
+          }
+          k.r = r;
+        }
+      };
+      auto epilogue = [&](const Carry& k) {
+        const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
+        float yy = fmaf(stg[k.r * DT + own], Down, ys);
+        if (HAS_Z) yy *= silu_f(stg[Cfg::OFF_Z + k.r * DT + own]);
+        stg_if(ybase + int64_t(tok[k.r]) * sys, yy, ev);
+      };
+      Carry ka, kb;
+      math(0, ka);
+#pragma unroll 2
+      for (int s = 1; s < nv; ++s) {
+        math(s, kb);
+        if (STORE_Y) epilogue(ka);
+        ka = kb;
       }
+      if (STORE_Y) epilogue(ka);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (SAVE_CK) {
-      float* dst = ckpt + ((size_t(b) * g.nboxes + i) * g.d_inner + dc) * NS + 4 * gq;
-      if (v0) *reinterpret_cast<float4*>(dst) = make_float4(h[0][0].x, h[0][0].y, h[0][1].x, h[0][1].y);
-      if (v1) *reinterpret_cast<float4*>(dst + NS) = make_float4(h[1][0].x, h[1][0].y, h[1][1].x, h[1][1].y);
+      float* dst = ckpt + ((size_t(b) * g.nboxes + i) * g.d_inner + dc) * NS;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (c ? v1 : v0) {
+#pragma unroll
+          for (int gi = 0; gi < 2; ++gi)
+            *reinterpret_cast<float4*>(dst + c * NS + pl.group_state(gi)) =
+                make_float4(h[c][2 * gi].x, h[c][2 * gi].y, h[c][2 * gi + 1].x, h[c][2 * gi + 1].y);
+        }
+      }
     }
   }
 }
