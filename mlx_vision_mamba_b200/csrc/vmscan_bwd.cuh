@@ -176,7 +176,8 @@ struct FwdCarry {
   int r;
 };
 
-// One box of the VJP (nv rows).
+// One box of the VJP (nv rows).  The loops are kept rolled (pairs of steps):
+// a fully unrolled box overflows the instruction cache and runs slower.
 template <bool HAS_Z, bool REV>
 __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, float* __restrict__ part, uint32_t taddr, int nv, int warp,
                                         int lane, int c0l, const PairLane& pl, bool has_ck, bool v0, bool v1,
@@ -290,6 +291,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
   if (s > 0) tmem_ld16(taddr + 16 * (s - 1), XB);
   bwd_rev_math(L, hs, dAbox, dDbox, XA, stg, row(s), c0l, pl, ka);
   if (s > 0) tmem_wait_ld16(XB);
+#pragma unroll 1
   for (--s; s >= 1; s -= 2) {
     tmem_ld16(taddr + 16 * (s - 1), XA);
     bwd_rev_math(L, hs, dAbox, dDbox, XB, stg, row(s), c0l, pl, kb);

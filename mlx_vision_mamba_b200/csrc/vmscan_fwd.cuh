@@ -27,6 +27,13 @@
 
 namespace vmscan {
 
+// Pairs of state decays per channel and step evaluated on the FMA pipe
+// instead of MUFU (the forward is bound by the exp2 unit).
+#ifndef VMSCAN_FWD_POLY_PAIRS
+#define VMSCAN_FWD_POLY_PAIRS 0
+#endif
+constexpr int kFwdPolyPairs = VMSCAN_FWD_POLY_PAIRS;
+
 template <int NCW>
 struct FwdCfg {
   static constexpr int DT = 32 * NCW;          // channels per CTA (32 per warp, 2 per lane pair)
@@ -74,25 +81,32 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
 
   if (warp == NCW) {
     // ---------------- producer warp ----------------
+    // Per box: lane 0 waits for the stage to drain (sleeping between polls),
+    // lanes < nv write the row -> token table, lane TMAX the row count, then
+    // lane 0 issues the TMA loads.
     if (lane == 0) {
       prefetch_tmap(&tm_u);
       prefetch_tmap(&tm_dt);
       if (LOAD_Z) prefetch_tmap(&tm_z);
       prefetch_tmap(&tm_B);
       if (STORE_Y) prefetch_tmap(&tm_C);
-      const uint32_t bytes = uint32_t(g.T) * uint32_t((LOAD_Z ? 3 : 2) * DT + (STORE_Y ? 2 : 1) * NS) * 4u;
-      for (int i = 0; i < g.nboxes; ++i) {
-        const int st = i % NST;
-        const uint32_t ph = uint32_t(i / NST) & 1u;
-        if (!mbar_wait(&empty[st], ph ^ 1u, abort_flag, status)) break;
-        const int k = REV ? g.nboxes - 1 - i : i;
-        int c[3], nv;
-        box_coords(g, k, c, nv);
-        float* base = sm + st * Cfg::STAGE_F;
-        if (STORE_Y) {
-          int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK);
-          for (int r = 0; r < nv; ++r) tok[r] = int(box_row_token(g, c, r));
-        }
+    }
+    const uint32_t bytes = uint32_t(g.T) * uint32_t((LOAD_Z ? 3 : 2) * DT + (STORE_Y ? 2 : 1) * NS) * 4u;
+    for (int i = 0; i < g.nboxes; ++i) {
+      const int st = i % NST;
+      const uint32_t ph = uint32_t(i / NST) & 1u;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait<true>(&empty[st], ph ^ 1u, abort_flag, status) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      const int k = REV ? g.nboxes - 1 - i : i;
+      int c[3], nv;
+      box_coords(g, k, c, nv);
+      float* base = sm + st * Cfg::STAGE_F;
+      int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK);
+      if (STORE_Y && lane < nv) tok[lane] = int(box_row_token(g, c, lane));
+      if (lane == TMAX) tok[TMAX] = nv;
+      __syncwarp();
+      if (lane == 0) {
         mbar_arrive_expect_tx(&full[st], bytes);
         tma_load_5d(base, &tm_u, &full[st], d0, c[0], c[1], c[2], b);
         tma_load_5d(base + Cfg::TILE, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
@@ -137,17 +151,12 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
   for (int i = 0; i < g.nboxes; ++i) {
     const int st = i % NST;
     const uint32_t ph = uint32_t(i / NST) & 1u;
-    int nv;
-    {
-      const int k = REV ? g.nboxes - 1 - i : i;
-      int c[3];
-      box_coords(g, k, c, nv);
-    }
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles below need the whole warp
     if (alive) {
       const float* __restrict__ stg = sm + st * Cfg::STAGE_F;
       const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
+      const int nv = tok[TMAX];
       auto math = [&](int s, Carry& k) {
         const int r = REV ? nv - 1 - s : s;
         const float2 u2 = lds2(stg + r * DT + c0l);
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float2 e[4];
-          decay8(dlc[c], Ar[c], e);
+          decay8<kFwdPolyPairs>(dlc[c], Ar[c], e);
           const float2 dub = bcast2(duc[c]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) h[c][j] = fma2(e[j], h[c][j], mul2(dub, B2[j]));
