@@ -263,10 +263,15 @@ def main():
     ap.add_argument("--batch", type=int, default=WORKLOAD["batch"], help="per-GPU batch (profiling runs)")
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
+    ap.add_argument("--model-profile", action="store_true",
+                    help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
     WORKLOAD.update(batch=args.batch, seqlen=args.seqlen, d_inner=args.dinner)
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.model_profile:
+        profile_model(args.warmup)
         return
 
     import torch
@@ -427,6 +432,47 @@ def run_model(dev, rank, world, steps, warmup, barrier):
             "dtype": "f32 (TF32 off)", "params": n_params, "loss": float(loss.item()),
             "parallelism": f"DDP NCCL all-reduce x{world}" if world > 1 else "single GPU",
             "config": "img 224x224x1, patch 16, embed 384, depth 6, d_state 16, K=4 directions, MSE vs N(0,1)"}
+
+
+def profile_model(warmup):
+    """Device time per kernel of one VisionMamba-2D training step (1 GPU,
+    torch.profiler over 2 steps after `warmup` steps), grouped as in the
+    committed model-step summary; prints a table, not a bench line."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from mlx_vision_mamba_b200 import train
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    dev = torch.device("cuda", 0)
+    cfg = train.VISION_MAMBA_2D
+    model = train.build_encoder(cfg, dev, seed=0)
+    opt = train.make_optimizer(model)
+    x, tgt = train.synthetic_batch(cfg, cfg.global_batch, dev, seed=100)
+    for _ in range(max(warmup, 1)):
+        train.train_step(model, opt, x, tgt)
+    torch.cuda.synchronize()
+    steps = 2
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            train.train_step(model, opt, x, tgt)
+        torch.cuda.synchronize()
+    rows = sorted(((e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0),
+                  reverse=True)
+    total = sum(r[0] for r in rows)
+    groups = {"gemm": 0.0, "scan_bwd": 0.0, "scan_fwd": 0.0, "conv": 0.0, "vmscan_reduce": 0.0, "other": 0.0}
+    for t_us, _, key in rows:
+        k = ("gemm" if "gemm" in key else "scan_bwd" if "scan_bwd_kernel" in key else
+             "scan_fwd" if "scan_fwd_kernel" in key else "conv" if "vmscan::conv" in key else
+             "vmscan_reduce" if "vmscan::reduce" in key else "other")
+        groups[k] += t_us
+    print(f"total device time per step: {total / steps / 1e3:.2f} ms")
+    for k, v in groups.items():
+        print(f"  {k:14s} {v / steps / 1e3:8.3f} ms  {100 * v / total:5.1f} %")
+    print("top kernels:")
+    for t_us, n, key in rows[:25]:
+        print(f"  {t_us / steps / 1e3:8.3f} ms {100 * t_us / total:5.1f} % x{n // steps:4d} {key[:100]}")
 
 
 def run_e2e(t, dev, K, warmup, world, barrier):
