@@ -338,7 +338,7 @@ def main():
     # ---- end to end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(t, dev, K=max(2, min(K, 4)), warmup=1, world=world, barrier=barrier)
+        e2e = run_e2e(t, dev, K=max(2, min(K, 8)), warmup=2, world=world, barrier=barrier)
     del runner, t
     torch.cuda.empty_cache()
 
@@ -476,38 +476,63 @@ def profile_model(warmup):
 
 
 def run_e2e(t, dev, K, warmup, world, barrier):
-    """Public API (selective_scan_cuda + backward) with pinned host inputs/outputs."""
+    """Public API (selective_scan_cuda + backward) with pinned host inputs and
+    outputs.  Every step copies its own inputs host->device and its output and
+    all gradients device->host inside the timed region; the copies run on
+    their own streams, double-buffered, so step i+1's upload and step i-1's
+    download overlap step i (PCIe is full duplex)."""
     import torch
 
     from mlx_vision_mamba_b200 import selective_scan_cuda
 
     host = {k: v.detach().cpu().pin_memory() for k, v in t.items()}
     b, l, d = t["u"].shape
-    outs = {k: torch.empty(s, dtype=torch.float32).pin_memory() for k, s in (
-        ("y", (b, l, d)), ("du", (b, l, d)), ("ddelta", (b, l, d)), ("dz", (b, l, d)), ("dA", (d, N_STATE)),
-        ("dB", (b, l, N_STATE)), ("dC", (b, l, N_STATE)), ("dD", (d,)))}
+    shapes = (("y", (b, l, d)), ("du", (b, l, d)), ("ddelta", (b, l, d)), ("dz", (b, l, d)), ("dA", (d, N_STATE)),
+              ("dB", (b, l, N_STATE)), ("dC", (b, l, N_STATE)), ("dD", (d,)))
+    outs = [{k: torch.empty(sh, dtype=torch.float32).pin_memory() for k, sh in shapes} for _ in range(2)]
+    din = [{k: torch.empty_like(v, device=dev) for k, v in host.items()} for _ in range(2)]
     h2d = sum(v.numel() * 4 for v in host.values())
-    d2h = sum(v.numel() * 4 for v in outs.values())
+    d2h = sum(v.numel() * 4 for v in outs[0].values())
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    for ev in done:
+        ev.record(comp)
 
-    def step():
-        dv = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
-        leaves = {k: dv[k].requires_grad_(True) for k in ("u", "delta", "A", "B", "C", "D", "z")}
+    def step(i):
+        sl = i & 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(done[sl])  # step i-2 finished reading this input slot
+            for k, v in host.items():
+                din[sl][k].copy_(v, non_blocking=True)
+        comp.wait_stream(s_in)
+        leaves = {}
+        for k in ("u", "delta", "A", "B", "C", "D", "z"):
+            leaves[k] = din[sl][k].detach().requires_grad_(True)
         y = selective_scan_cuda(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"],
                                 leaves["D"], z=leaves["z"])
-        y.backward(dv["dy"])
-        outs["y"].copy_(y.detach(), non_blocking=True)
+        y.backward(din[sl]["dy"])
+        res = {"y": y.detach()}
         for k in ("u", "delta", "z", "A", "B", "C", "D"):
-            outs["d" + k].copy_(leaves[k].grad, non_blocking=True)
+            res["d" + k] = leaves[k].grad
+        done[sl].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done[sl])
+            for k, v in res.items():
+                v.record_stream(s_out)
+                outs[sl][k].copy_(v, non_blocking=True)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(K):
-        step()
-    e1.record()
+    e0.record(comp)
+    s_in.wait_stream(comp)
+    for i in range(K):
+        step(i)
+    comp.wait_stream(s_out)
+    e1.record(comp)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     tm = torch.tensor([ms], device=dev)
@@ -519,7 +544,8 @@ def run_e2e(t, dev, K, warmup, world, barrier):
     byt = fwd_bytes(b, l, d) + bwd_bytes(b, l, d)
     return {"value": world * K * byt / (ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / K, "steps": K,
-            "api": "mlx_vision_mamba_b200.selective_scan_cuda(...).backward(dy), pinned host buffers"}
+            "api": "mlx_vision_mamba_b200.selective_scan_cuda(...).backward(dy), pinned host buffers, "
+                   "uploads / downloads on their own streams (double-buffered, overlapping the previous / next step)"}
 
 
 if __name__ == "__main__":
