@@ -114,20 +114,38 @@ class MambaBlock(nn.Module):
         self.out_proj = Linear(self.d_inner, d_model, bias=False)
 
     def forward(self, x: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
+        return self.out_proj(self.scan_branch(self.in_proj(x), direction))
+
+    def scan_branch(self, xz: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
+        """Everything between in_proj and out_proj (mamba_block.py:166-190): xz is
+        the in_proj output (B, L, 2 d_inner), possibly a strided column slice of a
+        wider projection; returns the gated scan output (B, L, d_inner)."""
         dn, r, n = self.d_inner, self.dt_rank, self.d_state
-        xz = self.in_proj(x)
-        x_branch = xz[:, :, :dn]
-        z = xz[:, :, dn:]
+        # split (not slicing): its backward concatenates the pieces' gradients
+        # instead of materialising a zero-filled full-width gradient per piece
+        x_branch, z = torch.split(xz, [dn, dn], dim=-1)
         x_branch = self.conv1d.silu_along(x_branch, direction)
         x_dbc = self.x_proj(x_branch)
-        dt = x_dbc[:, :, :r]
-        B_proj = x_dbc[:, :, r : r + n]
-        C_proj = x_dbc[:, :, r + n :]
+        dt, B_proj, C_proj = torch.split(x_dbc, [r, n, n], dim=-1)
         delta = self.dt_proj(dt)
         delta = torch.log(1.0 + torch.exp(delta))  # softplus written as in mamba_block.py:181
         A = -torch.exp(self.A_log)
-        y = selective_scan_cuda(x_branch, delta, A, B_proj, C_proj, self.D, z=z, direction=direction)
-        return self.out_proj(y)
+        return selective_scan_cuda(x_branch, delta, A, B_proj, C_proj, self.D, z=z, direction=direction)
+
+
+def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[ScanDirection]], h: torch.Tensor):
+    """sum_k blocks[k](h, directions[k]) with the projections batched over the
+    directions: one in_proj GEMM against the K blocks' concatenated weights
+    (each direction reads its column slice in place) and one out_proj GEMM over
+    the concatenated inner dimension, which performs the sum over directions
+    (the reference adds the K block outputs, mamba_block.py:562-566).  The
+    parameters stay per block, as in the reference."""
+    if len(blocks) == 1:
+        return blocks[0](h, directions[0])
+    two_dn = 2 * blocks[0].d_inner
+    xz = F.linear(h, torch.cat([b.in_proj.weight for b in blocks], 0))
+    ys = [b.scan_branch(part, d) for b, d, part in zip(blocks, directions, torch.split(xz, two_dn, dim=-1))]
+    return F.linear(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
 
 
 class ResidualMambaBlock(nn.Module):
@@ -154,9 +172,7 @@ class BidirectionalMambaBlock(nn.Module):
 
     def forward(self, x):
         h = self.norm(x)
-        y_fwd = self.forward_mamba(h)
-        y_bwd = self.backward_mamba(h, BACKWARD)
-        return x + y_fwd + y_bwd
+        return x + directions_sum([self.forward_mamba, self.backward_mamba], [None, BACKWARD], h)
 
 
 class MultiDirectionalMambaBlock(nn.Module):
@@ -199,10 +215,5 @@ class MultiDirectionalMambaBlock(nn.Module):
         h = self.norm(x)
         expected = math.prod(self.grid_shape) if self.grid_shape is not None else n
         if n != expected and self.num_directions > 2:
-            y_fwd = self.mamba_blocks[0](h)
-            y_bwd = self.mamba_blocks[1](h, BACKWARD)
-            return x + y_fwd + y_bwd
-        y = self.mamba_blocks[0](h, self.directions[0])
-        for k in range(1, self.num_directions):
-            y = y + self.mamba_blocks[k](h, self.directions[k])
-        return x + y
+            return x + directions_sum(self.mamba_blocks[:2], [None, BACKWARD], h)
+        return x + directions_sum(self.mamba_blocks, self.directions, h)

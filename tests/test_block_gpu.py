@@ -84,3 +84,39 @@ def test_vision_mamba_training_step_updates_parameters():
     assert losses[-1] < losses[0]
     changed = sum(not torch.equal(before[k], p.detach()) for k, p in model.named_parameters())
     assert changed == len(before)
+
+
+def test_batched_direction_projections_match_per_block_sum():
+    """One in_proj / out_proj GEMM over the K directions equals the reference's
+    per-block computation summed over directions (mamba_block.py:562-566)."""
+    import mlx_vision_mamba_b200 as vm
+    from mlx_vision_mamba_b200.mamba_block import directions_sum
+
+    torch.manual_seed(0)
+    blk = vm.MultiDirectionalMambaBlock(64, 16, 4, 2, num_directions=4, grid_shape=(14, 14)).cuda()
+    h = torch.randn(2, 196, 64, device="cuda")
+    w = torch.randn(2, 196, 64, device="cuda")
+
+    def run(fn):
+        blk.zero_grad(set_to_none=True)
+        hh = h.clone().requires_grad_(True)
+        out = fn(hh)
+        (out * w).sum().backward()
+        return out.detach(), hh.grad.detach(), {k: p.grad.detach().clone() for k, p in blk.named_parameters()
+                                                if p.grad is not None}
+
+    blocks, dirs = list(blk.mamba_blocks), blk.directions
+    y1, dh1, g1 = run(lambda hh: directions_sum(blocks, dirs, hh))
+
+    def per_block(hh):
+        y = blocks[0](hh, dirs[0])
+        for k in range(1, 4):
+            y = y + blocks[k](hh, dirs[k])
+        return y
+
+    y2, dh2, g2 = run(per_block)
+    torch.testing.assert_close(y1, y2, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(dh1, dh2, rtol=1e-5, atol=1e-5)
+    assert g1.keys() == g2.keys()
+    for k in g1:
+        torch.testing.assert_close(g1[k], g2[k], rtol=1e-4, atol=1e-5, msg=k)
