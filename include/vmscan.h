@@ -233,6 +233,34 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
                            vmscan_stream_t stream);
 
 /*
+ * dt_proj + bias + softplus producing the scan's delta
+ * (mamba_block.py:177-181: `delta = log(1 + exp(dt_proj(x_dbc[..., :dt_rank])))`):
+ *   delta[t, d] = log(1 + exp(bias[d] + sum_r x[t, r] * weight[d, r]))
+ * for ntok tokens t (rows of x every ldx floats, rows of delta every
+ * ld_delta floats) and d < d_inner; weight is nn.Linear's (d_inner, dt_rank)
+ * row-major matrix.  dt_rank in 1..64.
+ */
+int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
+                           const float* x, int64_t ldx,
+                           const float* weight, const float* bias,
+                           float* delta, int64_t ld_delta,
+                           vmscan_stream_t stream);
+
+/*
+ * Softplus part of the VJP of vmscan_dt_softplus_fwd: dpre = ddelta *
+ * sigmoid(pre) with pre recomputed from x, weight, bias (the gradient the
+ * reference's autograd forms through log(1 + exp(.))).  dx = dpre weight,
+ * dweight = dpre^T x and dbias = column sums of dpre are left to the caller
+ * (plain GEMMs).
+ */
+int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
+                           const float* x, int64_t ldx,
+                           const float* weight, const float* bias,
+                           const float* ddelta, int64_t ld_ddelta,
+                           float* dpre, int64_t ld_dpre,
+                           vmscan_stream_t stream);
+
+/*
  * Host-only introspection (no CUDA call): writes the token index visited at
  * every scan step of `dir` into tokens[0..seqlen), computed the way the
  * kernels compute it.  mode 0 enumerates the TMA boxes (box coordinates +

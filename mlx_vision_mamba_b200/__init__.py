@@ -15,6 +15,7 @@ from .mamba_block import (
 from .scan import (
     conv1d_silu_cuda,
     device_status,
+    dt_softplus_cuda,
     selective_scan,
     selective_scan_cuda,
     selective_scan_metal,
@@ -38,6 +39,7 @@ __all__ = [
     "BACKWARD",
     "directions_for",
     "selective_scan",
+    "dt_softplus_cuda",
     "selective_scan_cuda",
     "selective_scan_metal",
     "selective_scan_metal_trainable",

@@ -16,6 +16,7 @@
 #include "vmscan_bwd.cuh"
 #include "vmscan_common.cuh"
 #include "vmscan_conv.cuh"
+#include "vmscan_dt.cuh"
 #include "vmscan_fwd.cuh"
 
 using namespace vmscan;
@@ -337,6 +338,45 @@ int check_common(int64_t d_state, const float* A, const float* D) {
 
 }  // namespace
 
+namespace {
+
+template <bool BWD>
+int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
+                       const float* weight, const float* bias, const float* gin, int64_t ldg, float* out,
+                       int64_t ldo, vmscan_stream_t stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr || (BWD && gin == nullptr))
+    return VMSCAN_ERR_NULL;
+  if (ntok <= 0 || d_inner <= 0 || d_inner > INT32_MAX || dt_rank < 1 || dt_rank > DTP_RMAX)
+    return fail(VMSCAN_ERR_SHAPE, "dt_softplus: ntok %lld, dt_rank %lld (1..%d), d_inner %lld",
+                (long long)ntok, (long long)dt_rank, DTP_RMAX, (long long)d_inner);
+  if (ldx < dt_rank || ldo < d_inner || (BWD && ldg < d_inner))
+    return fail(VMSCAN_ERR_SHAPE, "dt_softplus: row strides shorter than the rows");
+  if ((ntok + DTP_TOKENS - 1) / DTP_TOKENS > 65535)
+    return fail(VMSCAN_ERR_SHAPE, "dt_softplus: %lld tokens exceed the launch grid", (long long)ntok);
+  VM_TRY(ensure_context(x));
+  const dim3 grid(unsigned((d_inner + DTP_THREADS - 1) / DTP_THREADS), unsigned((ntok + DTP_TOKENS - 1) / DTP_TOKENS));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int R = int(dt_rank), D = int(d_inner);
+#define VM_DTP(RP)                                                                                           \
+  dt_softplus_kernel<RP, BWD><<<grid, DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, ntok, D)
+  if (R <= 8)
+    VM_DTP(8);
+  else if (R <= 16)
+    VM_DTP(16);
+  else if (R <= 24)
+    VM_DTP(24);
+  else if (R <= 32)
+    VM_DTP(32);
+  else if (R <= 48)
+    VM_DTP(48);
+  else
+    VM_DTP(64);
+#undef VM_DTP
+  return check_launch();
+}
+
+}  // namespace
+
 extern "C" {
 
 int vmscan_version(void) { return 100; }
@@ -471,6 +511,20 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
   const int nA = int(d_inner * NS);
   reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch), int(d_inner));
   return check_launch();
+}
+
+int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
+                           const float* weight, const float* bias, float* delta, int64_t ld_delta,
+                           vmscan_stream_t stream) {
+  return launch_dt_softplus<false>(ntok, dt_rank, d_inner, x, ldx, weight, bias, nullptr, 0, delta, ld_delta,
+                                   stream);
+}
+
+int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
+                           const float* weight, const float* bias, const float* ddelta, int64_t ld_ddelta,
+                           float* dpre, int64_t ld_dpre, vmscan_stream_t stream) {
+  return launch_dt_softplus<true>(ntok, dt_rank, d_inner, x, ldx, weight, bias, ddelta, ld_ddelta, dpre, ld_dpre,
+                                  stream);
 }
 
 int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,

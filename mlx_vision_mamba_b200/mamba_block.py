@@ -26,7 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .direction import BACKWARD, ScanDirection, directions_for
-from .scan import conv1d_silu_cuda, selective_scan_cuda
+from .scan import conv1d_silu_cuda, dt_softplus_cuda, selective_scan_cuda
 
 GPU_SCAN_MODES = ("cuda_fused", "metal_fused", "metal_train", "metal")
 CPU_SCAN_MODES = ("sequential", "chunked", "parallel")
@@ -127,8 +127,8 @@ class MambaBlock(nn.Module):
         x_branch = self.conv1d.silu_along(x_branch, direction)
         x_dbc = self.x_proj(x_branch)
         dt, B_proj, C_proj = torch.split(x_dbc, [r, n, n], dim=-1)
-        delta = self.dt_proj(dt)
-        delta = torch.log(1.0 + torch.exp(delta))  # softplus written as in mamba_block.py:181
+        # dt_proj + bias + softplus (log(1 + exp(.)), mamba_block.py:180-181) in one kernel
+        delta = dt_softplus_cuda(dt, self.dt_proj.weight, self.dt_proj.bias)
         A = -torch.exp(self.A_log)
         return selective_scan_cuda(x_branch, delta, A, B_proj, C_proj, self.D, z=z, direction=direction)
 

@@ -279,6 +279,67 @@ def conv1d_silu_cuda(
     return _ConvSiluFn.apply(x, weight, bias, direction)
 
 
+def _token_rows(t: torch.Tensor) -> torch.Tensor:
+    """t (B, L, C) as ntok = B*L rows of C floats with one row stride (a view
+    when the layout allows it, else a contiguous copy)."""
+    if t.dtype != torch.float32:
+        t = t.float()
+    b, l, c = t.shape
+    if t.stride(2) == 1 and t.stride(1) >= c and (b == 1 or t.stride(0) == l * t.stride(1)):
+        return t
+    return t.contiguous()
+
+
+class _DtSoftplusFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        lib = _native.load()
+        b, l, r = x.shape
+        dn = weight.shape[0]
+        x_ = _token_rows(x)
+        w_ = weight.detach().float().contiguous()
+        b_ = bias.detach().float().contiguous()
+        delta = _empty_seq(b, l, dn, x.device)
+        st = lib.vmscan_dt_softplus_fwd(b * l, r, dn, _ptr(x_), x_.stride(1), _ptr(w_), _ptr(b_), _ptr(delta),
+                                        delta.stride(1), _stream(x))
+        _native.check(st, "vmscan_dt_softplus_fwd")
+        ctx.save_for_backward(x_, w_, b_)
+        return delta
+
+    @staticmethod
+    def backward(ctx, ddelta):
+        lib = _native.load()
+        x_, w_, b_ = ctx.saved_tensors
+        b, l, r = x_.shape
+        dn = w_.shape[0]
+        g_in = _token_rows(ddelta)
+        dpre = _empty_seq(b, l, dn, x_.device)
+        st = lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(x_), x_.stride(1), _ptr(w_), _ptr(b_), _ptr(g_in),
+                                        g_in.stride(1), _ptr(dpre), dpre.stride(1), _stream(x_))
+        _native.check(st, "vmscan_dt_softplus_bwd")
+        g2 = dpre.reshape(b * l, dn)
+        dx = (g2 @ w_).reshape(b, l, r)
+        dw = g2.t() @ x_.reshape(b * l, r)
+        db = g2.sum(0)
+        return dx, dw, db
+
+
+def dt_softplus_cuda(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """delta = log(1 + exp(x @ weight.T + bias)) in one kernel (the reference's
+    `dt_proj` followed by its softplus, mlx_vision_mamba/mamba_block.py:180-181).
+
+    x: (B, L, dt_rank) CUDA fp32 (the dt columns of x_dbc, a strided view is
+    fine); weight: (d_inner, dt_rank) and bias: (d_inner,) of nn.Linear.
+    Returns (B, L, d_inner).  The backward forms dpre = ddelta * sigmoid(pre)
+    in a kernel and leaves dx, dweight, dbias to cuBLAS GEMMs / a reduction.
+    """
+    if not (x.is_cuda and weight.is_cuda and bias.is_cuda):
+        raise RuntimeError("dt_softplus_cuda: inputs must be CUDA tensors (there is no CPU path)")
+    if x.dim() != 3 or weight.dim() != 2 or weight.shape[1] != x.shape[2] or bias.shape != (weight.shape[0],):
+        raise ValueError(f"bad shapes x={tuple(x.shape)} weight={tuple(weight.shape)} bias={tuple(bias.shape)}")
+    return _DtSoftplusFn.apply(x, weight, bias)
+
+
 def device_status(device: Optional[torch.device] = None, clear: bool = True) -> int:
     """Synchronise the current stream and return the sticky device status (0 = ok)."""
     lib = _native.load()
