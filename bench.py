@@ -263,6 +263,7 @@ def main():
     ap.add_argument("--batch", type=int, default=WORKLOAD["batch"], help="per-GPU batch (profiling runs)")
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
+    ap.add_argument("--model-eager", action="store_true", help="run the model steps eagerly (no CUDA graph)")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
@@ -285,6 +286,9 @@ def main():
     if world > 1:
         from datetime import timedelta
 
+        # collectives captured in a CUDA graph (the model step) cannot be polled
+        # by NCCL's asynchronous error watchdog
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     args.warmup = max(args.warmup, 3)
 
@@ -345,7 +349,8 @@ def main():
     # ---- VisionMamba-2D training throughput (second half of the metric) ----
     model_line = None
     if not args.no_model:
-        model_line = run_model(dev, rank, world, steps=max(3, min(K, 10)), warmup=3, barrier=barrier)
+        model_line = run_model(dev, rank, world, steps=max(3, min(K, 10)), warmup=3, barrier=barrier,
+                               graphed=not args.model_eager)
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -393,10 +398,11 @@ def main():
         dist.destroy_process_group()
 
 
-def run_model(dev, rank, world, steps, warmup, barrier):
+def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
     """VisionMamba-2D (K=4, 224x224x1, patch 16, E 384, depth 6) training steps:
     forward, MSE, backward (DDP all-reduce over NCCL when world > 1), AdamW.
-    Global batch 64 split over the ranks (strong scaling), fp32 (TF32 off)."""
+    Global batch 64 split over the ranks (strong scaling), fp32 (TF32 off).
+    `graphed`: the whole step is one CUDA graph replay (train.GraphedTrainStep)."""
     import torch
     import torch.distributed as dist
 
@@ -406,19 +412,34 @@ def run_model(dev, rank, world, steps, warmup, barrier):
     torch.backends.cudnn.allow_tf32 = False
     cfg = train.VISION_MAMBA_2D
     a, b = train.shard(cfg.global_batch, rank, world)
-    model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
-    opt = train.make_optimizer(model)
+    side = torch.cuda.Stream(dev)
+    if graphed:
+        with torch.cuda.stream(side):  # DDP is constructed on the capture's side stream
+            model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+        torch.cuda.current_stream(dev).wait_stream(side)
+    else:
+        model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+    opt = train.make_optimizer(model, capturable=graphed)
     x, tgt = train.synthetic_batch(cfg, b - a, dev, seed=100 + rank)
+    if graphed:
+        gstep = train.GraphedTrainStep(model, opt, x, tgt, side_stream=side)
+        step = lambda: gstep()  # noqa: E731
+    else:
+        gstep = None
+        step = lambda: train.train_step(model, opt, x, tgt)  # noqa: E731
     for _ in range(warmup):
-        train.train_step(model, opt, x, tgt)
+        step()
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        loss = train.train_step(model, opt, x, tgt)
+        loss = step()
     e1.record()
     torch.cuda.synchronize()
+    loss = float(loss.item())
+    if gstep is not None:
+        gstep.close()
     ms = e0.elapsed_time(e1)
     tm = torch.tensor([ms], device=dev)
     if world > 1:
@@ -429,7 +450,8 @@ def run_model(dev, rank, world, steps, warmup, barrier):
     torch.cuda.empty_cache()
     return {"img_per_s": cfg.global_batch * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
             "warmup": warmup, "global_batch": cfg.global_batch, "per_gpu_batch": b - a, "scaling": "strong",
-            "dtype": "f32 (TF32 off)", "params": n_params, "loss": float(loss.item()),
+            "dtype": "f32 (TF32 off)", "params": n_params, "loss": loss,
+            "execution": "one CUDA graph per step (forward, backward, all-reduce, AdamW)" if graphed else "eager",
             "parallelism": f"DDP NCCL all-reduce x{world}" if world > 1 else "single GPU",
             "config": "img 224x224x1, patch 16, embed 384, depth 6, d_state 16, K=4 directions, MSE vs N(0,1)"}
 

@@ -144,8 +144,41 @@ def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[S
         return blocks[0](h, directions[0])
     two_dn = 2 * blocks[0].d_inner
     xz = F.linear(h, torch.cat([b.in_proj.weight for b in blocks], 0))
-    ys = [b.scan_branch(part, d) for b, d, part in zip(blocks, directions, torch.split(xz, two_dn, dim=-1))]
+    parts = torch.split(xz, two_dn, dim=-1)
+    if h.is_cuda:
+        ys = _branches_on_streams(blocks, directions, parts)
+    else:
+        ys = [b.scan_branch(part, d) for b, d, part in zip(blocks, directions, parts)]
     return F.linear(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
+
+
+_STREAMS = {}
+
+
+def _branch_streams(device: torch.device, k: int):
+    key = (device.index, k)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(device=device) for _ in range(k)]
+    return _STREAMS[key]
+
+
+def _branches_on_streams(blocks, directions, parts):
+    """Run the K independent direction branches (conv, x_proj, dt_proj, scan)
+    concurrently, one CUDA stream each, so that small per-GPU batches still fill
+    the GPU (a branch of batch 8 launches only a few dozen CTAs per kernel).
+    Autograd runs each branch's backward on the same stream; under CUDA graph
+    capture the streams become parallel branches of the graph."""
+    cur = torch.cuda.current_stream(parts[0].device)
+    streams = _branch_streams(parts[0].device, len(blocks))
+    ys = []
+    for b, d, part, s in zip(blocks, directions, parts, streams):
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            ys.append(b.scan_branch(part, d))
+    for y, s in zip(ys, streams):
+        cur.wait_stream(s)
+        y.record_stream(cur)
+    return ys
 
 
 class ResidualMambaBlock(nn.Module):

@@ -98,5 +98,51 @@ def train_step(model, optimizer, x, target) -> torch.Tensor:
     return loss.detach()
 
 
-def make_optimizer(model, lr: float = 1e-4):
-    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=0.05)
+def make_optimizer(model, lr: float = 1e-4, capturable: bool = False):
+    """AdamW; `capturable` keeps its step counters on the device so the
+    update can be replayed inside a CUDA graph."""
+    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=0.05, capturable=capturable)
+
+
+class GraphedTrainStep:
+    """The whole training step (forward, MSE, backward with DDP's gradient
+    all-reduce, AdamW update) captured once into a CUDA graph and replayed:
+    one graph launch per step instead of hundreds of kernel launches and the
+    Python autograd work around them, so small per-GPU batches stay GPU-bound.
+
+    Inputs are copied into static buffers before each replay.  The model must
+    be wrapped by `wrap_data_parallel` inside `side_stream` (DDP's documented
+    requirement for capture) and the optimizer built with `capturable=True`.
+    `warmup` eager steps run on the side stream first (DDP needs at least 11
+    before its buckets are final).  Release the step (`close()`) before
+    destroying a process group whose collectives it captured.
+    """
+
+    def __init__(self, model, optimizer, x, target, side_stream=None, warmup: int = 11):
+        self.model, self.optimizer = model, optimizer
+        self.x = x.detach().clone()
+        self.target = target.detach().clone()
+        stream = side_stream if side_stream is not None else torch.cuda.Stream(device=x.device)
+        stream.wait_stream(torch.cuda.current_stream(x.device))
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                train_step(model, optimizer, self.x, self.target)
+        torch.cuda.current_stream(x.device).wait_stream(stream)
+        optimizer.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            out = model(self.x)
+            self.loss = F.mse_loss(out, self.target)
+            self.loss.backward()
+            optimizer.step()
+
+    def __call__(self, x=None, target=None) -> torch.Tensor:
+        if x is not None:
+            self.x.copy_(x, non_blocking=True)
+        if target is not None:
+            self.target.copy_(target, non_blocking=True)
+        self.graph.replay()
+        return self.loss
+
+    def close(self) -> None:
+        self.graph = None

@@ -120,3 +120,26 @@ def test_batched_direction_projections_match_per_block_sum():
     assert g1.keys() == g2.keys()
     for k in g1:
         torch.testing.assert_close(g1[k], g2[k], rtol=1e-4, atol=1e-5, msg=k)
+
+
+def test_graphed_training_step_matches_eager():
+    """The CUDA-graph captured step replays the same computation as the eager
+    step: same losses and parameters after the same number of updates."""
+    from mlx_vision_mamba_b200 import train
+
+    cfg = train.EncoderConfig("tiny 2D", (32, 32, 1), 32, 8, embed_dim=32, depth=2, input_dim=2, global_batch=4)
+    dev = torch.device("cuda", 0)
+    x, tgt = train.synthetic_batch(cfg, 4, dev, seed=0)
+
+    eager = train.build_encoder(cfg, dev, seed=1)
+    opt_e = train.make_optimizer(eager, lr=1e-3, capturable=True)
+    losses_e = [train.train_step(eager, opt_e, x, tgt).item() for _ in range(14)]
+
+    graphed = train.build_encoder(cfg, dev, seed=1)
+    opt_g = train.make_optimizer(graphed, lr=1e-3, capturable=True)
+    step = train.GraphedTrainStep(graphed, opt_g, x, tgt, warmup=11)
+    losses_g = [step().item() for _ in range(3)]
+    step.close()
+    torch.testing.assert_close(torch.tensor(losses_g), torch.tensor(losses_e[11:]), rtol=1e-5, atol=1e-6)
+    for (k, p), q in zip(eager.named_parameters(), graphed.parameters()):
+        torch.testing.assert_close(q.detach(), p.detach(), rtol=1e-5, atol=1e-6, msg=k)
