@@ -264,6 +264,8 @@ def main():
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
     ap.add_argument("--model-eager", action="store_true", help="run the model steps eagerly (no CUDA graph)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time forward and VJP separately on the 12 op-sweep points and print a table")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
@@ -273,6 +275,9 @@ def main():
         return
     if args.model_profile:
         profile_model(args.warmup)
+        return
+    if args.sweep:
+        run_sweep(max(args.steps, 20), max(args.warmup, 3))
         return
 
     import torch
@@ -454,6 +459,63 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
             "execution": "one CUDA graph per step (forward, backward, all-reduce, AdamW)" if graphed else "eager",
             "parallelism": f"DDP NCCL all-reduce x{world}" if world > 1 else "single GPU",
             "config": "img 224x224x1, patch 16, embed 384, depth 6, d_state 16, K=4 directions, MSE vs N(0,1)"}
+
+
+SWEEP = [(b, l, d) for b in (8, 64) for l in (196, 1024, 4096) for d in (768, 1536)]
+
+
+def run_sweep(iters, warmup):
+    """The op sweep (batch x L x d_inner = {8, 64} x {196, 1024, 4096} x {768,
+    1536}, gated, seeded inputs with the sweep's distributions): forward and
+    VJP through the C ABI timed separately with CUDA events, median of `iters`
+    launches after `warmup`; a 256 MB buffer is overwritten before every timed
+    launch whose inputs fit in L2, so no point is timed from a warm cache.
+    Prints one JSON line per point and a table."""
+    import statistics
+
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream_t = torch.cuda.current_stream(dev)
+    stream = ctypes.c_void_p(stream_t.cuda_stream)
+    peak, peak_kind = measured_peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    rows = []
+    for b, l, d in SWEEP:
+        t = make_inputs(b, l, d, dev, seed=7)
+        runner = AbiScan(t)
+        in_bytes = 4 * 4 * b * l * d
+        need_flush = in_bytes < 2 * 126 * 1024 * 1024
+        res = {}
+        for name, fn in (("fwd", runner.fwd), ("bwd", runner.bwd)):
+            for _ in range(warmup):
+                fn(stream)
+            times = []
+            for _ in range(iters):
+                if need_flush:
+                    flush.fill_(1.0)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream_t)
+                fn(stream)
+                e1.record(stream_t)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1))
+            res[name] = statistics.median(times)
+        fb, bb = fwd_bytes(b, l, d), bwd_bytes(b, l, d)
+        row = {"batch": b, "seqlen": l, "d_inner": d, "fwd_ms": res["fwd"], "bwd_ms": res["bwd"],
+               "fwd_gbs": fb / res["fwd"] / 1e6, "bwd_gbs": bb / res["bwd"] / 1e6,
+               "fwd_frac": fb / res["fwd"] / 1e6 / peak, "bwd_frac": bb / res["bwd"] / 1e6 / peak,
+               "l2_flush": need_flush, "peak": peak, "peak_source": peak_kind}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del runner, t
+        torch.cuda.empty_cache()
+    print("| batch | L | d_inner | fwd ms | fwd GB/s | fwd % peak | VJP ms | VJP GB/s | VJP % peak |")
+    print("|---:|---:|---:|---:|---:|---:|---:|---:|---:|")
+    for r in rows:
+        print(f"| {r['batch']} | {r['seqlen']} | {r['d_inner']} | {r['fwd_ms']:.4f} | {r['fwd_gbs']:.0f} | "
+              f"{100 * r['fwd_frac']:.1f} | {r['bwd_ms']:.4f} | {r['bwd_gbs']:.0f} | {100 * r['bwd_frac']:.1f} |")
 
 
 def profile_model(warmup):
