@@ -159,6 +159,9 @@ class AbiScan:
         self.g["dB"] = torch.empty(b, l, N_STATE, device=dev)
         self.g["dC"] = torch.empty(b, l, N_STATE, device=dev)
         self.g["dD"] = torch.empty(d, device=dev)
+        self.fws_n = lib.vmscan_fwd_workspace_bytes(b, l, d, N_STATE, None)
+        self.fws = torch.empty(max(self.fws_n, 16), dtype=torch.uint8, device=dev)
+        self.fws_ptr = self.fws.data_ptr() if self.fws_n > 0 else None
         self.ws_n = lib.vmscan_bwd_workspace_bytes(b, l, d, N_STATE, None, 0)
         self.ws = torch.empty(self.ws_n, dtype=torch.uint8, device=dev)
 
@@ -173,7 +176,7 @@ class AbiScan:
         st = self.lib.vmscan_fwd(b, l, d, N_STATE, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(),
                                  S(t["delta"]), t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(),
                                  S(t["C"]), t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), self.y.data_ptr(),
-                                 S(self.y), self.ck.data_ptr(), None, stream)
+                                 S(self.y), self.ck.data_ptr(), None, self.fws_ptr, self.fws_n, stream)
         if st:
             raise RuntimeError(f"vmscan_fwd: {self.lib.vmscan_strerror(st).decode()}")
 

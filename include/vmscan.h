@@ -100,10 +100,20 @@ int64_t vmscan_ckpt_elems(int64_t batch, int64_t seqlen, int64_t d_inner,
                           int64_t d_state, const vmscan_direction* dir);
 
 /*
+ * Workspace of vmscan_fwd: the chunk carries of a scan chunked over L (used
+ * when batch x channel tiles would leave most SMs idle); 0 when the scan is
+ * not chunked.  Negative on a bad argument.
+ */
+int64_t vmscan_fwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner,
+                                   int64_t d_state, const vmscan_direction* dir);
+
+/*
  * Fused forward: y = (selective_scan(u, delta, A, B, C, D)) * silu(z).
  * z == NULL drops the gate (plain reference `selective_scan` output).
  * ckpt == NULL skips the checkpoints (inference); otherwise ckpt must hold
- * vmscan_ckpt_elems(...) floats.
+ * vmscan_ckpt_elems(...) floats.  workspace (16-byte aligned) of at least
+ * vmscan_fwd_workspace_bytes(...) enables the chunked scan over L; NULL (or
+ * too small) runs every sequence in one piece (same results up to rounding).
  * Replaces mamba_metal_fused.py:148-179 (+ the gate at mamba_block.py:190).
  */
 int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
@@ -117,6 +127,7 @@ int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
                float* y, vmscan_strides sy,
                float* ckpt,
                const vmscan_direction* dir,
+               void* workspace, size_t workspace_bytes,
                vmscan_stream_t stream);
 
 /*

@@ -47,9 +47,10 @@ SIGNATURES = {
     "vmscan_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vmscan_last_error": (ctypes.c_char_p, []),
     "vmscan_ckpt_elems": (_i64, [_i64, _i64, _i64, _i64, _D]),
+    "vmscan_fwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _D]),
     "vmscan_fwd": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _D, _p],
+        [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _D, _p, _sz, _p],
     ),
     "vmscan_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _D, ctypes.c_int]),
     "vmscan_bwd": (

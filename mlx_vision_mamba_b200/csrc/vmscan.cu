@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/vmscan.h"
@@ -252,44 +253,135 @@ int check_launch() {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct BwdWorkspace {
-  size_t part, wA, wD, ck, total;
+  int nc, bpc;  // chunks over L and boxes per chunk
+  size_t part, wA, wD, p_local, carry_s, p_in, ck, fws, total;
 };
 
+int sm_count();
+int scan_chunks(int64_t ctas, int64_t slots, int nboxes, int min_boxes);
+size_t fwd_chunk_bytes(const ScanGeom& g);
+
+// VJP workspace: dB/dC partials per (batch, box, channel tile); dA/dD
+// partials per (batch, chunk); the adjoint carries of a chunked VJP; and,
+// when the VJP rebuilds the checkpoints, their buffer and the forward's
+// chunk carries.
 BwdWorkspace bwd_layout(const ScanGeom& g, int ndt, bool with_ck) {
   BwdWorkspace w;
+  w.nc = scan_chunks(int64_t(g.batch) * ndt, int64_t(sm_count()) * 2, g.nboxes, 2);
+  w.bpc = (g.nboxes + w.nc - 1) / w.nc;
+  const size_t rows = size_t(g.batch) * w.nc * g.d_inner;
   w.part = 0;
   const size_t part_bytes = size_t(g.batch) * g.nboxes * ndt * TMAX * kPartRow * 4;
   w.wA = align256(w.part + part_bytes);
-  w.wD = align256(w.wA + size_t(g.batch) * g.d_inner * NS * 4);
-  w.ck = align256(w.wD + size_t(g.batch) * g.d_inner * 4);
+  w.wD = align256(w.wA + rows * NS * 4);
+  w.p_local = align256(w.wD + rows * 4);
+  const size_t carry = w.nc > 1 ? rows * NS * 4 : 0;
+  w.carry_s = align256(w.p_local + carry);
+  w.p_in = align256(w.carry_s + (w.nc > 1 ? rows * 4 : 0));
+  w.ck = align256(w.p_in + carry);
   const size_t ck_bytes = with_ck ? size_t(g.batch) * g.nboxes * g.d_inner * NS * 4 : 0;
-  w.total = align256(w.ck + ck_bytes);
+  w.fws = align256(w.ck + ck_bytes);
+  w.total = align256(w.fws + (with_ck ? fwd_chunk_bytes(g) : 0));
   return w;
 }
 
-template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
+// SMs of the current device (cached per device).
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    cache[dev] = (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) ? n : 148;
+  }
+  return cache[dev];
+}
+
+// Number of chunks over L for a scan whose unchunked grid has `ctas` CTAs
+// when `slots` CTAs fit on the GPU at once: 1 while the grid fills at least
+// half the slots (chunking costs an extra pass), otherwise enough chunks to
+// fill them, each chunk at least `min_boxes` boxes, at most 32 chunks.
+int scan_chunks(int64_t ctas, int64_t slots, int nboxes, int min_boxes) {
+  if (ctas * 2 >= slots) return 1;
+  int nc = int(std::min<int64_t>(slots / ctas, 32));
+  nc = std::min(nc, nboxes / min_boxes);
+  if (nc < 2) return 1;
+  const int bpc = (nboxes + nc - 1) / nc;
+  return (nboxes + bpc - 1) / bpc;
+}
+
+struct ChunkPlan {
+  int nc, bpc;
+  size_t bytes;  // workspace for the carries (0 when nc == 1)
+};
+
+ChunkPlan fwd_chunk_plan(const ScanGeom& g) {
+  using Cfg = FwdCfg<kFwdNCW>;
+  const int64_t tiles = (g.d_inner + Cfg::DT - 1) / Cfg::DT;
+  // the forward's carry pass and extra launches cost more than they save on
+  // chunks shorter than 8 boxes (measured at L = 196)
+  const int nc = scan_chunks(int64_t(g.batch) * tiles, int64_t(sm_count()) * 4, g.nboxes, 8);
+  const size_t per = size_t(g.batch) * nc * g.d_inner;
+  return {nc, (g.nboxes + nc - 1) / nc, nc > 1 ? 2 * align256(per * NS * 4) + align256(per * 4) : 0};
+}
+
+size_t fwd_chunk_bytes(const ScanGeom& g) { return fwd_chunk_plan(g).bytes; }
+
+template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY>
 int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
                  const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
-                 const ScanGeom& g, cudaStream_t stream) {
+                 const ChunkArgs& ch, int nz, const ScanGeom& g, cudaStream_t stream) {
   using Cfg = FwdCfg<kFwdNCW>;
-  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y, REV>;
+  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_fwd_kernel) failed");
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
   int sys = 0;
   if (STORE_Y) VM_TRY(seq_stride32("y", sy, g.seqlen, sys));
-  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sys, A, D, ckpt, g, st);
+  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch), unsigned(nz));
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sys, A, D, ckpt, ch, g, st);
   return check_launch();
+}
+
+// Forward scan, chunked over L when the grid would leave most of the GPU idle
+// and `ws` (fwd_chunk_plan(g).bytes) is given: a carry pass over chunks
+// 0 .. nc-2, the carry chain, then the main pass over all chunks.
+template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
+int run_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
+              const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
+              void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
+  const ChunkPlan plan = fwd_chunk_plan(g);
+  if (plan.nc == 1 || ws == nullptr || ws_bytes < plan.bytes) {
+    const ChunkArgs one{g.nboxes, 1, nullptr, nullptr, nullptr};
+    return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, one, 1, g,
+                                                             stream);
+  }
+  const size_t per = size_t(g.batch) * plan.nc * g.d_inner;
+  char* w = static_cast<char*>(ws);
+  float* carry_h = reinterpret_cast<float*>(w);
+  float* h_start = reinterpret_cast<float*>(w + align256(per * NS * 4));
+  float* carry_s = reinterpret_cast<float*>(w + 2 * align256(per * NS * 4));
+  const ChunkArgs ch{plan.bpc, plan.nc, h_start, carry_h, carry_s};
+  VM_TRY((launch_fwd_t<false, false, false, REV, true>(mu, mdt, mz, mB, mC, nullptr, vmscan_strides{0, 0}, A, D,
+                                                      nullptr, ch, plan.nc - 1, g, stream)));
+  const int64_t n = int64_t(g.batch) * g.d_inner * NS;
+  carry_fwd_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(A, carry_h, carry_s, h_start, g.batch, plan.nc,
+                                                                  g.d_inner);
+  VM_TRY(check_launch());
+  return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ch, plan.nc, g,
+                                                           stream);
 }
 
 template <bool HAS_Z, bool SAVE_CK, bool STORE_Y>
 int launch_fwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
                const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
-               const ScanGeom& g, cudaStream_t stream) {
-  if (g.reverse) return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, stream);
-  return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, stream);
+               void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
+  if (g.reverse)
+    return run_fwd_t<HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g, stream);
+  return run_fwd_t<HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g, stream);
 }
 
 struct BwdOut {
@@ -304,30 +396,53 @@ struct BwdOut {
 template <bool HAS_Z, bool REV>
 int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
                  const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
-                 const float* ckpt, float* wpart, float* wA, float* wD, const ScanGeom& g, cudaStream_t stream) {
+                 const float* ckpt, float* wpart, float* wA, float* wD, const BwdWorkspace& wl, char* ws,
+                 const ScanGeom& g, cudaStream_t stream) {
   using Cfg = BwdCfg;
+  int* st = status_ptr();
+  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  const unsigned ndt = unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT);
+  float* p_in = nullptr;
+  if (wl.nc > 1) {
+    // adjoint carries of the chunks, then their chain
+    using CC = BwdCarryCfg;
+    auto ck = scan_bwd_carry_kernel<HAS_Z, REV>;
+    if (cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, int(CC::SMEM_BYTES)) != cudaSuccess)
+      return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_carry_kernel) failed");
+    float* p_local = reinterpret_cast<float*>(ws + wl.p_local);
+    float* carry_s = reinterpret_cast<float*>(ws + wl.carry_s);
+    p_in = reinterpret_cast<float*>(ws + wl.p_in);
+    ck<<<dim3(ndt, unsigned(g.batch), unsigned(wl.nc - 1)), CC::NT, CC::SMEM_BYTES, stream>>>(
+        mdt, mz, mdy, mC, A, p_local, carry_s, wl.bpc, wl.nc, g, st);
+    VM_TRY(check_launch());
+    const int64_t n = int64_t(g.batch) * g.d_inner * NS;
+    carry_bwd_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(A, p_local, carry_s, p_in, g.batch, wl.nc,
+                                                                    g.d_inner);
+    VM_TRY(check_launch());
+  }
   auto kern = scan_bwd_kernel<HAS_Z, REV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_kernel) failed");
-  int* st = status_ptr();
-  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
   int sdus = 0, sdts = 0, sdzs = 0;
   VM_TRY(seq_stride32("du", o.sdu, g.seqlen, sdus));
   VM_TRY(seq_stride32("ddelta", o.sddt, g.seqlen, sdts));
   if (HAS_Z) VM_TRY(seq_stride32("dz", o.sdz, g.seqlen, sdzs));
-  const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch));
+  const BwdChunkArgs chunk{wl.bpc, wl.nc, p_in};
+  const dim3 grid(ndt, unsigned(g.batch), unsigned(wl.nc));
   kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, o.du, o.sdu.batch, sdus, o.ddt,
                                                    o.sddt.batch, sdts, o.dz, o.sdz.batch, sdzs, A, D, ckpt, wpart,
-                                                   wA, wD, g, st);
+                                                   wA, wD, chunk, g, st);
   return check_launch();
 }
 
 template <bool HAS_Z>
 int launch_bwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
                const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
-               const float* ckpt, float* wpart, float* wA, float* wD, const ScanGeom& g, cudaStream_t stream) {
-  if (g.reverse) return launch_bwd_t<HAS_Z, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, g, stream);
-  return launch_bwd_t<HAS_Z, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, g, stream);
+               const float* ckpt, float* wpart, float* wA, float* wD, const BwdWorkspace& wl, char* ws,
+               const ScanGeom& g, cudaStream_t stream) {
+  if (g.reverse)
+    return launch_bwd_t<HAS_Z, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
+  return launch_bwd_t<HAS_Z, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
 }
 
 int check_common(int64_t d_state, const float* A, const float* D) {
@@ -414,7 +529,8 @@ int64_t vmscan_ckpt_elems(int64_t batch, int64_t seqlen, int64_t d_inner, int64_
 int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const float* u, vmscan_strides su,
                const float* delta, vmscan_strides sdelta, const float* A, const float* B, vmscan_strides sB,
                const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz, float* y,
-               vmscan_strides sy, float* ckpt, const vmscan_direction* dir, vmscan_stream_t stream) {
+               vmscan_strides sy, float* ckpt, const vmscan_direction* dir, void* workspace,
+               size_t workspace_bytes, vmscan_stream_t stream) {
   VM_TRY(check_common(d_state, A, D));
   if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
   if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
@@ -434,10 +550,22 @@ int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
   VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool hz = z != nullptr, ck = ckpt != nullptr;
-  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
-  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
-  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
-  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, g, s);
+  void* ws = workspace;
+  const size_t wb = workspace_bytes;
+  if (ws != nullptr && !aligned16(ws)) return fail(VMSCAN_ERR_ALIGN, "workspace is not 16-byte aligned");
+  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+}
+
+int64_t vmscan_fwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                                   const vmscan_direction* dir) {
+  if (d_state != NS) return -VMSCAN_ERR_DSTATE;
+  ScanGeom g;
+  const int rc = make_geom(batch, seqlen, d_inner, dir, g);
+  if (rc != VMSCAN_OK) return -rc;
+  return int64_t(fwd_chunk_plan(g).bytes);
 }
 
 int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
@@ -488,28 +616,29 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const float* ck = ckpt;
   if (ck == nullptr) {
-    // Rebuild the checkpoints (the reference VJP also recomputes the forward).
-    // The forward's channel tile differs from the VJP's, so it gets its own maps.
+    // Rebuild the checkpoints (the reference VJP also recomputes the forward),
+    // chunked over L like vmscan_fwd; the forward gets its own maps.
     using FC = FwdCfg<kFwdNCW>;
     CUtensorMap fu, fdt, fB;
     VM_TRY(encode_map(&fu, "u", u, d_inner, FC::DT, su, g));
     VM_TRY(encode_map(&fdt, "delta", delta, d_inner, FC::DT, sdelta, g));
     VM_TRY(encode_map(&fB, "B", B, NS, NS, sB, g));
     float* ckw = reinterpret_cast<float*>(ws + wl.ck);
-    VM_TRY((launch_fwd<false, true, false>(fu, fdt, fu, fB, fB, nullptr, vmscan_strides{0, 0}, A, D, ckw, g, s)));
+    VM_TRY((launch_fwd<false, true, false>(fu, fdt, fu, fB, fB, nullptr, vmscan_strides{0, 0}, A, D, ckw,
+                                           ws + wl.fws, wl.total - wl.fws, g, s)));
     ck = ckw;
   }
   const BwdOut o{du, sdu, ddelta, sddelta, dz, sdz};
   if (z != nullptr) {
-    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, g, s));
+    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s));
   } else {
-    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, g, s));
+    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s));
   }
   reduce_dbc_kernel<<<dim3(unsigned(g.nboxes), unsigned(g.batch)), TMAX * kPartRow, 0, s>>>(
       wpart, dB, sdB.batch, sdB.seq, dC, sdC.batch, sdC.seq, g, ndt);
   VM_TRY(check_launch());
   const int nA = int(d_inner * NS);
-  reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch), int(d_inner));
+  reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch) * wl.nc, int(d_inner));
   return check_launch();
 }
 

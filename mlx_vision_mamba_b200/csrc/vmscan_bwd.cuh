@@ -316,6 +316,19 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
   L.dDacc += dDbox;
 }
 
+// Chunked VJP over L.  Chunk c holds forward boxes [c * bpc, min((c + 1) *
+// bpc, nboxes)); its CTA runs them last-to-first starting from the adjoint
+// carry p_in[c] (dA_{t+1} dh_{t+1} at the chunk end; zero for the last
+// chunk).  The carry depends linearly on the later chunks: a chunk maps an
+// incoming carry P to exp(A * sum_t delta_t) P + p_local, where p_local is
+// the carry it produces from a zero start (scan_bwd_carry_kernel), chained by
+// carry_bwd_kernel.  dA / dD partials are kept per (batch, chunk).
+struct BwdChunkArgs {
+  int bpc;
+  int nchunks;
+  const float* p_in;  // (batch, nchunks, d_inner, 16); row nchunks-1 unused
+};
+
 template <bool HAS_Z, bool REV>
 __global__ void __launch_bounds__(BwdCfg::NT, 2)
     scan_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
@@ -324,8 +337,8 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
                     float* __restrict__ du_out, int64_t sdub, int sdus, float* __restrict__ ddt_out,
                     int64_t sdtb, int sdts, float* __restrict__ dz_out, int64_t sdzb, int sdzs,
                     const float* __restrict__ A, const float* __restrict__ Dskip, const float* __restrict__ ckpt,
-                    float* __restrict__ wpart, float* __restrict__ wA, float* __restrict__ wD, const ScanGeom g,
-                    int* __restrict__ status) {
+                    float* __restrict__ wpart, float* __restrict__ wA, float* __restrict__ wD,
+                    const BwdChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
   using Cfg = BwdCfg;
   constexpr int DT = Cfg::DT, NST = Cfg::NST, NCT = Cfg::NCT, NCW = Cfg::NCW;
   extern __shared__ unsigned char smem_raw[];
@@ -336,10 +349,12 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty + NST) + 4;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int dtile = blockIdx.x, b = blockIdx.y;
+  const int dtile = blockIdx.x, b = blockIdx.y, cidx = blockIdx.z;
   const int ndt = gridDim.x;
   const int d0 = dtile * DT;
   const int nvalid_ch = min(DT, g.d_inner - d0);
+  // this CTA's chunk: forward box indices [i0, i1), visited last-to-first
+  const int i0 = cidx * chunk.bpc, i1 = min(i0 + chunk.bpc, g.nboxes), nbx = i1 - i0;
 
   if (tid == 0) {
 #pragma unroll
@@ -370,7 +385,7 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     if (lane == 0) ok = mbar_wait(&empty[st], ph ^ 1u, abort_flag, status) ? 1 : 0;
     ok = __shfl_sync(0xffffffffu, ok, 0);
     if (!ok) return;
-    const int ib = g.nboxes - 1 - i;  // forward processing index of this box
+    const int ib = i1 - 1 - i;  // forward processing index of this box
     const int k = REV ? g.nboxes - 1 - ib : ib;
     int c[3], nv;
     box_coords(g, k, c, nv);
@@ -404,7 +419,7 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
       prefetch_tmap(&tm_B);
       prefetch_tmap(&tm_C);
     }
-    for (int i = 0; i < NST - 1 && i < g.nboxes; ++i) issue(i);
+    for (int i = 0; i < NST - 1 && i < nbx; ++i) issue(i);
   }
 
   const PairLane pl(lane);
@@ -425,6 +440,16 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) L.P[c][j] = L.dAacc[c][j] = make_float2(0.f, 0.f);
+    // a chunk other than the last starts from the adjoint carry of the chunks after it
+    if (cidx + 1 < chunk.nchunks && vc) {
+      const float* src = chunk.p_in + ((size_t(b) * chunk.nchunks + cidx) * g.d_inner + dc + c) * NS;
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const float4 v = *reinterpret_cast<const float4*>(src + pl.group_state(gi));
+        L.P[c][2 * gi] = make_float2(v.x, v.y);
+        L.P[c][2 * gi + 1] = make_float2(v.z, v.w);
+      }
+    }
   }
   L.dDacc = 0.f;
   const int own = dc + pl.hb;
@@ -434,14 +459,14 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
   float* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
   bool alive = true;
 
-  for (int i = 0; i < g.nboxes; ++i) {
+  for (int i = 0; i < nbx; ++i) {
     const int st = i % NST;
     const uint32_t ph = uint32_t(i / NST) & 1u;
-    const int ib = g.nboxes - 1 - i;
+    const int ib = i1 - 1 - i;
     // the stage of box i-1 was released by every warp before the barrier that
     // closed box i-1, so this wait does not stall; the producer role rotates
     // over the warps so the per-box barrier does not wait on one busy warp
-    if (warp == (i % NCW) && alive && i + NST - 1 < g.nboxes) issue(i + NST - 1);
+    if (warp == (i % NCW) && alive && i + NST - 1 < nbx) issue(i + NST - 1);
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles and tcgen05 below need the whole warp
     float* part = sm + Cfg::OFF_PART + (i & 1) * (TMAX * NCW * 32);
@@ -478,17 +503,187 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     if (c ? v1 : v0) {
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi)
-        *reinterpret_cast<float4*>(wA + (size_t(b) * g.d_inner + dc + c) * NS + pl.group_state(gi)) =
+        *reinterpret_cast<float4*>(wA + ((size_t(b) * chunk.nchunks + cidx) * g.d_inner + dc + c) * NS +
+                                   pl.group_state(gi)) =
             make_float4(L.dAacc[c][2 * gi].x, L.dAacc[c][2 * gi].y, L.dAacc[c][2 * gi + 1].x,
                         L.dAacc[c][2 * gi + 1].y);
     }
   }
-  if (ev) wD[size_t(b) * g.d_inner + own] = L.dDacc;
+  if (ev) wD[(size_t(b) * chunk.nchunks + cidx) * g.d_inner + own] = L.dDacc;
   tmem_fence_before_sync();
   __syncthreads();
   if (warp == 0) {
     tmem_fence_after_sync();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+struct BwdCarryCfg {
+  static constexpr int NCW = 4;
+  static constexpr int DT = 32 * NCW;  // the VJP's channel tile (same tensor maps)
+  static constexpr int NCT = NCW * 32;
+  static constexpr int NT = NCT + 32;  // + producer warp
+  static constexpr int NST = 2;
+  static constexpr int TILE = TMAX * DT;
+  static constexpr int BCT = TMAX * NS;
+  static constexpr int OFF_Z = TILE, OFF_DY = 2 * TILE, OFF_C = 3 * TILE, OFF_NV = 3 * TILE + BCT;
+  static constexpr int STAGE_F = 3 * TILE + BCT + 32;
+  static constexpr size_t SMEM_BYTES = size_t(NST * STAGE_F) * 4 + 2 * NST * 8 + 16 + 1024;
+};
+static_assert(BwdCarryCfg::DT == BwdCfg::DT, "the carry pass reads the VJP's tensor maps");
+
+// Adjoint carry of chunks 1 .. nchunks-1 (grid z = chunk - 1) from a zero
+// carry at the chunk end: runs dh = C dy' + P, P = exp(delta A) dh backwards
+// over the chunk with the VJP's exact operations (gate included) and writes
+// P at the chunk start (p_local) and the chunk's sum of delta (carry_s).  The
+// state history is not needed for the carry, so this pass only streams
+// delta, z, dy and C.
+template <bool HAS_Z, bool REV>
+__global__ void __launch_bounds__(BwdCarryCfg::NT, 4)
+    scan_bwd_carry_kernel(const __grid_constant__ CUtensorMap tm_dt, const __grid_constant__ CUtensorMap tm_z,
+                          const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_C,
+                          const float* __restrict__ A, float* __restrict__ p_local, float* __restrict__ carry_s,
+                          int bpc, int nchunks, const ScanGeom g, int* __restrict__ status) {
+  using Cfg = BwdCarryCfg;
+  constexpr int DT = Cfg::DT, NST = Cfg::NST, NCW = Cfg::NCW;
+  extern __shared__ unsigned char smem_raw[];
+  float* sm = smem_align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + NST * Cfg::STAGE_F);
+  uint64_t* empty = full + NST;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int dtile = blockIdx.x, b = blockIdx.y, cidx = blockIdx.z + 1;
+  const int d0 = dtile * DT;
+  const int i0 = cidx * bpc, i1 = min(i0 + bpc, g.nboxes), nbx = i1 - i0;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NCW);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == NCW) {
+    // producer: boxes last-to-first, stage = delta, z, dy, C and the row count
+    if (lane == 0) {
+      prefetch_tmap(&tm_dt);
+      if (HAS_Z) prefetch_tmap(&tm_z);
+      prefetch_tmap(&tm_dy);
+      prefetch_tmap(&tm_C);
+      const uint32_t bytes = uint32_t(g.T) * uint32_t((HAS_Z ? 3 : 2) * DT + NS) * 4u;
+      for (int i = 0; i < nbx; ++i) {
+        const int st = i % NST;
+        const uint32_t ph = uint32_t(i / NST) & 1u;
+        if (!mbar_wait<true>(&empty[st], ph ^ 1u, abort_flag, status)) break;
+        const int ib = i1 - 1 - i;
+        const int k = REV ? g.nboxes - 1 - ib : ib;
+        int c[3], nv;
+        box_coords(g, k, c, nv);
+        float* base = sm + st * Cfg::STAGE_F;
+        reinterpret_cast<int*>(base + Cfg::OFF_NV)[0] = nv;
+        mbar_arrive_expect_tx(&full[st], bytes);
+        tma_load_5d(base, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
+        if (HAS_Z) tma_load_5d(base + Cfg::OFF_Z, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_DY, &tm_dy, &full[st], d0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_C, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
+      }
+    }
+    return;
+  }
+
+  const PairLane pl(lane);
+  const int c0l = warp * 32 + (lane & ~1);
+  const int dc = d0 + c0l;
+  const bool v0 = dc < g.d_inner, v1 = dc + 1 < g.d_inner;
+  float2 Ar[2][4], P[2][4];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const bool vc = c ? v1 : v0;
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const float4 a4 = vc ? *reinterpret_cast<const float4*>(A + size_t(dc + c) * NS + pl.group_state(gi))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      Ar[c][2 * gi] = make_float2(a4.x, a4.y);
+      Ar[c][2 * gi + 1] = make_float2(a4.z, a4.w);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) P[c][j] = make_float2(0.f, 0.f);
+  }
+  float2 dsum = make_float2(0.f, 0.f);
+  bool alive = true;
+  for (int i = 0; i < nbx; ++i) {
+    const int st = i % NST;
+    const uint32_t ph = uint32_t(i / NST) & 1u;
+    alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
+    if (alive) {
+      const float* __restrict__ stg = sm + st * Cfg::STAGE_F;
+      const int nv = reinterpret_cast<const int*>(stg + Cfg::OFF_NV)[0];
+#pragma unroll 2
+      for (int s = nv - 1; s >= 0; --s) {
+        const int r = REV ? nv - 1 - s : s;
+        const float2 t2 = lds2(stg + r * DT + c0l);
+        float2 dy2 = lds2(stg + Cfg::OFF_DY + r * DT + c0l);
+        if (HAS_Z) {
+          const float2 z2 = lds2(stg + Cfg::OFF_Z + r * DT + c0l);
+          const float s0 = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * z2.x));
+          const float s1 = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * z2.y));
+          dy2 = make_float2(dy2.x * (z2.x * s0), dy2.y * (z2.y * s1));
+        }
+        float2 C2[4];
+        load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+        const float2 dl2 = mul2(t2, bcast2(kLog2e));
+        dsum = add2(dsum, t2);
+        const float dyc[2] = {dy2.x, dy2.y}, dlc[2] = {dl2.x, dl2.y};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float2 e[4];
+          decay8(dlc[c], Ar[c], e);
+          const float2 dyb = bcast2(dyc[c]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) P[c][j] = mul2(e[j], fma2(C2[j], dyb, P[c][j]));
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (!alive) return;
+  float* dst = p_local + ((size_t(b) * nchunks + cidx) * g.d_inner + dc) * NS;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    if (c ? v1 : v0) {
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi)
+        *reinterpret_cast<float4*>(dst + c * NS + pl.group_state(gi)) =
+            make_float4(P[c][2 * gi].x, P[c][2 * gi].y, P[c][2 * gi + 1].x, P[c][2 * gi + 1].y);
+    }
+  }
+  if (pl.hb ? v1 : v0) carry_s[(size_t(b) * nchunks + cidx) * g.d_inner + dc + pl.hb] = pl.hb ? dsum.y : dsum.x;
+}
+
+// Chains the chunk maps P -> exp(A carry_s[c]) P + p_local[c] from the last
+// chunk backwards (zero carry after it) and writes the carry entering every
+// chunk c < nchunks-1 at its end into p_in.  One thread per (batch, channel,
+// state).
+__global__ void carry_bwd_kernel(const float* __restrict__ A, const float* __restrict__ p_local,
+                                 const float* __restrict__ carry_s, float* __restrict__ p_in, int batch, int nchunks,
+                                 int d_inner) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= int64_t(batch) * d_inner * NS) return;
+  const int n = int(idx % NS);
+  const int d = int((idx / NS) % d_inner);
+  const int b = int(idx / (int64_t(NS) * d_inner));
+  const float a = A[int64_t(d) * NS + n];
+  float pp = 0.f;
+  for (int c = nchunks - 1; c >= 1; --c) {
+    const size_t row = size_t(b) * nchunks + c;
+    pp = fmaf(expf(a * carry_s[row * d_inner + d]), pp, p_local[(row * d_inner + d) * NS + n]);
+    p_in[((row - 1) * d_inner + d) * NS + n] = pp;
   }
 }
 

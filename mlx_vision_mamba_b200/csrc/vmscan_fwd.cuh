@@ -48,15 +48,31 @@ struct FwdCfg {
   static constexpr size_t SMEM_BYTES = size_t(NST * STAGE_F) * 4 + 2 * NST * 8 + 16 + 1024;
 };
 
-template <int NCW, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
+// Chunked scan over L.  Chunk c holds boxes [c * bpc, min((c + 1) * bpc,
+// nboxes)) and runs in its own CTA (grid z).  A CARRY launch runs chunks
+// 0 .. nchunks-2 from a zero state and records, per channel, the state at the
+// chunk end (carry_h, 16 floats) and the chunk's sum of delta (carry_s): the
+// chunk maps a start state h0 to prod_t exp(delta_t A) h0 + carry_h =
+// exp(A * carry_s) h0 + carry_h.  carry_fwd_kernel chains those maps into
+// h_start, and the main launch starts chunk c from h_start[c].
+struct ChunkArgs {
+  int bpc;                  // boxes per chunk
+  int nchunks;
+  const float* h_start;     // (batch, nchunks, d_inner, 16); row c = 0 unused
+  float* carry_h;           // (batch, nchunks, d_inner, 16)
+  float* carry_s;           // (batch, nchunks, d_inner)
+};
+
+template <int NCW, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY = false>
 __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
                     const __grid_constant__ CUtensorMap tm_C, float* __restrict__ y, int64_t syb, int sys,
                     const float* __restrict__ A, const float* __restrict__ Dskip, float* __restrict__ ckpt,
-                    const ScanGeom g, int* __restrict__ status) {
+                    const ChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
   using Cfg = FwdCfg<NCW>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST;
+  static_assert(!CARRY || (!HAS_Z && !SAVE_CK && !STORE_Y), "a carry pass stores nothing but the carries");
   constexpr bool LOAD_Z = HAS_Z && STORE_Y;
   extern __shared__ unsigned char smem_raw[];
   float* sm = smem_align1024(smem_raw);
@@ -65,8 +81,9 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int dtile = blockIdx.x, b = blockIdx.y;
+  const int dtile = blockIdx.x, b = blockIdx.y, cidx = blockIdx.z;
   const int d0 = dtile * DT;
+  const int i0 = cidx * chunk.bpc, i1 = min(i0 + chunk.bpc, g.nboxes);  // this CTA's boxes
 
   if (tid == 0) {
 #pragma unroll
@@ -92,9 +109,9 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
       if (STORE_Y) prefetch_tmap(&tm_C);
     }
     const uint32_t bytes = uint32_t(g.T) * uint32_t((LOAD_Z ? 3 : 2) * DT + (STORE_Y ? 2 : 1) * NS) * 4u;
-    for (int i = 0; i < g.nboxes; ++i) {
-      const int st = i % NST;
-      const uint32_t ph = uint32_t(i / NST) & 1u;
+    for (int i = i0; i < i1; ++i) {
+      const int st = (i - i0) % NST;
+      const uint32_t ph = uint32_t((i - i0) / NST) & 1u;
       int ok = 1;
       if (lane == 0) ok = mbar_wait<true>(&empty[st], ph ^ 1u, abort_flag, status) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, ok, 0)) break;
@@ -137,7 +154,18 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) h[c][j] = make_float2(0.f, 0.f);
+    // a later chunk of a chunked scan starts from the chained carry
+    if (!CARRY && cidx > 0 && vc) {
+      const float* src = chunk.h_start + ((size_t(b) * chunk.nchunks + cidx) * g.d_inner + dc + c) * NS;
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const float4 v = *reinterpret_cast<const float4*>(src + pl.group_state(gi));
+        h[c][2 * gi] = make_float2(v.x, v.y);
+        h[c][2 * gi + 1] = make_float2(v.z, v.w);
+      }
+    }
   }
+  float2 dsum = make_float2(0.f, 0.f);  // CARRY: sum of delta over the chunk, both channels
   const int own = c0l + pl.hb;
   const float Down = ev ? Dskip[d0 + own] : 0.f;
   float* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
@@ -148,9 +176,9 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
     int r;
   };
 
-  for (int i = 0; i < g.nboxes; ++i) {
-    const int st = i % NST;
-    const uint32_t ph = uint32_t(i / NST) & 1u;
+  for (int i = i0; i < i1; ++i) {
+    const int st = (i - i0) % NST;
+    const uint32_t ph = uint32_t((i - i0) / NST) & 1u;
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles below need the whole warp
     if (alive) {
@@ -165,6 +193,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
         load8(stg + Cfg::OFF_B + r * NS, pl, B2);
         const float2 du2 = mul2(t2, u2);
         const float2 dl2 = mul2(t2, bcast2(kLog2e));
+        if (CARRY) dsum = add2(dsum, t2);
         const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -216,6 +245,41 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
         }
       }
     }
+  }
+  if (CARRY && alive) {
+    float* dst = chunk.carry_h + ((size_t(b) * chunk.nchunks + cidx) * g.d_inner + dc) * NS;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      if (c ? v1 : v0) {
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi)
+          *reinterpret_cast<float4*>(dst + c * NS + pl.group_state(gi)) =
+              make_float4(h[c][2 * gi].x, h[c][2 * gi].y, h[c][2 * gi + 1].x, h[c][2 * gi + 1].y);
+      }
+    }
+    if (ev) chunk.carry_s[(size_t(b) * chunk.nchunks + cidx) * g.d_inner + d0 + own] = pl.hb ? dsum.y : dsum.x;
+  }
+}
+
+// Chains the chunk maps h -> exp(A carry_s[c]) h + carry_h[c] over c = 0 ..
+// nchunks-2 from a zero state and writes the state entering every chunk c >= 1
+// into h_start.  One thread per (batch, channel, state); exp by the accurate
+// expf (the per-step decays of the scan use MUFU ex2; both approximate
+// prod_t exp(delta_t A) = exp(A sum_t delta_t)).
+__global__ void carry_fwd_kernel(const float* __restrict__ A, const float* __restrict__ carry_h,
+                                 const float* __restrict__ carry_s, float* __restrict__ h_start, int batch,
+                                 int nchunks, int d_inner) {
+  const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= int64_t(batch) * d_inner * NS) return;
+  const int n = int(idx % NS);
+  const int d = int((idx / NS) % d_inner);
+  const int b = int(idx / (int64_t(NS) * d_inner));
+  const float a = A[int64_t(d) * NS + n];
+  float hh = 0.f;
+  for (int c = 0; c + 1 < nchunks; ++c) {
+    const size_t row = size_t(b) * nchunks + c;
+    hh = fmaf(expf(a * carry_s[row * d_inner + d]), hh, carry_h[(row * d_inner + d) * NS + n]);
+    h_start[((row + 1) * d_inner + d) * NS + n] = hh;
   }
 }
 

@@ -135,11 +135,16 @@ class _SelectiveScanFn(torch.autograd.Function):
             if n_ck < 0:
                 _native.check(-n_ck, "vmscan_ckpt_elems")
             ckpt = torch.empty(n_ck, dtype=torch.float32, device=x.device)
+        fws_n = lib.vmscan_fwd_workspace_bytes(bt, l, dn, D_STATE, dptr)
+        if fws_n < 0:
+            _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
+        fws = torch.empty(int(fws_n), dtype=torch.uint8, device=x.device) if fws_n > 0 else None
         st = lib.vmscan_fwd(
             bt, l, dn, D_STATE,
             _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
             _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
-            _ptr(z_), _strides(z_), _ptr(y), _strides(y), _ptr(ckpt), dptr, _stream(x),
+            _ptr(z_), _strides(z_), _ptr(y), _strides(y), _ptr(ckpt), dptr,
+            _ptr(fws), int(fws_n), _stream(x),
         )
         _native.check(st, "vmscan_fwd")
         if need_grad:

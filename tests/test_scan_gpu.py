@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from golden_cases import SCAN_CASES, load
-from mlx_vision_mamba_b200 import ScanDirection, _native, device_status, directions_for, selective_scan_cuda
+from mlx_vision_mamba_b200 import BACKWARD, ScanDirection, _native, device_status, directions_for, selective_scan_cuda
 from oracle import scan_ref
 from parity import assert_parity
 
@@ -159,7 +159,7 @@ def test_bwd_without_checkpoints_recomputes_them():
     st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
                         t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
                         t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), ck.data_ptr(), None,
-                        stream)
+                        None, 0, stream)
     assert st == 0
     a = bwd(ck)
     r = bwd(None)
@@ -190,3 +190,41 @@ def test_device_status_is_clean():
     inp = scan_ref.sweep_inputs(2, 64, 64, seed=1)
     cuda_vjp(inp, True, ScanDirection(reverse=True))
     assert device_status() == 0
+
+
+CHUNKED = [
+    (1, 4096, 256, True, None),                         # 256 boxes over up to 32 chunks
+    (2, 1000, 200, True, "reverse"),                    # ragged last box and chunk, reversed order
+    (2, 784, 96, True, "colmajor"),                     # 28 x 28 grid, column-major (K=4 direction 1)
+    (1, 512, 40, False, None),
+]
+
+
+@pytest.mark.parametrize("b,l,dn,gated,dirname", CHUNKED)
+def test_chunked_scan_matches_oracle_and_unchunked(b, l, dn, gated, dirname):
+    """Small batch x channel grids run chunked over L (carry pass + carry chain
+    + main pass, forward and VJP): results match the oracle, and the forward
+    matches the same scan run in one piece (no workspace) to fp32 rounding."""
+    lib = _native.load()
+    direction = None
+    if dirname == "reverse":
+        direction = BACKWARD
+    elif dirname == "colmajor":
+        direction = directions_for(4, (28, 28))[1]
+    dptr = ctypes.byref(direction.to_native()) if direction is not None else None
+    assert lib.vmscan_fwd_workspace_bytes(b, l, dn, 16, dptr) > 0, "this shape should be chunked"
+    inp = scan_ref.sweep_inputs(b, l, dn, seed=l + dn)
+    check_all(inp, gated, direction, tag=f"chunked ({b},{l},{dn},{gated},{dirname})")
+
+    # the forward in one piece: raw ABI call without a workspace
+    S = lambda x: _native.Strides(x.stride(0), x.stride(1))  # noqa: E731
+    t = {k: v.cuda().float().contiguous() for k, v in inp.items()}
+    y1 = torch.empty(b, l, dn, device="cuda")
+    st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
+                        t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
+                        t["D"].data_ptr(), t["z"].data_ptr() if gated else None,
+                        S(t["z"]) if gated else _native.Strides(0, 0), y1.data_ptr(), S(y1), None, dptr,
+                        None, 0, torch.cuda.current_stream().cuda_stream)
+    assert st == 0, lib.vmscan_last_error()
+    y2, _ = cuda_vjp(inp, gated, direction)
+    torch.testing.assert_close(y2, y1.cpu(), rtol=1e-4, atol=1e-5)

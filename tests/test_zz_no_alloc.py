@@ -63,7 +63,7 @@ def test_noalloc_matches_workspace_entry_point_twice(direction):
     st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
                         t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
                         t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), ck.data_ptr(), dptr,
-                        _stream())
+                        None, 0, _stream())
     assert st == 0, lib.vmscan_last_error()
 
     # reference: the workspace-taking entry point
