@@ -208,6 +208,41 @@ class BidirectionalMambaBlock(nn.Module):
         return x + directions_sum([self.forward_mamba, self.backward_mamba], [None, BACKWARD], h)
 
 
+class _ToDirectionRanks(torch.autograd.Function):
+    """The block input entering the rank's direction branches: identity forward;
+    backward all-reduces (sums) the branches' input gradients over the ranks."""
+
+    @staticmethod
+    def forward(ctx, h, group):
+        ctx.group = group
+        return h.view_as(h)
+
+    @staticmethod
+    def backward(ctx, grad):
+        import torch.distributed as dist
+
+        grad = grad.contiguous()
+        dist.all_reduce(grad, group=ctx.group)
+        return grad, None
+
+
+class _FromDirectionRanks(torch.autograd.Function):
+    """Sum of the directions over the ranks: all-reduce forward; identity
+    backward (every rank holds the whole, replicated loss)."""
+
+    @staticmethod
+    def forward(ctx, y, group):
+        import torch.distributed as dist
+
+        y = y.contiguous().clone()
+        dist.all_reduce(y, group=group)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad):
+        return grad, None
+
+
 class MultiDirectionalMambaBlock(nn.Module):
     """K independent MambaBlocks, one per scan direction, summed plus residual
     (mamba_block.py:341-566).  Directions follow `_apply_direction` (:407-534);
@@ -242,11 +277,36 @@ class MultiDirectionalMambaBlock(nn.Module):
             [MambaBlock(d_model, d_state, d_conv, expand_factor, scan_mode) for _ in range(num_directions)]
         )
         self.directions = directions_for(num_directions, self.grid_shape)
+        self.direction_group = None  # process group sharing the directions (shard_directions)
+
+    def shard_directions(self, group) -> None:
+        """Direction parallelism (no counterpart in the reference, which runs one
+        device): rank r of `group` runs only the directions k with
+        k % world == r and the partial sums are combined by an all-reduce whose
+        backward sums the ranks' input gradients.  All ranks must feed the same
+        input; every parameter keeps its reference name, and the parameters of
+        the other ranks' directions simply receive no gradient here."""
+        self.direction_group = group
+
+    def _local(self, blocks, directions):
+        import torch.distributed as dist
+
+        world, rank = dist.get_world_size(self.direction_group), dist.get_rank(self.direction_group)
+        ks = [k for k in range(len(blocks)) if k % world == rank]
+        return [blocks[k] for k in ks], [directions[k] for k in ks]
+
+    def _sum(self, blocks, directions, h):
+        if self.direction_group is None:
+            return directions_sum(blocks, directions, h)
+        lb, ld = self._local(blocks, directions)
+        hl = _ToDirectionRanks.apply(h, self.direction_group)
+        y = directions_sum(lb, ld, hl) if lb else hl * 0.0
+        return _FromDirectionRanks.apply(y, self.direction_group)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         n = x.shape[1]
         h = self.norm(x)
         expected = math.prod(self.grid_shape) if self.grid_shape is not None else n
         if n != expected and self.num_directions > 2:
-            return x + directions_sum(self.mamba_blocks[:2], [None, BACKWARD], h)
-        return x + directions_sum(self.mamba_blocks, self.directions, h)
+            return x + self._sum(self.mamba_blocks[:2], [None, BACKWARD], h)
+        return x + self._sum(self.mamba_blocks, self.directions, h)

@@ -153,6 +153,13 @@ class VisionMamba(nn.Module):
         )
         self.norm = LayerNorm(embed_dim)
 
+    def shard_directions(self, group) -> None:
+        """Split every layer's scan directions across the ranks of `group`
+        (MultiDirectionalMambaBlock.shard_directions); all ranks process the
+        same batch."""
+        for block in self.blocks:
+            block.shard_directions(group)
+
     def forward(self, x: torch.Tensor, patch_indices: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x.dim() != 3:
             x = self.patch_embed(x)

@@ -78,3 +78,84 @@ def test_ddp_gradients_equal_full_batch(tmp_path):
     torch.nn.functional.mse_loss(model(x), tgt).backward()
     for k, p in model.named_parameters():
         torch.testing.assert_close(rec["grads"][k], p.grad, rtol=1e-5, atol=1e-6)
+
+
+class _FakeBranchBlock(torch.nn.Module):
+    """Stands in for a MambaBlock on the CPU (the scan kernels are CUDA-only):
+    the same projection parameters and `scan_branch` interface, with an
+    elementwise, direction-dependent body."""
+
+    def __init__(self, d_model, d_inner, seed):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.d_inner = d_inner
+        self.in_proj = torch.nn.Linear(d_model, 2 * d_inner, bias=False)
+        self.out_proj = torch.nn.Linear(d_inner, d_model, bias=False)
+        with torch.no_grad():
+            self.in_proj.weight.copy_(torch.randn(2 * d_inner, d_model, generator=g) * 0.3)
+            self.out_proj.weight.copy_(torch.randn(d_model, d_inner, generator=g) * 0.3)
+
+    def scan_branch(self, xz, direction):
+        x, z = torch.split(xz, [self.d_inner, self.d_inner], dim=-1)
+        y = torch.cumsum(torch.tanh(x), dim=1) if direction is None else torch.tanh(x).flip(1).cumsum(1).flip(1)
+        return y * torch.sigmoid(z)
+
+    def forward(self, h, direction=None):
+        return self.out_proj(self.scan_branch(self.in_proj(h), direction))
+
+
+def _directional_block(k):
+    from mlx_vision_mamba_b200.direction import BACKWARD
+    from mlx_vision_mamba_b200.mamba_block import MultiDirectionalMambaBlock
+
+    torch.manual_seed(0)
+    blk = MultiDirectionalMambaBlock(8, 16, 4, 2, num_directions=k, grid_shape=(4, 4) if k == 4 else None)
+    blk.mamba_blocks = torch.nn.ModuleList([_FakeBranchBlock(8, 16, seed=10 + i) for i in range(k)])
+    blk.directions = [None if i % 2 == 0 else BACKWARD for i in range(k)]
+    return blk
+
+
+def _shard_worker(rank, world, port, out_path, k):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        blk = _directional_block(k)
+        blk.shard_directions(dist.group.WORLD)
+        g = torch.Generator().manual_seed(7)
+        x = torch.randn(2, 16, 8, generator=g).requires_grad_(True)
+        dy = torch.randn(2, 16, 8, generator=g)
+        y = blk(x)
+        (y * dy).sum().backward()
+        grads = {n: (p.grad.clone() if p.grad is not None else None) for n, p in blk.named_parameters()}
+        torch.save({"y": y.detach(), "dx": x.grad.clone(), "grads": grads}, f"{out_path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("k", [2, 4])
+def test_direction_sharding_matches_unsharded(tmp_path, k):
+    """Directions split over 2 gloo ranks, summed by an autograd all-reduce:
+    every rank gets the unsharded output and input gradient; each direction's
+    parameters get their unsharded gradient on the rank that owns them; the
+    shared LayerNorm's gradient is the same on every rank."""
+    world = 2
+    out_path = str(tmp_path / "shard")
+    mp.spawn(_shard_worker, args=(world, _free_port(), out_path, k), nprocs=world, join=True)
+    blk = _directional_block(k)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 16, 8, generator=g).requires_grad_(True)
+    dy = torch.randn(2, 16, 8, generator=g)
+    y = blk(x)
+    (y * dy).sum().backward()
+    for r in range(world):
+        rec = torch.load(f"{out_path}.{r}")
+        torch.testing.assert_close(rec["y"], y.detach(), rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(rec["dx"], x.grad, rtol=1e-5, atol=1e-6)
+        for n, p in blk.named_parameters():
+            owner = n.startswith("mamba_blocks.") and int(n.split(".")[1]) % world == r
+            shared = not n.startswith("mamba_blocks.")
+            if owner or shared:
+                torch.testing.assert_close(rec["grads"][n], p.grad, rtol=1e-5, atol=1e-6, msg=n)
+            else:
+                assert rec["grads"][n] is None, n
