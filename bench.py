@@ -267,6 +267,9 @@ def main():
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
     ap.add_argument("--model-eager", action="store_true", help="run the model steps eagerly (no CUDA graph)")
+    ap.add_argument("--model4d", choices=["dp", "dirshard"],
+                    help="only time VisionMamba-4D training (config 5, global batch 8): data parallel, or the "
+                         "scan directions split over the ranks; prints one JSON line")
     ap.add_argument("--sweep", action="store_true",
                     help="time forward and VJP separately on the 12 op-sweep points and print a table")
     ap.add_argument("--model-profile", action="store_true",
@@ -299,6 +302,15 @@ def main():
         os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "0")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     args.warmup = max(args.warmup, 3)
+
+    if args.model4d:
+        barrier = (lambda: dist.barrier(device_ids=[local])) if world > 1 else (lambda: None)
+        line = run_model4d(dev, rank, world, args.model4d, max(3, min(args.steps, 10)), args.warmup, barrier)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     b, l, d = WORKLOAD["batch"], WORKLOAD["seqlen"], WORKLOAD["d_inner"]
     t = make_inputs(b, l, d, dev, seed=1234 + rank)
@@ -560,6 +572,64 @@ def profile_model(warmup):
     print("top kernels:")
     for t_us, n, key in rows[:25]:
         print(f"  {t_us / steps / 1e3:8.3f} ms {100 * t_us / total:5.1f} % x{n // steps:4d} {key[:100]}")
+
+
+def run_model4d(dev, rank, world, mode, steps, warmup, barrier):
+    """VisionMamba-4D (K=8, T=8 frames of 64^3 voxels, patch 16, E 384, depth
+    6) training steps, one CUDA graph per step.  "dp":
+    the global batch of 8 split over the ranks, gradients averaged by DDP.
+    "dirshard": every rank takes the whole batch and runs world-th of each
+    layer's 8 scan directions; the direction sums and the block-input
+    gradients are all-reduced inside the step."""
+    import torch
+    import torch.distributed as dist
+
+    from mlx_vision_mamba_b200 import train
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    cfg = train.VISION_MAMBA_4D
+    side = torch.cuda.Stream(dev)
+    if mode == "dp":
+        a, b = train.shard(cfg.global_batch, rank, world)
+        with torch.cuda.stream(side):
+            model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+        batch, seed = b - a, 100 + rank
+    else:
+        model = train.build_encoder(cfg, dev, seed=0)
+        if world > 1:
+            model.shard_directions(dist.group.WORLD)
+        batch, seed = cfg.global_batch, 100
+    torch.cuda.current_stream(dev).wait_stream(side)
+    opt = train.make_optimizer(model, capturable=True)
+    x, tgt = train.synthetic_batch(cfg, batch, dev, seed=seed)
+    step = train.GraphedTrainStep(model, opt, x, tgt, side_stream=side)
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    loss = float(loss.item())
+    step.close()
+    tm = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    ms = float(tm.item())
+    return {"metric": "VisionMamba-4D train img/s", "value": cfg.global_batch * steps / (ms / 1e3), "unit": "img/s",
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "strong", "dtype": "f32 (TF32 off)", "data": "synthetic",
+            "loss": loss, "config": {"workload": "VisionMamba-4D K=8, input (8, 8, 64, 64, 64, 1), patch 16, "
+                                                  "temporal patch 1, E 384, depth 6, MSE vs N(0,1)",
+                                     "global_batch": cfg.global_batch,
+                                     "parallelism": (f"data parallel x{world} (DDP)" if mode == "dp" else
+                                                     f"scan directions split x{world}, whole batch per rank"),
+                                     "execution": "one CUDA graph per step"}}
 
 
 def run_e2e(t, dev, K, warmup, world, barrier):
