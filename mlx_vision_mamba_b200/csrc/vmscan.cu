@@ -683,7 +683,8 @@ int64_t vmscan_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t
   if (batch <= 0 || seqlen <= 0 || channels <= 0) return -VMSCAN_ERR_SHAPE;
   if (ksize < 1 || ksize > CONV_KMAX) return -VMSCAN_ERR_CONV;
   const int64_t nchunk = (seqlen + CONV_CHUNK - 1) / CONV_CHUNK;
-  return int64_t(align256(size_t(batch) * nchunk * channels * (CONV_KMAX + 1) * 4));
+  return int64_t(align256(size_t(batch) * nchunk * channels * (CONV_KMAX + 1) * 4) +
+                 align256(size_t(CONV_RGROUPS) * channels * (CONV_KMAX + 1) * 4));
 }
 
 int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,
@@ -717,8 +718,15 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
                                                          int(ksize), g);
   VM_TRY(check_launch());
   const int n = int(channels * (ksize + 1));
-  conv_reduce_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(wpart, dweight, dbias, int(batch) * nchunk,
-                                                                int(channels), int(ksize));
+  const int nrows = int(batch) * nchunk;
+  const int ngroups = std::min(CONV_RGROUPS, nrows);
+  float* gpart = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                          align256(size_t(batch) * nchunk * channels * (CONV_KMAX + 1) * 4));
+  conv_reduce_kernel<<<dim3(unsigned((n + 255) / 256), unsigned(ngroups)), 256, 0, s>>>(wpart, gpart, nrows,
+                                                                                       int(channels), int(ksize));
+  VM_TRY(check_launch());
+  conv_reduce2_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(gpart, dweight, dbias, ngroups, int(channels),
+                                                               int(ksize));
   return check_launch();
 }
 

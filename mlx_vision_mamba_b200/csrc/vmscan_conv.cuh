@@ -21,7 +21,8 @@ namespace vmscan {
 
 constexpr int CONV_CHUNK = 32;
 constexpr int CONV_KMAX = 8;
-constexpr int CONV_THREADS = 128;
+constexpr int CONV_THREADS = 64;  // float4 channel groups per CTA (768 and 1536 channels fill whole CTAs)
+constexpr int CONV_RGROUPS = 16;  // row groups of the first dw/dbias reduction level
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
@@ -96,7 +97,8 @@ __global__ void __launch_bounds__(CONV_THREADS)
 // [p0, p0+CHUNK+K-1), forms dpre = dout * silu'(pre), emits
 //   dx[p'] = sum_k w[k] dpre[p' + K - 1 - k]
 // and per-thread partial sums of dw[k] = sum_p dpre[p] x[p-K+1+k] and
-// dbias = sum_p dpre[p] over the chunk, written to wpart[b][chunk][c][KMAX+1].
+// dbias = sum_p dpre[p] over the chunk, written slot-major to
+// wpart[b][chunk][slot][c] (slot k < K: dw[k], slot KMAX: dbias) as float4.
 template <int KW>
 __global__ void __launch_bounds__(CONV_THREADS)
     conv_silu_bwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
@@ -192,33 +194,40 @@ __global__ void __launch_bounds__(CONV_THREADS)
     }
   }
   // partials: slot k < K holds dw[k] (window slot KW-K+k), slot CONV_KMAX holds dbias
-  float* wp = wpart + ((size_t(b) * nchunk + blockIdx.y) * C + c4 * 4) * (CONV_KMAX + 1);
-  const float dbq[4] = {db_acc.x, db_acc.y, db_acc.z, db_acc.w};
+  float* wp = wpart + (size_t(b) * nchunk + blockIdx.y) * (CONV_KMAX + 1) * C + c4 * 4;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-#pragma unroll
-    for (int k = 0; k < KW; ++k) {
-      if (k < K) {
-        const float4 v = dw_acc[KW - K + k];
-        const float vq = q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
-        wp[q * (CONV_KMAX + 1) + k] = vq;
-      }
-    }
-    wp[q * (CONV_KMAX + 1) + CONV_KMAX] = dbq[q];
-  }
+  for (int k = 0; k < KW; ++k)
+    if (k < K) *reinterpret_cast<float4*>(wp + size_t(k) * C) = dw_acc[KW - K + k];
+  *reinterpret_cast<float4*>(wp + size_t(CONV_KMAX) * C) = db_acc;
 }
 
-// dweight (C, K) and dbias (C): sum partials over (batch, chunk) in order.
-__global__ void conv_reduce_kernel(const float* __restrict__ wpart, float* __restrict__ dw, float* __restrict__ db,
-                                   int nrows, int C, int K) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= C * (K + 1)) return;
-  const int c = idx / (K + 1), k = idx % (K + 1);
-  const int slot = (k < K) ? k : CONV_KMAX;
+// dweight (C, K) and dbias (C) from the (batch, chunk) partials, in two
+// fixed-order levels: conv_reduce_kernel sums row group blockIdx.y (rows
+// r = y, y + G, ...) of every (slot, channel) column into gpart[y]; then
+// conv_reduce2_kernel sums the G group partials in order.  Columns are
+// contiguous in the slot-major layout, so every load is coalesced.
+__global__ void conv_reduce_kernel(const float* __restrict__ wpart, float* __restrict__ gpart, int nrows, int C,
+                                   int K) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;  // slot * C + c over the K + 1 used slots
+  if (col >= (K + 1) * C) return;
+  const int sl = col / C, c = col % C;
+  const int slot = sl < K ? sl : CONV_KMAX;
+  const size_t stride = size_t(CONV_KMAX + 1) * C;
+  const float* src = wpart + size_t(slot) * C + c;
   float acc = 0.f;
-  for (int r = 0; r < nrows; ++r) acc += wpart[(size_t(r) * C + c) * (CONV_KMAX + 1) + slot];
-  if (k < K)
-    dw[size_t(c) * K + k] = acc;
+  for (int r = blockIdx.y; r < nrows; r += gridDim.y) acc += src[r * stride];
+  gpart[size_t(blockIdx.y) * (K + 1) * C + col] = acc;
+}
+
+__global__ void conv_reduce2_kernel(const float* __restrict__ gpart, float* __restrict__ dw, float* __restrict__ db,
+                                    int ngroups, int C, int K) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= (K + 1) * C) return;
+  float acc = 0.f;
+  for (int gi = 0; gi < ngroups; ++gi) acc += gpart[size_t(gi) * (K + 1) * C + col];
+  const int sl = col / C, c = col % C;
+  if (sl < K)
+    dw[size_t(c) * K + sl] = acc;
   else
     db[c] = acc;
 }
