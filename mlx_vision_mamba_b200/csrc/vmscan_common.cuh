@@ -381,47 +381,15 @@ __device__ __forceinline__ float pair_scatter(float v0, float v1, int hb) {
   return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
-// 2^x of a pair on the FMA pipe: Cody-Waite split x = n + f (n integer by
-// the 1.5 * 2^23 rounding trick, f in [-0.5, 0.5]), 2^f by a degree-6
-// polynomial whose coefficients were fitted here to 2^f on [-0.5, 0.5] for
-// minimax relative error (Lawson-weighted least squares; 1.9e-9 in exact
-// arithmetic; 0.93 ulp max and 0.01 ulp mean error after fp32 Horner
-// evaluation), and 2^n added to the exponent field with one integer
-// multiply-add (the low bits of the rounded sum are n, so (bits << 23) is
-// n << 23).  x is clamped to [-126, 127]: below, the result is 2^-126 where
-// ex2.approx.ftz returns 0 (an absolute difference under 1.2e-38).
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x.x = fminf(fmaxf(x.x, -126.0f), 127.0f);
-  x.y = fminf(fmaxf(x.y, -126.0f), 127.0f);
-  const float2 t = add2(x, bcast2(kRound));
-  const float2 n = add2(t, bcast2(-kRound));
-  const float2 f = fma2(n, bcast2(-1.0f), x);
-  float2 p = fma2(bcast2(1.5345811e-4f), f, bcast2(1.3399931e-3f));
-  p = fma2(p, f, bcast2(9.6184891e-3f));
-  p = fma2(p, f, bcast2(5.5503286e-2f));
-  p = fma2(p, f, bcast2(2.4022646e-1f));
-  p = fma2(p, f, bcast2(6.9314718e-1f));
-  p = fma2(p, f, bcast2(1.0f));
-  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
-                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
-}
-
-// exp(delta A) of the lane's 8 states of one channel; the VJP's forward
-// recompute and its reverse pass call this with identical arguments.  The
-// last NPOLY pairs go to the FMA pipe (exp2_poly2, argument without the MUFU
-// bias offset), the rest to MUFU ex2.approx.
-template <int NPOLY = 0>
+// exp(delta A) of the lane's 8 states of one channel (MUFU ex2.approx with
+// the bias-correcting argument offset); the VJP's forward recompute and its
+// reverse pass call this with identical arguments.
 __device__ __forceinline__ void decay8(float dl, const float2 Ar[4], float2 e[4]) {
   const float2 dlb = bcast2(dl), off2 = bcast2(kEx2ArgBias);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    if (j >= 4 - NPOLY) {
-      e[j] = exp2_poly2(mul2(dlb, Ar[j]));
-    } else {
-      const float2 a = fma2(dlb, Ar[j], off2);
-      e[j] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
-    }
+    const float2 a = fma2(dlb, Ar[j], off2);
+    e[j] = make_float2(ex2_approx(a.x), ex2_approx(a.y));
   }
 }
 

@@ -27,12 +27,6 @@
 
 namespace vmscan {
 
-// Pairs of state decays per channel and step evaluated on the FMA pipe
-// instead of MUFU (the forward is bound by the exp2 unit).
-#ifndef VMSCAN_FWD_POLY_PAIRS
-#define VMSCAN_FWD_POLY_PAIRS 0
-#endif
-constexpr int kFwdPolyPairs = VMSCAN_FWD_POLY_PAIRS;
 
 template <int NCW>
 struct FwdCfg {
@@ -198,7 +192,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float2 e[4];
-          decay8<kFwdPolyPairs>(dlc[c], Ar[c], e);
+          decay8(dlc[c], Ar[c], e);
           const float2 dub = bcast2(duc[c]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) h[c][j] = fma2(e[j], h[c][j], mul2(dub, B2[j]));
