@@ -267,9 +267,11 @@ def main():
     ap.add_argument("--seqlen", type=int, default=WORKLOAD["seqlen"])
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
     ap.add_argument("--model-eager", action="store_true", help="run the model steps eagerly (no CUDA graph)")
-    ap.add_argument("--model4d", choices=["dp", "dirshard"],
-                    help="only time VisionMamba-4D training (config 5, global batch 8): data parallel, or the "
-                         "scan directions split over the ranks; prints one JSON line")
+    ap.add_argument("--encoder", choices=["3d", "4d"],
+                    help="only time VisionMamba-3D (config 4, K=6, global batch 16) or -4D (config 5, K=8, global "
+                         "batch 8) training and print one JSON line")
+    ap.add_argument("--parallel", choices=["dp", "dirshard"], default="dp",
+                    help="with --encoder: data parallel, or the scan directions split over the ranks")
     ap.add_argument("--sweep", action="store_true",
                     help="time forward and VJP separately on the 12 op-sweep points and print a table")
     ap.add_argument("--model-profile", action="store_true",
@@ -303,9 +305,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     args.warmup = max(args.warmup, 3)
 
-    if args.model4d:
+    if args.encoder:
         barrier = (lambda: dist.barrier(device_ids=[local])) if world > 1 else (lambda: None)
-        line = run_model4d(dev, rank, world, args.model4d, max(3, min(args.steps, 10)), args.warmup, barrier)
+        line = run_encoder(dev, rank, world, args.encoder, args.parallel, max(3, min(args.steps, 10)), args.warmup,
+                           barrier)
         if rank == 0:
             print(json.dumps(line), flush=True)
         if world > 1:
@@ -614,13 +617,21 @@ def profile_model(warmup):
         print(f"  {t_us / steps / 1e3:8.3f} ms {100 * t_us / total:5.1f} % x{n // steps:4d} {key[:100]}")
 
 
-def run_model4d(dev, rank, world, mode, steps, warmup, barrier):
-    """VisionMamba-4D (K=8, T=8 frames of 64^3 voxels, patch 16, E 384, depth
-    6) training steps, one CUDA graph per step.  "dp":
-    the global batch of 8 split over the ranks, gradients averaged by DDP.
-    "dirshard": every rank takes the whole batch and runs world-th of each
-    layer's 8 scan directions; the direction sums and the block-input
-    gradients are all-reduced inside the step."""
+ENCODERS = {
+    "3d": ("VisionMamba-3D", "VisionMamba-3D K=6, input (16, 128, 128, 128, 1), patch 16 (512 tokens), E 384, "
+           "depth 6, MSE vs N(0,1)"),
+    "4d": ("VisionMamba-4D", "VisionMamba-4D K=8, input (8, 8, 64, 64, 64, 1), patch 16, temporal patch 1 "
+           "(512 tokens), E 384, depth 6, MSE vs N(0,1)"),
+}
+
+
+def run_encoder(dev, rank, world, which, mode, steps, warmup, barrier):
+    """VisionMamba-3D (K=6, 128^3 volumes, global batch 16)
+    or -4D (config 5: K=8, 8 frames of 64^3, global batch 8) training steps,
+    one CUDA graph per step.  "dp": the global batch split over the ranks,
+    gradients averaged by DDP.  "dirshard": every rank takes the whole batch
+    and runs its share of each layer's scan directions; the direction sums and
+    the block-input gradients are all-reduced inside the step."""
     import torch
     import torch.distributed as dist
 
@@ -628,7 +639,8 @@ def run_model4d(dev, rank, world, mode, steps, warmup, barrier):
 
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
-    cfg = train.VISION_MAMBA_4D
+    cfg = train.VISION_MAMBA_3D if which == "3d" else train.VISION_MAMBA_4D
+    name, workload = ENCODERS[which]
     side = torch.cuda.Stream(dev)
     if mode == "dp":
         a, b = train.shard(cfg.global_batch, rank, world)
@@ -661,11 +673,10 @@ def run_model4d(dev, rank, world, mode, steps, warmup, barrier):
     if world > 1:
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
     ms = float(tm.item())
-    return {"metric": "VisionMamba-4D train img/s", "value": cfg.global_batch * steps / (ms / 1e3), "unit": "img/s",
+    return {"metric": f"{name} train img/s", "value": cfg.global_batch * steps / (ms / 1e3), "unit": "img/s",
             "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
             "higher_is_better": True, "scaling": "strong", "dtype": "f32 (TF32 off)", "data": "synthetic",
-            "loss": loss, "config": {"workload": "VisionMamba-4D K=8, input (8, 8, 64, 64, 64, 1), patch 16, "
-                                                  "temporal patch 1, E 384, depth 6, MSE vs N(0,1)",
+            "loss": loss, "config": {"workload": workload,
                                      "global_batch": cfg.global_batch,
                                      "parallelism": (f"data parallel x{world} (DDP)" if mode == "dp" else
                                                      f"scan directions split x{world}, whole batch per rank"),
