@@ -285,6 +285,15 @@ int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int
                       int64_t* geom);
 
 /*
+ * Exercises the device-side wait failure path: a one-warp kernel waits on an
+ * mbarrier that nothing arrives on, gives up after `tries` polls (each polls
+ * for at most ~1 us), sets the sticky status to VMSCAN_ERR_TIMEOUT and
+ * returns.  Nothing faults; vmscan_device_status then reports and clears it.
+ * No reference counterpart (the reference has no device error reporting).
+ */
+int vmscan_wait_timeout_selftest(uint32_t tries, vmscan_stream_t stream);
+
+/*
  * Synchronises `stream` and returns the sticky device-side status (0 or
  * VMSCAN_ERR_TIMEOUT, set when a kernel's bounded wait ran out and the kernel
  * returned early); clears it when `clear` != 0.

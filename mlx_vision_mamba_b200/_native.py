@@ -93,6 +93,7 @@ SIGNATURES = {
     "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p]),
     "vmscan_scan_order": (ctypes.c_int, [_i64, _D, ctypes.c_int, _p, _p]),
     "vmscan_device_status": (ctypes.c_int, [_p, ctypes.c_int]),
+    "vmscan_wait_timeout_selftest": (ctypes.c_int, [ctypes.c_uint32, _p]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -113,8 +114,41 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    _add_nvtx_ranges(lib)
     _lib = lib
     return lib
+
+
+# Entry points that launch kernels; each call is wrapped in an NVTX range of
+# its name so profiler timelines (nsys, ncu --nvtx) group the launches.
+TRACED = (
+    "vmscan_fwd", "vmscan_bwd", "vmscan_bwd_noalloc", "vmscan_conv1d_silu_fwd", "vmscan_conv1d_silu_bwd",
+    "vmscan_dt_softplus_fwd", "vmscan_dt_softplus_bwd",
+)
+
+
+def _add_nvtx_ranges(lib: ctypes.CDLL) -> None:
+    try:
+        import torch
+
+        if not torch.cuda.is_available():
+            return
+        push, pop = torch.cuda.nvtx.range_push, torch.cuda.nvtx.range_pop
+    except Exception:  # noqa: BLE001 - tracing is optional
+        return
+
+    def traced(name, fn):
+        def call(*args):
+            push(name)
+            try:
+                return fn(*args)
+            finally:
+                pop()
+
+        return call
+
+    for name in TRACED:
+        setattr(lib, name, traced(name, getattr(lib, name)))
 
 
 class VmscanError(RuntimeError):

@@ -492,6 +492,22 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
 
 }  // namespace
 
+// The failure path of every bounded wait, exercised on purpose: one warp
+// waits on an mbarrier that nothing arrives on, gives up after `tries`
+// polls, records VMSCAN_ERR_TIMEOUT in the sticky status and returns; no
+// fault, no trap, and the context stays usable.
+__global__ void wait_timeout_selftest_kernel(uint32_t tries, int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0u, &abort_flag, status, tries);
+}
+
 extern "C" {
 
 int vmscan_version(void) { return 100; }
@@ -806,6 +822,14 @@ int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d
   return vmscan_bwd(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy, sdy,
                     du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, scratch,
                     size_t(VMSCAN_NOALLOC_SCRATCH_BYTES), stream);
+}
+
+int vmscan_wait_timeout_selftest(uint32_t tries, vmscan_stream_t stream) {
+  if (tries == 0 || tries > kWaitLimit) return fail(VMSCAN_ERR_SHAPE, "tries must be in 1..%u", kWaitLimit);
+  int* st = status_ptr();
+  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(tries, st);
+  return check_launch();
 }
 
 int vmscan_device_status(vmscan_stream_t stream, int clear) {

@@ -259,9 +259,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // BACKOFF: sleep kBackoffNs between polls (a producer waiting for a stage to
 // drain would otherwise spend issue slots its consumers need).
 template <bool BACKOFF = false>
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
-  for (uint32_t it = 0; it < kWaitLimit; ++it) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          uint32_t limit = kWaitLimit) {
+  for (uint32_t it = 0; it < limit; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (BACKOFF) __nanosleep(kBackoffNs);

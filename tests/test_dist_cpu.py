@@ -5,6 +5,7 @@ is model-agnostic."""
 
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -159,3 +160,39 @@ def test_direction_sharding_matches_unsharded(tmp_path, k):
                 torch.testing.assert_close(rec["grads"][n], p.grad, rtol=1e-5, atol=1e-6, msg=n)
             else:
                 assert rec["grads"][n] is None, n
+
+
+def _failing_rank_worker(rank, world, port, out_path):
+    """Rank 1 dies between steps (before the gradient all-reduce of its next
+    step); rank 0's next collective must end with an error within the process
+    group's short timeout instead of waiting forever."""
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    model = train.wrap_data_parallel(_tiny_model())
+    opt = torch.optim.SGD(model.parameters(), lr=0.1)
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(2, 8, 8, 1, generator=g)
+    tgt = torch.randn(2, 4, 8, generator=g)
+    train.train_step(model, opt, x, tgt)  # one healthy step on both ranks
+    if rank == 1:
+        os._exit(0)  # the rank leaves between steps, with nothing in flight
+    t0 = time.monotonic()
+    try:
+        train.train_step(model, opt, x, tgt)
+        outcome = "completed"
+    except Exception as e:  # noqa: BLE001 - any backend error is the expected signal
+        outcome = f"raised {type(e).__name__}"
+    with open(out_path, "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.1f}")
+    os._exit(0)
+
+
+def test_lost_rank_surfaces_as_an_error_not_a_hang(tmp_path):
+    out_path = str(tmp_path / "outcome.txt")
+    mp.spawn(_failing_rank_worker, args=(2, _free_port(), out_path), nprocs=2, join=True)
+    outcome, seconds = open(out_path).read().rsplit(" ", 1)
+    assert outcome.startswith("raised"), outcome
+    assert float(seconds) < 60.0

@@ -44,3 +44,39 @@ def test_module_oracle_matches_reference(name):
     for k, g in rec["grads"].items():
         gg = got[k].grad if got[k].grad is not None else torch.zeros_like(got[k])
         close(gg.reshape(g.shape), g)
+
+
+def test_oracle_scan_passes_gradcheck():
+    """fp64 gradcheck of the restated sequential scan (with the gate): the
+    oracle's autograd gradients are the derivatives of its forward."""
+    import torch
+
+    from oracle import scan_ref
+
+    g = torch.Generator().manual_seed(0)
+    b, l, d = 1, 5, 3
+    u = torch.randn(b, l, d, generator=g, dtype=torch.float64)
+    delta = torch.nn.functional.softplus(torch.randn(b, l, d, generator=g, dtype=torch.float64))
+    A = -torch.rand(d, 16, generator=g, dtype=torch.float64) - 0.5
+    B = torch.randn(b, l, 16, generator=g, dtype=torch.float64)
+    C = torch.randn(b, l, 16, generator=g, dtype=torch.float64)
+    D = torch.randn(d, generator=g, dtype=torch.float64)
+    z = torch.randn(b, l, d, generator=g, dtype=torch.float64)
+    args = [t.requires_grad_(True) for t in (u, delta, A, B, C, D, z)]
+
+    def f(u, delta, A, B, C, D, z):
+        return scan_ref.selective_scan(u, delta, A, B, C, D) * scan_ref.silu(z)
+
+    assert torch.autograd.gradcheck(f, args, eps=1e-6, atol=1e-7, rtol=1e-6)
+
+
+def test_chunked_oracle_equals_sequential_in_fp32():
+    """The chunked restatement (mamba_fast.py) equals the sequential one."""
+    import torch
+
+    from oracle import scan_ref
+
+    inp = scan_ref.sweep_inputs(2, 77, 12, seed=3)
+    a = scan_ref.selective_scan(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"])
+    c = scan_ref.selective_scan_chunked(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"])
+    torch.testing.assert_close(c, a, rtol=1e-6, atol=1e-6)

@@ -228,3 +228,18 @@ def test_chunked_scan_matches_oracle_and_unchunked(b, l, dn, gated, dirname):
     assert st == 0, lib.vmscan_last_error()
     y2, _ = cuda_vjp(inp, gated, direction)
     torch.testing.assert_close(y2, y1.cpu(), rtol=1e-4, atol=1e-5)
+
+
+def test_bounded_wait_times_out_reports_and_context_survives():
+    """The failure path of the kernels' bounded waits, triggered on purpose: a
+    wait on a barrier that nothing arrives on gives up, the sticky status reads
+    VMSCAN_ERR_TIMEOUT once, and the context keeps working."""
+    lib = _native.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.vmscan_device_status(stream, 1) == 0
+    assert lib.vmscan_wait_timeout_selftest(2000, stream) == 0
+    assert lib.vmscan_device_status(stream, 1) == 9  # VMSCAN_ERR_TIMEOUT
+    assert lib.vmscan_device_status(stream, 1) == 0
+    inp = scan_ref.sweep_inputs(1, 40, 24, seed=11)
+    check_all(inp, True, tag="after timeout")
+    assert lib.vmscan_device_status(stream, 1) == 0
