@@ -156,15 +156,6 @@ __device__ __forceinline__ void tmem_fence_after_sync() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// Store 8 consecutive columns of this thread's lane.
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float v[8]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
-      : "memory");
-}
 
 // Store 16 consecutive columns of this thread's lane.  The 16-column TMEM
 // helpers carry no memory clobber: Tensor Memory is not reachable by ordinary
@@ -195,16 +186,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t r[16]) {
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// Issue a load of 8 consecutive columns.  The registers are not valid until
-// tmem_wait_ld8 on the same array, which ties them to the wait so the
-// compiler cannot read them earlier.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t r[8]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-      : "r"(taddr)
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_wait_ld16(uint32_t r[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
@@ -213,10 +194,6 @@ __device__ __forceinline__ void tmem_wait_ld16(uint32_t r[16]) {
                  "+r"(r[15]));
 }
 
-__device__ __forceinline__ void tmem_wait_ld8(uint32_t r[8]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7])::"memory");
-}
 
 // silu(z) = z / (1 + 2^(-z*log2 e))
 __device__ __forceinline__ float silu_f(float z) {
@@ -290,28 +267,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
-// 5-D tiled TMA store from shared memory (bulk-group completion).
-__device__ __forceinline__ void tma_store_5d(const CUtensorMap* map, const void* src, int c0, int c1, int c2,
-                                             int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-      : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-template <int N>
-__device__ __forceinline__ void bulk_wait() {
-  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Make generic-proxy shared-memory writes visible to the TMA (async proxy).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -327,21 +282,6 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 
 __device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
-// Four lanes of a quad each hold v[0..3] (partials for four consecutive scan
-// steps).  Returns, in lane q of the quad, the quad-wide sum for step q.
-__device__ __forceinline__ float quad_transpose_sum(const float v[4], int q) {
-  const bool hi2 = (q & 2) != 0;
-  float keep0 = hi2 ? v[2] : v[0];
-  float keep1 = hi2 ? v[3] : v[1];
-  const float send0 = hi2 ? v[0] : v[2];
-  const float send1 = hi2 ? v[1] : v[3];
-  keep0 += __shfl_xor_sync(0xffffffffu, send0, 2);
-  keep1 += __shfl_xor_sync(0xffffffffu, send1, 2);
-  const bool hi1 = (q & 1) != 0;
-  const float keep = hi1 ? keep1 : keep0;
-  const float send = hi1 ? keep0 : keep1;
-  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
-}
 
 // First 1024-byte aligned float of the dynamic shared-memory window.  The
 // offset is added to the shared array itself (not through an integer cast),
