@@ -41,14 +41,15 @@ WORKLOAD = dict(batch=64, seqlen=4096, d_inner=1536)
 CPU_SAMPLE = dict(batch=1, seqlen=512, d_inner=1536)
 
 
-def fwd_bytes(b, l, d, n=N_STATE):
-    """read u, delta, z, B, C, A, D; write y."""
-    return 4 * (4 * b * l * d + 2 * b * l * n + d * n + d)
+def fwd_bytes(b, l, d, n=N_STATE, es=4):
+    """read u, delta, z, B, C, A, D; write y (sequence tensors of es bytes an
+    element, A and D fp32)."""
+    return es * (4 * b * l * d + 2 * b * l * n) + 4 * (d * n + d)
 
 
-def bwd_bytes(b, l, d, n=N_STATE):
+def bwd_bytes(b, l, d, n=N_STATE, es=4):
     """read u, delta, z, dy, B, C, A, D; write du, ddelta, dz, dB, dC, dA, dD."""
-    return 4 * (7 * b * l * d + 4 * b * l * n + 2 * d * n + 2 * d)
+    return es * (7 * b * l * d + 4 * b * l * n) + 4 * (2 * d * n + 2 * d)
 
 
 def measured_peaks():
@@ -140,24 +141,32 @@ def make_inputs(b, l, d, device, seed):
 
 
 class AbiScan:
-    """Preallocated fwd + VJP through the C ABI (no allocation in the timed loop)."""
+    """Preallocated fwd + VJP through the C ABI (no allocation in the timed loop).
 
-    def __init__(self, t):
+    bf16=True casts the sequence tensors (u, delta, z, B, C, dy) to bf16 and
+    calls vmscan_fwd_bf16 / vmscan_bwd_bf16 (A, D, dA, dD, checkpoints fp32)."""
+
+    def __init__(self, t, bf16=False):
         import torch
 
         from mlx_vision_mamba_b200 import _native
 
         self.lib = lib = _native.load()
+        if bf16:
+            t = {k: (v.to(torch.bfloat16) if k not in ("A", "D") else v) for k, v in t.items()}
+        self.fwd_fn = lib.vmscan_fwd_bf16 if bf16 else lib.vmscan_fwd
+        self.bwd_fn = lib.vmscan_bwd_bf16 if bf16 else lib.vmscan_bwd
         self.t = t
         b, l, d = t["u"].shape
         self.shape = (b, l, d)
         dev = t["u"].device
+        sd = t["u"].dtype
         self.y = torch.empty_like(t["u"])
         self.ck = torch.empty(lib.vmscan_ckpt_elems(b, l, d, N_STATE, None), device=dev)
         self.g = {k: torch.empty_like(t["u"]) for k in ("du", "ddelta", "dz")}
         self.g["dA"] = torch.empty(d, N_STATE, device=dev)
-        self.g["dB"] = torch.empty(b, l, N_STATE, device=dev)
-        self.g["dC"] = torch.empty(b, l, N_STATE, device=dev)
+        self.g["dB"] = torch.empty(b, l, N_STATE, device=dev, dtype=sd)
+        self.g["dC"] = torch.empty(b, l, N_STATE, device=dev, dtype=sd)
         self.g["dD"] = torch.empty(d, device=dev)
         self.fws_n = lib.vmscan_fwd_workspace_bytes(b, l, d, N_STATE, None)
         self.fws = torch.empty(max(self.fws_n, 16), dtype=torch.uint8, device=dev)
@@ -173,7 +182,7 @@ class AbiScan:
     def fwd(self, stream):
         t, S = self.t, self._S
         b, l, d = self.shape
-        st = self.lib.vmscan_fwd(b, l, d, N_STATE, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(),
+        st = self.fwd_fn(b, l, d, N_STATE, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(),
                                  S(t["delta"]), t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(),
                                  S(t["C"]), t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), self.y.data_ptr(),
                                  S(self.y), self.ck.data_ptr(), None, self.fws_ptr, self.fws_n, stream)
@@ -183,7 +192,7 @@ class AbiScan:
     def bwd(self, stream):
         t, g, S = self.t, self.g, self._S
         b, l, d = self.shape
-        st = self.lib.vmscan_bwd(
+        st = self.bwd_fn(
             b, l, d, N_STATE, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
             t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]), t["D"].data_ptr(),
             t["z"].data_ptr(), S(t["z"]), self.ck.data_ptr(), t["dy"].data_ptr(), S(t["dy"]),
@@ -274,6 +283,8 @@ def main():
                     help="with --encoder: data parallel, or the scan directions split over the ranks")
     ap.add_argument("--sweep", action="store_true",
                     help="time forward and VJP separately on the 12 op-sweep points and print a table")
+    ap.add_argument("--io", choices=["f32", "bf16"], default="f32",
+                    help="with --sweep: sequence tensors in fp32 (the reference's dtype) or bf16")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
@@ -285,7 +296,7 @@ def main():
         profile_model(args.warmup)
         return
     if args.sweep:
-        run_sweep(max(args.steps, 20), max(args.warmup, 3))
+        run_sweep(max(args.steps, 20), max(args.warmup, 3), bf16=args.io == "bf16")
         return
 
     import torch
@@ -365,6 +376,9 @@ def main():
     # ---- BASELINE config 1 shape: the reference's only published scan numbers ----
     cfg1 = time_config1(dev, stream) if rank == 0 else None
 
+    # ---- the same workload through the bf16 I/O entry points (not the metric) ----
+    bf16_io = time_bf16_io(t, dev, stream, K, args.warmup) if rank == 0 else None
+
     # ---- end to end through the public API with host buffers ----
     e2e = None
     if not args.no_e2e:
@@ -417,6 +431,7 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "config1_scan": cfg1,
+            "bf16_io": bf16_io,
             "cpu_baseline": base,
             "vision_mamba_2d_train": model_line,
         }
@@ -519,10 +534,42 @@ def time_config1(dev, stream, iters=50):
             "reference_published_on": "Apple M5 Pro, MLX 0.31, metal_fused scan (README.md:25)"}
 
 
+def time_bf16_io(t, dev, stream, K, warmup):
+    """The headline workload with the sequence tensors in bf16
+    (vmscan_fwd_bf16 / vmscan_bwd_bf16; fp32 arithmetic and state).  Reported
+    beside the metric, which stays fp32 like the reference."""
+    import torch
+
+    b, l, d = t["u"].shape
+    runner = AbiScan(t, bf16=True)
+    st = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        runner.fwd(stream)
+        runner.bwd(stream)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    torch.cuda.synchronize()
+    for i in range(K):
+        ev[i][0].record(st)
+        runner.fwd(stream)
+        ev[i][1].record(st)
+        runner.bwd(stream)
+        ev[i][2].record(st)
+    torch.cuda.synchronize()
+    f = statistics.mean(ev[i][0].elapsed_time(ev[i][1]) for i in range(K))
+    bw = statistics.mean(ev[i][1].elapsed_time(ev[i][2]) for i in range(K))
+    fb, bb = fwd_bytes(b, l, d, es=2), bwd_bytes(b, l, d, es=2)
+    peak, _ = measured_peaks()
+    del runner
+    torch.cuda.empty_cache()
+    return {"api": "vmscan_fwd_bf16 + vmscan_bwd_bf16", "fwd_ms": f, "bwd_ms": bw, "ms_per_step": f + bw,
+            "fwd_gbs": fb / f / 1e6, "bwd_gbs": bb / bw / 1e6, "fwd_frac": fb / f / 1e6 / peak,
+            "bwd_frac": bb / bw / 1e6 / peak, "algorithmic_bytes_per_step": fb + bb}
+
+
 SWEEP = [(b, l, d) for b in (8, 64) for l in (196, 1024, 4096) for d in (768, 1536)]
 
 
-def run_sweep(iters, warmup):
+def run_sweep(iters, warmup, bf16=False):
     """The op sweep (batch x L x d_inner = {8, 64} x {196, 1024, 4096} x {768,
     1536}, gated, seeded inputs with the sweep's distributions): forward and
     VJP through the C ABI timed separately with CUDA events, median of `iters`
@@ -542,8 +589,9 @@ def run_sweep(iters, warmup):
     rows = []
     for b, l, d in SWEEP:
         t = make_inputs(b, l, d, dev, seed=7)
-        runner = AbiScan(t)
-        in_bytes = 4 * 4 * b * l * d
+        runner = AbiScan(t, bf16=bf16)
+        es = 2 if bf16 else 4
+        in_bytes = es * 4 * b * l * d
         need_flush = in_bytes < 2 * 126 * 1024 * 1024
         res = {}
         for name, fn in (("fwd", runner.fwd), ("bwd", runner.bwd)):
@@ -560,8 +608,8 @@ def run_sweep(iters, warmup):
                 e1.synchronize()
                 times.append(e0.elapsed_time(e1))
             res[name] = statistics.median(times)
-        fb, bb = fwd_bytes(b, l, d), bwd_bytes(b, l, d)
-        row = {"batch": b, "seqlen": l, "d_inner": d, "fwd_ms": res["fwd"], "bwd_ms": res["bwd"],
+        fb, bb = fwd_bytes(b, l, d, es=es), bwd_bytes(b, l, d, es=es)
+        row = {"io": "bf16" if bf16 else "f32", "batch": b, "seqlen": l, "d_inner": d, "fwd_ms": res["fwd"], "bwd_ms": res["bwd"],
                "fwd_gbs": fb / res["fwd"] / 1e6, "bwd_gbs": bb / res["bwd"] / 1e6,
                "fwd_frac": fb / res["fwd"] / 1e6 / peak, "bwd_frac": bb / res["bwd"] / 1e6 / peak,
                "l2_flush": need_flush, "peak": peak, "peak_source": peak_kind}

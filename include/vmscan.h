@@ -169,6 +169,52 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
                vmscan_stream_t stream);
 
 /*
+ * bf16 I/O variants of vmscan_fwd / vmscan_bwd.  The sequence tensors
+ * (u, delta, B, C, z, y; dy and du, ddelta, dB, dC, dz) are bf16, passed as
+ * void* so that the header needs no CUDA include; A, D, dA, dD and the
+ * checkpoints stay fp32, and every operation inside the kernels runs in fp32
+ * (loads widen bf16 to fp32, stores round to nearest even).  Strides must be
+ * multiples of 8 elements (16 bytes).  Checkpoint and workspace sizes are the
+ * fp32 calls' (vmscan_ckpt_elems, vmscan_fwd_workspace_bytes,
+ * vmscan_bwd_workspace_bytes).  The reference computes in fp32 only; these
+ * halve the scan's HBM traffic for a caller that keeps activations in bf16.
+ */
+int vmscan_fwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                    const void* u, vmscan_strides su,
+                    const void* delta, vmscan_strides sdelta,
+                    const float* A,
+                    const void* B, vmscan_strides sB,
+                    const void* C, vmscan_strides sC,
+                    const float* D,
+                    const void* z, vmscan_strides sz,
+                    void* y, vmscan_strides sy,
+                    float* ckpt,
+                    const vmscan_direction* dir,
+                    void* workspace, size_t workspace_bytes,
+                    vmscan_stream_t stream);
+
+int vmscan_bwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                    const void* u, vmscan_strides su,
+                    const void* delta, vmscan_strides sdelta,
+                    const float* A,
+                    const void* B, vmscan_strides sB,
+                    const void* C, vmscan_strides sC,
+                    const float* D,
+                    const void* z, vmscan_strides sz,
+                    const float* ckpt,
+                    const void* dy, vmscan_strides sdy,
+                    void* du, vmscan_strides sdu,
+                    void* ddelta, vmscan_strides sddelta,
+                    float* dA,
+                    void* dB, vmscan_strides sdB,
+                    void* dC, vmscan_strides sdC,
+                    float* dD,
+                    void* dz, vmscan_strides sdz,
+                    const vmscan_direction* dir,
+                    void* workspace, size_t workspace_bytes,
+                    vmscan_stream_t stream);
+
+/*
  * Size of the device array behind vmscan_bwd_noalloc: 32 MiB, reserved on
  * every GPU that loads libvmscan.so, for as long as the library stays loaded.
  */

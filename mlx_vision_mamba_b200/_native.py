@@ -52,8 +52,27 @@ SIGNATURES = {
         ctypes.c_int,
         [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _D, _p, _sz, _p],
     ),
+    "vmscan_fwd_bf16": (
+        ctypes.c_int,
+        [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _D, _p, _sz, _p],
+    ),
     "vmscan_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _D, ctypes.c_int]),
     "vmscan_bwd": (
+        ctypes.c_int,
+        [
+            _i64, _i64, _i64, _i64,
+            _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S,  # u delta A B C D z
+            _p,  # ckpt
+            _p, _S,  # dy
+            _p, _S, _p, _S,  # du ddelta
+            _p,  # dA
+            _p, _S, _p, _S,  # dB dC
+            _p,  # dD
+            _p, _S,  # dz
+            _D, _p, _sz, _p,
+        ],
+    ),
+    "vmscan_bwd_bf16": (
         ctypes.c_int,
         [
             _i64, _i64, _i64, _i64,
@@ -122,7 +141,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 # Entry points that launch kernels; each call is wrapped in an NVTX range of
 # its name so profiler timelines (nsys, ncu --nvtx) group the launches.
 TRACED = (
-    "vmscan_fwd", "vmscan_bwd", "vmscan_bwd_noalloc", "vmscan_conv1d_silu_fwd", "vmscan_conv1d_silu_bwd",
+    "vmscan_fwd", "vmscan_bwd", "vmscan_fwd_bf16", "vmscan_bwd_bf16", "vmscan_bwd_noalloc", "vmscan_conv1d_silu_fwd", "vmscan_conv1d_silu_bwd",
     "vmscan_dt_softplus_fwd", "vmscan_dt_softplus_bwd",
 )
 

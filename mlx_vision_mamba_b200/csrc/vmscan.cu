@@ -195,15 +195,17 @@ int seq_stride32(const char* what, vmscan_strides s, int64_t seqlen, int& out) {
   return VMSCAN_OK;
 }
 
-// Tensor map of a (batch, seq, inner) fp32 view seen in scan order:
-// dims {inner, scan0, scan1, scan2, batch}, box {box_inner, box...}.
+// Tensor map of a (batch, seq, inner) view of esize-byte elements (4: fp32,
+// 2: bf16) seen in scan order: dims {inner, scan0, scan1, scan2, batch}, box
+// {box_inner, box...}.  Strides must be whole 16-byte multiples.
 int encode_map(CUtensorMap* m, const char* what, const void* ptr, int64_t inner, int box_inner,
-               vmscan_strides st, const ScanGeom& g) {
+               vmscan_strides st, const ScanGeom& g, int esize) {
   if (ptr == nullptr) return fail(VMSCAN_ERR_NULL, "%s is NULL", what);
   if (!aligned16(ptr)) return fail(VMSCAN_ERR_ALIGN, "%s base %p is not 16-byte aligned", what, ptr);
-  if ((g.seqlen > 1 && (st.seq <= 0 || st.seq % 4 != 0)) || (g.batch > 1 && (st.batch <= 0 || st.batch % 4 != 0)))
-    return fail(VMSCAN_ERR_ALIGN, "%s strides {batch %lld, seq %lld} must be positive multiples of 4", what,
-                (long long)st.batch, (long long)st.seq);
+  const int64_t q = 16 / esize;
+  if ((g.seqlen > 1 && (st.seq <= 0 || st.seq % q != 0)) || (g.batch > 1 && (st.batch <= 0 || st.batch % q != 0)))
+    return fail(VMSCAN_ERR_ALIGN, "%s strides {batch %lld, seq %lld} must be positive multiples of %lld", what,
+                (long long)st.batch, (long long)st.seq, (long long)q);
   auto fn = encode_fn();
   if (fn == nullptr) return fail(VMSCAN_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[5];
@@ -211,11 +213,11 @@ int encode_map(CUtensorMap* m, const char* what, const void* ptr, int64_t inner,
   dims[0] = cuuint64_t(inner);
   for (int i = 0; i < 3; ++i) {
     dims[1 + i] = cuuint64_t(g.size[i]);
-    int64_t s = (i < g.nsd && g.size[i] > 1) ? g.tstride[i] * st.seq * 4 : 16;
+    int64_t s = (i < g.nsd && g.size[i] > 1) ? g.tstride[i] * st.seq * esize : 16;
     strides[i] = cuuint64_t(s);
   }
   dims[4] = cuuint64_t(g.batch);
-  strides[3] = cuuint64_t(g.batch > 1 ? st.batch * 4 : 16);
+  strides[3] = cuuint64_t(g.batch > 1 ? st.batch * esize : 16);
   for (int i = 0; i < 4; ++i)
     if (strides[i] == 0 || strides[i] % 16 != 0 || strides[i] >= (cuuint64_t(1) << 40))
       return fail(VMSCAN_ERR_ALIGN, "%s byte stride %llu of dim %d is invalid", what, (unsigned long long)strides[i],
@@ -224,7 +226,8 @@ int encode_map(CUtensorMap* m, const char* what, const void* ptr, int64_t inner,
   box_extent(g, box3);
   cuuint32_t box[5] = {cuuint32_t(box_inner), box3[0], box3[1], box3[2], 1u};
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<void*>(ptr), dims, strides, box, estr,
+  const CUtensorMapDataType dtype = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = fn(m, dtype, 5, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -329,12 +332,12 @@ ChunkPlan fwd_chunk_plan(const ScanGeom& g) {
 
 size_t fwd_chunk_bytes(const ScanGeom& g) { return fwd_chunk_plan(g).bytes; }
 
-template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY>
+template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY>
 int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-                 const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
+                 const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
                  const ChunkArgs& ch, int nz, const ScanGeom& g, cudaStream_t stream) {
-  using Cfg = FwdCfg<kFwdNCW>;
-  auto kern = scan_fwd_kernel<kFwdNCW, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY>;
+  using Cfg = FwdCfg<kFwdNCW, T>;
+  auto kern = scan_fwd_kernel<kFwdNCW, T, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_fwd_kernel) failed");
   int* st = status_ptr();
@@ -349,15 +352,15 @@ int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
 // Forward scan, chunked over L when the grid would leave most of the GPU idle
 // and `ws` (fwd_chunk_plan(g).bytes) is given: a carry pass over chunks
 // 0 .. nc-2, the carry chain, then the main pass over all chunks.
-template <bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
+template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
 int run_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-              const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
+              const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
               void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
   const ChunkPlan plan = fwd_chunk_plan(g);
   if (plan.nc == 1 || ws == nullptr || ws_bytes < plan.bytes) {
     const ChunkArgs one{g.nboxes, 1, nullptr, nullptr, nullptr};
-    return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, one, 1, g,
-                                                             stream);
+    return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, one, 1, g,
+                                                                stream);
   }
   const size_t per = size_t(g.batch) * plan.nc * g.d_inner;
   char* w = static_cast<char*>(ws);
@@ -365,48 +368,51 @@ int run_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& 
   float* h_start = reinterpret_cast<float*>(w + align256(per * NS * 4));
   float* carry_s = reinterpret_cast<float*>(w + 2 * align256(per * NS * 4));
   const ChunkArgs ch{plan.bpc, plan.nc, h_start, carry_h, carry_s};
-  VM_TRY((launch_fwd_t<false, false, false, REV, true>(mu, mdt, mz, mB, mC, nullptr, vmscan_strides{0, 0}, A, D,
-                                                      nullptr, ch, plan.nc - 1, g, stream)));
+  VM_TRY((launch_fwd_t<T, false, false, false, REV, true>(mu, mdt, mz, mB, mC, nullptr, vmscan_strides{0, 0}, A,
+                                                         D, nullptr, ch, plan.nc - 1, g, stream)));
   const int64_t n = int64_t(g.batch) * g.d_inner * NS;
   carry_fwd_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(A, carry_h, carry_s, h_start, g.batch, plan.nc,
                                                                   g.d_inner);
   VM_TRY(check_launch());
-  return launch_fwd_t<HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ch, plan.nc, g,
-                                                           stream);
+  return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ch, plan.nc,
+                                                              g, stream);
 }
 
-template <bool HAS_Z, bool SAVE_CK, bool STORE_Y>
+template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y>
 int launch_fwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-               const CUtensorMap& mC, float* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
+               const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
                void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
   if (g.reverse)
-    return run_fwd_t<HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g, stream);
-  return run_fwd_t<HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g, stream);
+    return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g,
+                                                       stream);
+  return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g,
+                                                      stream);
 }
 
+template <typename T>
 struct BwdOut {
-  float* du;
+  T* du;
   vmscan_strides sdu;
-  float* ddt;
+  T* ddt;
   vmscan_strides sddt;
-  float* dz;
+  T* dz;
   vmscan_strides sdz;
 };
 
-template <bool HAS_Z, bool REV>
+template <typename T, bool HAS_Z, bool REV>
 int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
-                 const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
+                 const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut<T>& o, const float* A, const float* D,
                  const float* ckpt, float* wpart, float* wA, float* wD, const BwdWorkspace& wl, char* ws,
                  const ScanGeom& g, cudaStream_t stream) {
-  using Cfg = BwdCfg;
+  using Cfg = BwdCfg<T>;
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
   const unsigned ndt = unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT);
   float* p_in = nullptr;
   if (wl.nc > 1) {
     // adjoint carries of the chunks, then their chain
-    using CC = BwdCarryCfg;
-    auto ck = scan_bwd_carry_kernel<HAS_Z, REV>;
+    using CC = BwdCarryCfg<T>;
+    auto ck = scan_bwd_carry_kernel<T, HAS_Z, REV>;
     if (cudaFuncSetAttribute(ck, cudaFuncAttributeMaxDynamicSharedMemorySize, int(CC::SMEM_BYTES)) != cudaSuccess)
       return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_carry_kernel) failed");
     float* p_local = reinterpret_cast<float*>(ws + wl.p_local);
@@ -420,7 +426,7 @@ int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
                                                                     g.d_inner);
     VM_TRY(check_launch());
   }
-  auto kern = scan_bwd_kernel<HAS_Z, REV>;
+  auto kern = scan_bwd_kernel<T, HAS_Z, REV>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_kernel) failed");
   int sdus = 0, sdts = 0, sdzs = 0;
@@ -435,20 +441,123 @@ int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
   return check_launch();
 }
 
-template <bool HAS_Z>
+template <typename T, bool HAS_Z>
 int launch_bwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mdy,
-               const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut& o, const float* A, const float* D,
+               const CUtensorMap& mB, const CUtensorMap& mC, const BwdOut<T>& o, const float* A, const float* D,
                const float* ckpt, float* wpart, float* wA, float* wD, const BwdWorkspace& wl, char* ws,
                const ScanGeom& g, cudaStream_t stream) {
   if (g.reverse)
-    return launch_bwd_t<HAS_Z, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
-  return launch_bwd_t<HAS_Z, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
+    return launch_bwd_t<T, HAS_Z, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
+  return launch_bwd_t<T, HAS_Z, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ckpt, wpart, wA, wD, wl, ws, g, stream);
 }
 
 int check_common(int64_t d_state, const float* A, const float* D) {
   if (d_state != NS) return VMSCAN_ERR_DSTATE;
   if (A == nullptr || D == nullptr) return VMSCAN_ERR_NULL;
   return VMSCAN_OK;
+}
+
+// Forward entry (fp32 or bf16 sequence tensors; A, D and the checkpoints are fp32).
+template <typename T>
+int fwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const T* u, vmscan_strides su,
+             const T* delta, vmscan_strides sdelta, const float* A, const T* B, vmscan_strides sB, const T* C,
+             vmscan_strides sC, const float* D, const T* z, vmscan_strides sz, T* y, vmscan_strides sy,
+             float* ckpt, const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
+             vmscan_stream_t stream) {
+  constexpr int ES = int(sizeof(T));
+  VM_TRY(check_common(d_state, A, D));
+  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
+  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
+  VM_TRY(ensure_context(u));
+  using Cfg = FwdCfg<kFwdNCW, T>;
+  CUtensorMap mu, mdt, mz, mB, mC;
+  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g, ES));
+  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g, ES));
+  if (z != nullptr) {
+    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g, ES));
+  } else {
+    mz = mu;
+  }
+  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g, ES));
+  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g, ES));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool hz = z != nullptr, ck = ckpt != nullptr;
+  void* ws = workspace;
+  const size_t wb = workspace_bytes;
+  if (ws != nullptr && !aligned16(ws)) return fail(VMSCAN_ERR_ALIGN, "workspace is not 16-byte aligned");
+  if (hz && ck) return launch_fwd<T, true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  if (hz) return launch_fwd<T, true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  if (ck) return launch_fwd<T, false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  return launch_fwd<T, false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+}
+
+// VJP entry (fp32 or bf16 sequence tensors and their gradients; A, D, dA,
+// dD and the checkpoints are fp32).
+template <typename T>
+int bwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const T* u, vmscan_strides su,
+             const T* delta, vmscan_strides sdelta, const float* A, const T* B, vmscan_strides sB, const T* C,
+             vmscan_strides sC, const float* D, const T* z, vmscan_strides sz, const float* ckpt, const T* dy,
+             vmscan_strides sdy, T* du, vmscan_strides sdu, T* ddelta, vmscan_strides sddelta, float* dA, T* dB,
+             vmscan_strides sdB, T* dC, vmscan_strides sdC, float* dD, T* dz, vmscan_strides sdz,
+             const vmscan_direction* dir, void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
+  constexpr int ES = int(sizeof(T));
+  VM_TRY(check_common(d_state, A, D));
+  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || dy == nullptr || du == nullptr ||
+      ddelta == nullptr || dA == nullptr || dB == nullptr || dC == nullptr || dD == nullptr)
+    return VMSCAN_ERR_NULL;
+  if (z != nullptr && dz == nullptr) return VMSCAN_ERR_NULL;
+  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
+  ScanGeom g;
+  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
+  VM_TRY(ensure_context(u));
+  using Cfg = BwdCfg<T>;
+  const int ndt = int((d_inner + Cfg::DT - 1) / Cfg::DT);
+  const BwdWorkspace wl = bwd_layout(g, ndt, ckpt == nullptr);
+  if (workspace == nullptr || workspace_bytes < wl.total || !aligned16(workspace)) return VMSCAN_ERR_WORKSPACE;
+  char* ws = static_cast<char*>(workspace);
+  float* wpart = reinterpret_cast<float*>(ws + wl.part);
+  float* wA = reinterpret_cast<float*>(ws + wl.wA);
+  float* wD = reinterpret_cast<float*>(ws + wl.wD);
+  CUtensorMap mu, mdt, mz, mdy, mB, mC;
+  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g, ES));
+  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g, ES));
+  if (z != nullptr) {
+    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g, ES));
+  } else {
+    mz = mu;
+  }
+  VM_TRY(encode_map(&mdy, "dy", dy, d_inner, Cfg::DT, sdy, g, ES));
+  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g, ES));
+  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g, ES));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float* ck = ckpt;
+  if (ck == nullptr) {
+    // Rebuild the checkpoints (the reference VJP also recomputes the forward),
+    // chunked over L like vmscan_fwd; the forward gets its own maps.
+    using FC = FwdCfg<kFwdNCW, T>;
+    CUtensorMap fu, fdt, fB;
+    VM_TRY(encode_map(&fu, "u", u, d_inner, FC::DT, su, g, ES));
+    VM_TRY(encode_map(&fdt, "delta", delta, d_inner, FC::DT, sdelta, g, ES));
+    VM_TRY(encode_map(&fB, "B", B, NS, NS, sB, g, ES));
+    float* ckw = reinterpret_cast<float*>(ws + wl.ck);
+    VM_TRY((launch_fwd<T, false, true, false>(fu, fdt, fu, fB, fB, static_cast<T*>(nullptr), vmscan_strides{0, 0}, A, D, ckw,
+                                           ws + wl.fws, wl.total - wl.fws, g, s)));
+    ck = ckw;
+  }
+  const BwdOut<T> o{du, sdu, ddelta, sddelta, dz, sdz};
+  if (z != nullptr) {
+    VM_TRY((launch_bwd<T, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s)));
+  } else {
+    VM_TRY((launch_bwd<T, false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s)));
+  }
+  reduce_dbc_kernel<T><<<dim3(unsigned(g.nboxes), unsigned(g.batch)), TMAX * kPartRow, 0, s>>>(
+      wpart, dB, sdB.batch, sdB.seq, dC, sdC.batch, sdC.seq, g, ndt);
+  VM_TRY(check_launch());
+  const int nA = int(d_inner * NS);
+  reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch) * wl.nc, int(d_inner));
+  return check_launch();
 }
 
 }  // namespace
@@ -547,32 +656,20 @@ int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
                const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz, float* y,
                vmscan_strides sy, float* ckpt, const vmscan_direction* dir, void* workspace,
                size_t workspace_bytes, vmscan_stream_t stream) {
-  VM_TRY(check_common(d_state, A, D));
-  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
-  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
-  ScanGeom g;
-  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
-  VM_TRY(ensure_context(u));
-  using Cfg = FwdCfg<kFwdNCW>;
-  CUtensorMap mu, mdt, mz, mB, mC;
-  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g));
-  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g));
-  if (z != nullptr) {
-    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g));
-  } else {
-    mz = mu;
-  }
-  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g));
-  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g));
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool hz = z != nullptr, ck = ckpt != nullptr;
-  void* ws = workspace;
-  const size_t wb = workspace_bytes;
-  if (ws != nullptr && !aligned16(ws)) return fail(VMSCAN_ERR_ALIGN, "workspace is not 16-byte aligned");
-  if (hz && ck) return launch_fwd<true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  if (hz) return launch_fwd<true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  if (ck) return launch_fwd<false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  return launch_fwd<false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  return fwd_impl<float>(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, y, sy,
+                         ckpt, dir, workspace, workspace_bytes, stream);
+}
+
+int vmscan_fwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const void* u,
+                    vmscan_strides su, const void* delta, vmscan_strides sdelta, const float* A, const void* B,
+                    vmscan_strides sB, const void* C, vmscan_strides sC, const float* D, const void* z,
+                    vmscan_strides sz, void* y, vmscan_strides sy, float* ckpt, const vmscan_direction* dir,
+                    void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
+  using T = __nv_bfloat16;
+  return fwd_impl<T>(batch, seqlen, d_inner, d_state, static_cast<const T*>(u), su, static_cast<const T*>(delta),
+                     sdelta, A, static_cast<const T*>(B), sB, static_cast<const T*>(C), sC, D,
+                     static_cast<const T*>(z), sz, static_cast<T*>(y), sy, ckpt, dir, workspace, workspace_bytes,
+                     stream);
 }
 
 int64_t vmscan_fwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
@@ -590,7 +687,7 @@ int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inne
   ScanGeom g;
   const int rc = make_geom(batch, seqlen, d_inner, dir, g);
   if (rc != VMSCAN_OK) return -rc;
-  const int ndt = int((d_inner + BwdCfg::DT - 1) / BwdCfg::DT);
+  const int ndt = int((d_inner + BwdCfg<>::DT - 1) / BwdCfg<>::DT);
   return int64_t(bwd_layout(g, ndt, recompute_ckpt != 0).total);
 }
 
@@ -601,61 +698,24 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
                float* ddelta, vmscan_strides sddelta, float* dA, float* dB, vmscan_strides sdB, float* dC,
                vmscan_strides sdC, float* dD, float* dz, vmscan_strides sdz, const vmscan_direction* dir,
                void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
-  VM_TRY(check_common(d_state, A, D));
-  if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || dy == nullptr || du == nullptr ||
-      ddelta == nullptr || dA == nullptr || dB == nullptr || dC == nullptr || dD == nullptr)
-    return VMSCAN_ERR_NULL;
-  if (z != nullptr && dz == nullptr) return VMSCAN_ERR_NULL;
-  if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
-  ScanGeom g;
-  VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
-  VM_TRY(ensure_context(u));
-  using Cfg = BwdCfg;
-  const int ndt = int((d_inner + Cfg::DT - 1) / Cfg::DT);
-  const BwdWorkspace wl = bwd_layout(g, ndt, ckpt == nullptr);
-  if (workspace == nullptr || workspace_bytes < wl.total || !aligned16(workspace)) return VMSCAN_ERR_WORKSPACE;
-  char* ws = static_cast<char*>(workspace);
-  float* wpart = reinterpret_cast<float*>(ws + wl.part);
-  float* wA = reinterpret_cast<float*>(ws + wl.wA);
-  float* wD = reinterpret_cast<float*>(ws + wl.wD);
-  CUtensorMap mu, mdt, mz, mdy, mB, mC;
-  VM_TRY(encode_map(&mu, "u", u, d_inner, Cfg::DT, su, g));
-  VM_TRY(encode_map(&mdt, "delta", delta, d_inner, Cfg::DT, sdelta, g));
-  if (z != nullptr) {
-    VM_TRY(encode_map(&mz, "z", z, d_inner, Cfg::DT, sz, g));
-  } else {
-    mz = mu;
-  }
-  VM_TRY(encode_map(&mdy, "dy", dy, d_inner, Cfg::DT, sdy, g));
-  VM_TRY(encode_map(&mB, "B", B, NS, NS, sB, g));
-  VM_TRY(encode_map(&mC, "C", C, NS, NS, sC, g));
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const float* ck = ckpt;
-  if (ck == nullptr) {
-    // Rebuild the checkpoints (the reference VJP also recomputes the forward),
-    // chunked over L like vmscan_fwd; the forward gets its own maps.
-    using FC = FwdCfg<kFwdNCW>;
-    CUtensorMap fu, fdt, fB;
-    VM_TRY(encode_map(&fu, "u", u, d_inner, FC::DT, su, g));
-    VM_TRY(encode_map(&fdt, "delta", delta, d_inner, FC::DT, sdelta, g));
-    VM_TRY(encode_map(&fB, "B", B, NS, NS, sB, g));
-    float* ckw = reinterpret_cast<float*>(ws + wl.ck);
-    VM_TRY((launch_fwd<false, true, false>(fu, fdt, fu, fB, fB, nullptr, vmscan_strides{0, 0}, A, D, ckw,
-                                           ws + wl.fws, wl.total - wl.fws, g, s)));
-    ck = ckw;
-  }
-  const BwdOut o{du, sdu, ddelta, sddelta, dz, sdz};
-  if (z != nullptr) {
-    VM_TRY(launch_bwd<true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s));
-  } else {
-    VM_TRY(launch_bwd<false>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s));
-  }
-  reduce_dbc_kernel<<<dim3(unsigned(g.nboxes), unsigned(g.batch)), TMAX * kPartRow, 0, s>>>(
-      wpart, dB, sdB.batch, sdB.seq, dC, sdC.batch, sdC.seq, g, ndt);
-  VM_TRY(check_launch());
-  const int nA = int(d_inner * NS);
-  reduce_dad_kernel<<<unsigned((nA + 255) / 256), 256, 0, s>>>(wA, wD, dA, dD, int(batch) * wl.nc, int(d_inner));
-  return check_launch();
+  return bwd_impl<float>(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy,
+                         sdy, du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, workspace,
+                         workspace_bytes, stream);
+}
+
+int vmscan_bwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const void* u,
+                    vmscan_strides su, const void* delta, vmscan_strides sdelta, const float* A, const void* B,
+                    vmscan_strides sB, const void* C, vmscan_strides sC, const float* D, const void* z,
+                    vmscan_strides sz, const float* ckpt, const void* dy, vmscan_strides sdy, void* du,
+                    vmscan_strides sdu, void* ddelta, vmscan_strides sddelta, float* dA, void* dB,
+                    vmscan_strides sdB, void* dC, vmscan_strides sdC, float* dD, void* dz, vmscan_strides sdz,
+                    const vmscan_direction* dir, void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
+  using T = __nv_bfloat16;
+  return bwd_impl<T>(batch, seqlen, d_inner, d_state, static_cast<const T*>(u), su, static_cast<const T*>(delta),
+                     sdelta, A, static_cast<const T*>(B), sB, static_cast<const T*>(C), sC, D,
+                     static_cast<const T*>(z), sz, ckpt, static_cast<const T*>(dy), sdy, static_cast<T*>(du), sdu,
+                     static_cast<T*>(ddelta), sddelta, dA, static_cast<T*>(dB), sdB, static_cast<T*>(dC), sdC, dD,
+                     static_cast<T*>(dz), sdz, dir, workspace, workspace_bytes, stream);
 }
 
 int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,

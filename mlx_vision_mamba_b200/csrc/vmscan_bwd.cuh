@@ -43,6 +43,9 @@
 
 namespace vmscan {
 
+// T: element type of the sequence tensors (float, or __nv_bfloat16 for the
+// bf16 I/O variant).  Stage offsets are in bytes.
+template <typename T = float>
 struct BwdCfg {
   static constexpr int NCW = 4;            // one warpgroup: the 4 TMEM lane quarters
   static constexpr int DT = 32 * NCW;      // channels per CTA (32 per warp, 2 per lane pair)
@@ -54,14 +57,45 @@ struct BwdCfg {
   static constexpr int CKT = DT * NS;
   static constexpr int TOKF = 32;             // 16 row tokens + row count
   static constexpr uint32_t TMEM_COLS = 256;  // 16 steps x 2 channels x 8 states of h_{t-1}
-  // stage: u, delta, z, dy tiles, B, C tiles, checkpoint, token table
-  static constexpr int OFF_DT = TILE, OFF_Z = 2 * TILE, OFF_DY = 3 * TILE, OFF_B = 4 * TILE,
-                       OFF_C = 4 * TILE + BCT, OFF_CK = 4 * TILE + 2 * BCT, OFF_TOK = 4 * TILE + 2 * BCT + CKT;
-  static constexpr int STAGE_F = 4 * TILE + 2 * BCT + CKT + TOKF;
-  static constexpr int PART_F = 2 * TMAX * NCW * 32;  // double-buffered per-warp dB/dC partials
-  static constexpr int OFF_PART = NST * STAGE_F;
-  static constexpr int OFF_BAR = OFF_PART + PART_F;
-  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) * 4 + 2 * NST * 8 + 32 + 1024;
+  static constexpr int ES = int(sizeof(T));
+  static constexpr bool F32 = sizeof(T) == 4;
+  // stage: u, delta, z, dy tiles (T), B, C tiles (T), checkpoint (fp32), token
+  // table, and for 16-bit T an fp32 tile for dy' (fp32 T overwrites dy in place)
+  static constexpr int OFF_DT_B = TILE * ES, OFF_Z_B = 2 * TILE * ES, OFF_DY_B = 3 * TILE * ES,
+                       OFF_B_B = 4 * TILE * ES, OFF_C_B = 4 * TILE * ES + BCT * ES,
+                       OFF_CK_B = (4 * TILE * ES + 2 * BCT * ES + 15) / 16 * 16,
+                       OFF_TOK_B = OFF_CK_B + CKT * 4, OFF_DYP_B = F32 ? OFF_DY_B : OFF_TOK_B + TOKF * 4;
+  static constexpr int STAGE_B = ((F32 ? OFF_TOK_B + TOKF * 4 : OFF_DYP_B + TILE * 4) + 127) / 128 * 128;
+  static constexpr int PART_F = 2 * TMAX * NCW * 32;  // double-buffered per-warp dB/dC partials (fp32)
+  static constexpr int OFF_PART_B = NST * STAGE_B;
+  static constexpr int OFF_BAR_B = OFF_PART_B + PART_F * 4;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR_B) + 2 * NST * 8 + 32 + 1024;
+};
+
+// Typed views of one VJP stage.
+template <typename T>
+struct BwdStage {
+  const T* u;
+  const T* dt;
+  const T* z;
+  const T* dy;
+  float* dyp;  // dy' = dy silu(z) (fp32), written by the recompute pass
+  const T* B;
+  const T* C;
+  const float* ck;
+  const int* tok;
+  __device__ __forceinline__ explicit BwdStage(unsigned char* base) {
+    using Cfg = BwdCfg<T>;
+    u = reinterpret_cast<const T*>(base);
+    dt = reinterpret_cast<const T*>(base + Cfg::OFF_DT_B);
+    z = reinterpret_cast<const T*>(base + Cfg::OFF_Z_B);
+    dy = reinterpret_cast<const T*>(base + Cfg::OFF_DY_B);
+    dyp = reinterpret_cast<float*>(base + Cfg::OFF_DYP_B);
+    B = reinterpret_cast<const T*>(base + Cfg::OFF_B_B);
+    C = reinterpret_cast<const T*>(base + Cfg::OFF_C_B);
+    ck = reinterpret_cast<const float*>(base + Cfg::OFF_CK_B);
+    tok = reinterpret_cast<const int*>(base + Cfg::OFF_TOK_B);
+  }
 };
 
 // Rows of the per-(CTA, step) dB/dC partial: 16 dB values then 16 dC values.
@@ -110,17 +144,19 @@ struct RevCarry {
 };
 
 // State math of one reverse step (row r) with the history h_{s-1} in hp.
+template <typename T, bool HAS_Z>
 __device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], float2 (&dAbox)[2][4], float& dDbox,
-                                             const uint32_t (&hp)[16], const float* __restrict__ stg, int r,
-                                             int c0l, const PairLane& pl, RevCarry& k) {
-  using Cfg = BwdCfg;
-  constexpr int DT = Cfg::DT;
-  const float2 dy2 = lds2(stg + Cfg::OFF_DY + r * DT + c0l);
-  const float2 u2 = lds2(stg + r * DT + c0l);
-  const float2 t2 = lds2(stg + Cfg::OFF_DT + r * DT + c0l);
+                                             const uint32_t (&hp)[16], const BwdStage<T>& S, int r, int c0l,
+                                             const PairLane& pl, RevCarry& k) {
+  constexpr int DT = BwdCfg<T>::DT;
+  // dy' of the gated scan is the recompute pass's fp32 tile; without a gate
+  // dy' = dy (for fp32 T the two are the same tile)
+  const float2 dy2 = (HAS_Z || BwdCfg<T>::F32) ? lds2(S.dyp + r * DT + c0l) : ld_pair(S.dy + r * DT + c0l);
+  const float2 u2 = ld_pair(S.u + r * DT + c0l);
+  const float2 t2 = ld_pair(S.dt + r * DT + c0l);
   float2 B2[4], C2[4];
-  load8(stg + Cfg::OFF_B + r * NS, pl, B2);
-  load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+  load8t(S.B + r * NS, pl, B2);
+  load8t(S.C + r * NS, pl, C2);
   const float2 du2 = mul2(t2, u2);
   const float2 dl2 = mul2(t2, bcast2(kLog2e));
   const float dyc[2] = {dy2.x, dy2.y}, duc[2] = {du2.x, du2.y}, dtc[2] = {t2.x, t2.y}, dlc[2] = {dl2.x, dl2.y};
@@ -157,16 +193,16 @@ __device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], flo
 }
 
 // Epilogue of a reverse step: du / ddelta of the own channel, dB / dC row partial.
-__device__ __forceinline__ void bwd_rev_epilogue(const RevCarry& k, const float* __restrict__ stg,
-                                                 float* __restrict__ part, int warp, const PairLane& pl, float Down,
-                                                 float* du_b, float* dt_b, int sdus, int sdts, bool ev) {
-  using Cfg = BwdCfg;
-  const int tk = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK)[k.r];
+template <typename T>
+__device__ __forceinline__ void bwd_rev_epilogue(const RevCarry& k, const BwdStage<T>& S, float* __restrict__ part,
+                                                 int warp, const PairLane& pl, float Down, T* du_b, T* dt_b, int sdus,
+                                                 int sdts, bool ev) {
+  const int tk = S.tok[k.r];
   const float sB = pair_scatter(k.sBc[0], k.sBc[1], pl.hb);
   const float sA = pair_scatter(k.sAc[0], k.sAc[1], pl.hb);
-  stg_if(du_b + int64_t(tk) * sdus, fmaf(k.dyo, Down, k.to * sB), ev);
-  stg_if(dt_b + int64_t(tk) * sdts, fmaf(k.uo, sB, sA), ev);
-  part[(k.r * Cfg::NCW + warp) * 32 + pl.part_slot()] = dbc_reduce_scatter(k.vb, k.vc, pl);
+  stg_if_t(du_b + int64_t(tk) * sdus, fmaf(k.dyo, Down, k.to * sB), ev);
+  stg_if_t(dt_b + int64_t(tk) * sdts, fmaf(k.uo, sB, sA), ev);
+  part[(k.r * BwdCfg<T>::NCW + warp) * 32 + pl.part_slot()] = dbc_reduce_scatter(k.vb, k.vc, pl);
 }
 
 // What a recompute step hands to its gate epilogue.
@@ -178,14 +214,13 @@ struct FwdCarry {
 
 // One box of the VJP (nv rows).  The loops are kept rolled (pairs of steps):
 // a fully unrolled box overflows the instruction cache and runs slower.
-template <bool HAS_Z, bool REV>
-__device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, float* __restrict__ part, uint32_t taddr, int nv, int warp,
-                                        int lane, int c0l, const PairLane& pl, bool has_ck, bool v0, bool v1,
-                                        float Down, float* du_b, float* dt_b, float* dz_b, int sdus, int sdts,
+template <typename T, bool HAS_Z, bool REV>
+__device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float* __restrict__ part, uint32_t taddr,
+                                        int nv, int warp, int lane, int c0l, const PairLane& pl, bool has_ck,
+                                        bool v0, bool v1, float Down, T* du_b, T* dt_b, T* dz_b, int sdus, int sdts,
                                         int sdzs, bool ev) {
-  using Cfg = BwdCfg;
-  constexpr int DT = Cfg::DT;
-  const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
+  constexpr int DT = BwdCfg<T>::DT;
+  const int* tok = S.tok;
   const int own = c0l + pl.hb;
 
   float2 h[2][4];
@@ -193,7 +228,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
   for (int c = 0; c < 2; ++c) {
     // the checkpoint copy only covers valid channels; other rows are stale
     if (has_ck && (c ? v1 : v0)) {
-      load8(stg + Cfg::OFF_CK + (c0l + c) * NS, pl, h[c]);
+      load8(S.ck + (c0l + c) * NS, pl, h[c]);
     } else {
 #pragma unroll
       for (int j = 0; j < 4; ++j) h[c][j] = make_float2(0.f, 0.f);
@@ -203,10 +238,10 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
   // ---- forward pass: recompute, park history in TMEM, gate ----
   auto fwd_math = [&](int s, FwdCarry& k) {
     const int r = REV ? nv - 1 - s : s;
-    const float2 u2 = lds2(stg + r * DT + c0l);
-    const float2 t2 = lds2(stg + Cfg::OFF_DT + r * DT + c0l);
+    const float2 u2 = ld_pair(S.u + r * DT + c0l);
+    const float2 t2 = ld_pair(S.dt + r * DT + c0l);
     float2 B2[4];
-    load8(stg + Cfg::OFF_B + r * NS, pl, B2);
+    load8t(S.B + r * NS, pl, B2);
     const float2 du2 = mul2(t2, u2);
     const float2 dl2 = mul2(t2, bcast2(kLog2e));
     const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
@@ -229,7 +264,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
     }
     if (HAS_Z) {
       float2 C2[4];
-      load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+      load8t(S.C + r * NS, pl, C2);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const float2 acc = add2(fma2(C2[1], h[c][1], mul2(C2[0], h[c][0])), fma2(C2[3], h[c][3], mul2(C2[2], h[c][2])));
@@ -239,16 +274,16 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
       k.r = r;
     }
   };
-  // gate of the own channel: y_pre, dy' (written over dy in the stage), dz
+  // gate of the own channel: y_pre, dy' (into the stage's fp32 dy' tile,
+  // which for fp32 I/O is the dy tile itself), dz
   auto fwd_epilogue = [&](const FwdCarry& k) {
     const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
-    const float zz = stg[Cfg::OFF_Z + k.r * DT + own];
-    float* sdy = stg + Cfg::OFF_DY + k.r * DT + own;
-    const float dyv = *sdy;
+    const float zz = ld_one(S.z + k.r * DT + own);
+    const float dyv = ld_one(S.dy + k.r * DT + own);
     const float ypre = fmaf(k.uo, Down, ys);
     const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * zz));
-    stg_if(dz_b + int64_t(tok[k.r]) * sdzs, dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f), ev);
-    *sdy = dyv * (zz * sig);
+    stg_if_t(dz_b + int64_t(tok[k.r]) * sdzs, dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f), ev);
+    S.dyp[k.r * DT + own] = dyv * (zz * sig);
   };
   {
     FwdCarry fa, fb;
@@ -289,25 +324,25 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, float* __restrict__ stg, flo
   tmem_ld16(taddr + 16 * s, XA);
   tmem_wait_ld16(XA);
   if (s > 0) tmem_ld16(taddr + 16 * (s - 1), XB);
-  bwd_rev_math(L, hs, dAbox, dDbox, XA, stg, row(s), c0l, pl, ka);
+  bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XA, S, row(s), c0l, pl, ka);
   if (s > 0) tmem_wait_ld16(XB);
 #pragma unroll 1
   for (--s; s >= 1; s -= 2) {
     tmem_ld16(taddr + 16 * (s - 1), XA);
-    bwd_rev_math(L, hs, dAbox, dDbox, XB, stg, row(s), c0l, pl, kb);
-    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XB, S, row(s), c0l, pl, kb);
+    bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
     tmem_wait_ld16(XA);
     tmem_ld16(taddr + 16 * max(s - 2, 0), XB);
-    bwd_rev_math(L, hs, dAbox, dDbox, XA, stg, row(s - 1), c0l, pl, ka);
-    bwd_rev_epilogue(kb, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XA, S, row(s - 1), c0l, pl, ka);
+    bwd_rev_epilogue(kb, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
     tmem_wait_ld16(XB);
   }
   if (s == 0) {
-    bwd_rev_math(L, hs, dAbox, dDbox, XB, stg, row(0), c0l, pl, kb);
-    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
-    bwd_rev_epilogue(kb, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XB, S, row(0), c0l, pl, kb);
+    bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_epilogue(kb, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
   } else {
-    bwd_rev_epilogue(ka, stg, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
   }
 #pragma unroll
   for (int c = 0; c < 2; ++c)
@@ -329,21 +364,21 @@ struct BwdChunkArgs {
   const float* p_in;  // (batch, nchunks, d_inner, 16); row nchunks-1 unused
 };
 
-template <bool HAS_Z, bool REV>
-__global__ void __launch_bounds__(BwdCfg::NT, 2)
+template <typename T, bool HAS_Z, bool REV>
+__global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     scan_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_dy,
                     const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
-                    float* __restrict__ du_out, int64_t sdub, int sdus, float* __restrict__ ddt_out,
-                    int64_t sdtb, int sdts, float* __restrict__ dz_out, int64_t sdzb, int sdzs,
+                    T* __restrict__ du_out, int64_t sdub, int sdus, T* __restrict__ ddt_out,
+                    int64_t sdtb, int sdts, T* __restrict__ dz_out, int64_t sdzb, int sdzs,
                     const float* __restrict__ A, const float* __restrict__ Dskip, const float* __restrict__ ckpt,
                     float* __restrict__ wpart, float* __restrict__ wA, float* __restrict__ wD,
                     const BwdChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
-  using Cfg = BwdCfg;
+  using Cfg = BwdCfg<T>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST, NCT = Cfg::NCT, NCW = Cfg::NCW;
   extern __shared__ unsigned char smem_raw[];
-  float* sm = smem_align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Cfg::OFF_BAR);
+  unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + Cfg::OFF_BAR_B);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(empty + NST) + 4;
@@ -389,24 +424,24 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     const int k = REV ? g.nboxes - 1 - ib : ib;
     int c[3], nv;
     box_coords(g, k, c, nv);
-    float* base = sm + st * Cfg::STAGE_F;
-    int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK);
+    unsigned char* base = smb + st * Cfg::STAGE_B;
+    int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK_B);
     if (lane < nv) tok[lane] = int(box_row_token(g, c, lane));
     if (lane == TMAX) tok[TMAX] = nv;
     __syncwarp();
     if (lane == 0) {
-      const uint32_t tile_bytes = uint32_t(g.T) * uint32_t((HAS_Z ? 4 : 3) * DT + 2 * NS) * 4u;
+      const uint32_t tile_bytes = uint32_t(g.T) * uint32_t((HAS_Z ? 4 : 3) * DT + 2 * NS) * uint32_t(Cfg::ES);
       const uint32_t ck_bytes = uint32_t(nvalid_ch) * NS * 4u;
       mbar_arrive_expect_tx(&full[st], tile_bytes + (ib > 0 ? ck_bytes : 0u));
       tma_load_5d(base, &tm_u, &full[st], d0, c[0], c[1], c[2], b);
-      tma_load_5d(base + Cfg::OFF_DT, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
-      if (HAS_Z) tma_load_5d(base + Cfg::OFF_Z, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
-      tma_load_5d(base + Cfg::OFF_DY, &tm_dy, &full[st], d0, c[0], c[1], c[2], b);
-      tma_load_5d(base + Cfg::OFF_B, &tm_B, &full[st], 0, c[0], c[1], c[2], b);
-      tma_load_5d(base + Cfg::OFF_C, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
+      tma_load_5d(base + Cfg::OFF_DT_B, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
+      if (HAS_Z) tma_load_5d(base + Cfg::OFF_Z_B, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
+      tma_load_5d(base + Cfg::OFF_DY_B, &tm_dy, &full[st], d0, c[0], c[1], c[2], b);
+      tma_load_5d(base + Cfg::OFF_B_B, &tm_B, &full[st], 0, c[0], c[1], c[2], b);
+      tma_load_5d(base + Cfg::OFF_C_B, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
       if (ib > 0) {
         const float* src = ckpt + ((size_t(b) * g.nboxes + (ib - 1)) * g.d_inner + d0) * NS;
-        bulk_load(base + Cfg::OFF_CK, src, ck_bytes, &full[st]);
+        bulk_load(base + Cfg::OFF_CK_B, src, ck_bytes, &full[st]);
       }
     }
   };
@@ -454,9 +489,9 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
   L.dDacc = 0.f;
   const int own = dc + pl.hb;
   const float Down = ev ? Dskip[own] : 0.f;
-  float* du_b = du_out + b * sdub + own;
-  float* dt_b = ddt_out + b * sdtb + own;
-  float* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
+  T* du_b = du_out + b * sdub + own;
+  T* dt_b = ddt_out + b * sdtb + own;
+  T* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
   bool alive = true;
 
   for (int i = 0; i < nbx; ++i) {
@@ -469,11 +504,11 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
     if (warp == (i % NCW) && alive && i + NST - 1 < nbx) issue(i + NST - 1);
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles and tcgen05 below need the whole warp
-    float* part = sm + Cfg::OFF_PART + (i & 1) * (TMAX * NCW * 32);
-    float* stg = sm + st * Cfg::STAGE_F;
-    const int nv = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK)[TMAX];
+    float* part = reinterpret_cast<float*>(smb + Cfg::OFF_PART_B) + (i & 1) * (TMAX * NCW * 32);
+    const BwdStage<T> S(smb + st * Cfg::STAGE_B);
+    const int nv = S.tok[TMAX];
     if (alive)
-      bwd_box<HAS_Z, REV>(L, stg, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
+      bwd_box<T, HAS_Z, REV>(L, S, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
                           sdus, sdts, sdzs, ev);
     // dy' was written into the stage: order those generic-proxy writes before
     // the TMA load that will refill the stage
@@ -518,6 +553,7 @@ __global__ void __launch_bounds__(BwdCfg::NT, 2)
   }
 }
 
+template <typename T = float>
 struct BwdCarryCfg {
   static constexpr int NCW = 4;
   static constexpr int DT = 32 * NCW;  // the VJP's channel tile (same tensor maps)
@@ -526,11 +562,13 @@ struct BwdCarryCfg {
   static constexpr int NST = 2;
   static constexpr int TILE = TMAX * DT;
   static constexpr int BCT = TMAX * NS;
-  static constexpr int OFF_Z = TILE, OFF_DY = 2 * TILE, OFF_C = 3 * TILE, OFF_NV = 3 * TILE + BCT;
-  static constexpr int STAGE_F = 3 * TILE + BCT + 32;
-  static constexpr size_t SMEM_BYTES = size_t(NST * STAGE_F) * 4 + 2 * NST * 8 + 16 + 1024;
+  static constexpr int ES = int(sizeof(T));
+  static constexpr int OFF_Z_B = TILE * ES, OFF_DY_B = 2 * TILE * ES, OFF_C_B = 3 * TILE * ES,
+                       OFF_NV_B = 3 * TILE * ES + BCT * ES;
+  static constexpr int STAGE_B = (OFF_NV_B + 128 + 127) / 128 * 128;
+  static constexpr size_t SMEM_BYTES = size_t(NST) * STAGE_B + 2 * NST * 8 + 16 + 1024;
 };
-static_assert(BwdCarryCfg::DT == BwdCfg::DT, "the carry pass reads the VJP's tensor maps");
+static_assert(BwdCarryCfg<>::DT == BwdCfg<>::DT, "the carry pass reads the VJP's tensor maps");
 
 // Adjoint carry of chunks 1 .. nchunks-1 (grid z = chunk - 1) from a zero
 // carry at the chunk end: runs dh = C dy' + P, P = exp(delta A) dh backwards
@@ -538,17 +576,17 @@ static_assert(BwdCarryCfg::DT == BwdCfg::DT, "the carry pass reads the VJP's ten
 // P at the chunk start (p_local) and the chunk's sum of delta (carry_s).  The
 // state history is not needed for the carry, so this pass only streams
 // delta, z, dy and C.
-template <bool HAS_Z, bool REV>
-__global__ void __launch_bounds__(BwdCarryCfg::NT, 4)
+template <typename T, bool HAS_Z, bool REV>
+__global__ void __launch_bounds__(BwdCarryCfg<T>::NT, 4)
     scan_bwd_carry_kernel(const __grid_constant__ CUtensorMap tm_dt, const __grid_constant__ CUtensorMap tm_z,
                           const __grid_constant__ CUtensorMap tm_dy, const __grid_constant__ CUtensorMap tm_C,
                           const float* __restrict__ A, float* __restrict__ p_local, float* __restrict__ carry_s,
                           int bpc, int nchunks, const ScanGeom g, int* __restrict__ status) {
-  using Cfg = BwdCarryCfg;
+  using Cfg = BwdCarryCfg<T>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST, NCW = Cfg::NCW;
   extern __shared__ unsigned char smem_raw[];
-  float* sm = smem_align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + NST * Cfg::STAGE_F);
+  unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + NST * Cfg::STAGE_B);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
 
@@ -575,7 +613,7 @@ __global__ void __launch_bounds__(BwdCarryCfg::NT, 4)
       if (HAS_Z) prefetch_tmap(&tm_z);
       prefetch_tmap(&tm_dy);
       prefetch_tmap(&tm_C);
-      const uint32_t bytes = uint32_t(g.T) * uint32_t((HAS_Z ? 3 : 2) * DT + NS) * 4u;
+      const uint32_t bytes = uint32_t(g.T) * uint32_t((HAS_Z ? 3 : 2) * DT + NS) * uint32_t(Cfg::ES);
       for (int i = 0; i < nbx; ++i) {
         const int st = i % NST;
         const uint32_t ph = uint32_t(i / NST) & 1u;
@@ -584,13 +622,13 @@ __global__ void __launch_bounds__(BwdCarryCfg::NT, 4)
         const int k = REV ? g.nboxes - 1 - ib : ib;
         int c[3], nv;
         box_coords(g, k, c, nv);
-        float* base = sm + st * Cfg::STAGE_F;
-        reinterpret_cast<int*>(base + Cfg::OFF_NV)[0] = nv;
+        unsigned char* base = smb + st * Cfg::STAGE_B;
+        reinterpret_cast<int*>(base + Cfg::OFF_NV_B)[0] = nv;
         mbar_arrive_expect_tx(&full[st], bytes);
         tma_load_5d(base, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
-        if (HAS_Z) tma_load_5d(base + Cfg::OFF_Z, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
-        tma_load_5d(base + Cfg::OFF_DY, &tm_dy, &full[st], d0, c[0], c[1], c[2], b);
-        tma_load_5d(base + Cfg::OFF_C, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
+        if (HAS_Z) tma_load_5d(base + Cfg::OFF_Z_B, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_DY_B, &tm_dy, &full[st], d0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_C_B, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
       }
     }
     return;
@@ -621,21 +659,25 @@ __global__ void __launch_bounds__(BwdCarryCfg::NT, 4)
     const uint32_t ph = uint32_t(i / NST) & 1u;
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     if (alive) {
-      const float* __restrict__ stg = sm + st * Cfg::STAGE_F;
-      const int nv = reinterpret_cast<const int*>(stg + Cfg::OFF_NV)[0];
+      const unsigned char* sb = smb + st * Cfg::STAGE_B;
+      const T* __restrict__ sdt = reinterpret_cast<const T*>(sb);
+      const T* __restrict__ sz = reinterpret_cast<const T*>(sb + Cfg::OFF_Z_B);
+      const T* __restrict__ sdy = reinterpret_cast<const T*>(sb + Cfg::OFF_DY_B);
+      const T* __restrict__ sC = reinterpret_cast<const T*>(sb + Cfg::OFF_C_B);
+      const int nv = reinterpret_cast<const int*>(sb + Cfg::OFF_NV_B)[0];
 #pragma unroll 2
       for (int s = nv - 1; s >= 0; --s) {
         const int r = REV ? nv - 1 - s : s;
-        const float2 t2 = lds2(stg + r * DT + c0l);
-        float2 dy2 = lds2(stg + Cfg::OFF_DY + r * DT + c0l);
+        const float2 t2 = ld_pair(sdt + r * DT + c0l);
+        float2 dy2 = ld_pair(sdy + r * DT + c0l);
         if (HAS_Z) {
-          const float2 z2 = lds2(stg + Cfg::OFF_Z + r * DT + c0l);
+          const float2 z2 = ld_pair(sz + r * DT + c0l);
           const float s0 = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * z2.x));
           const float s1 = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * z2.y));
           dy2 = make_float2(dy2.x * (z2.x * s0), dy2.y * (z2.y * s1));
         }
         float2 C2[4];
-        load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+        load8t(sC + r * NS, pl, C2);
         const float2 dl2 = mul2(t2, bcast2(kLog2e));
         dsum = add2(dsum, t2);
         const float dyc[2] = {dy2.x, dy2.y}, dlc[2] = {dl2.x, dl2.y};
@@ -689,9 +731,9 @@ __global__ void carry_bwd_kernel(const float* __restrict__ A, const float* __res
 
 // dB/dC: sum the per-(channel tile) partials in tile order and scatter each
 // row back to its token.  grid (nboxes, batch), block TMAX*32.
-__global__ void reduce_dbc_kernel(const float* __restrict__ wpart, float* __restrict__ dB, int64_t sBb,
-                                  int64_t sBs, float* __restrict__ dC, int64_t sCb, int64_t sCs, const ScanGeom g,
-                                  int ndt) {
+template <typename T>
+__global__ void reduce_dbc_kernel(const float* __restrict__ wpart, T* __restrict__ dB, int64_t sBb, int64_t sBs,
+                                  T* __restrict__ dC, int64_t sCb, int64_t sCs, const ScanGeom g, int ndt) {
   const int ib = blockIdx.x, b = blockIdx.y;
   const int k = g.reverse ? g.nboxes - 1 - ib : ib;
   int c[3], nv;

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -346,6 +347,63 @@ __device__ __forceinline__ void load8(const float* p, const PairLane& pl, float2
 __device__ __forceinline__ void stg_if(float* p, float v, bool pred) {
   asm volatile(
       "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.f32 [%0], %1;\n\t}" ::"l"(p), "f"(v),
+      "r"(int(pred)));
+}
+
+// ---- element-type access for the scan's input / output tensors ----
+// The scans keep their state, accumulations, checkpoints and dA / dD in
+// fp32; the sequence tensors (u, delta, z, B, C, dy and y, du, ddelta, dz,
+// dB, dC) are fp32 or bf16 (the optional bf16 I/O variant).  Shared-memory
+// tiles hold the tensor's own element type; these helpers widen on load and
+// round (to nearest even) on store.
+template <typename T>
+__device__ __forceinline__ float2 ld_pair(const T* p);
+template <>
+__device__ __forceinline__ float2 ld_pair<float>(const float* p) {
+  return lds2(p);
+}
+template <>
+__device__ __forceinline__ float2 ld_pair<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
+template <typename T>
+__device__ __forceinline__ float ld_one(const T* p) {
+  return float(*p);
+}
+template <>
+__device__ __forceinline__ float ld_one<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat162float(*p);
+}
+
+// 8 states of slot order from a row of 16 (B or C of one step).
+template <typename T>
+__device__ __forceinline__ void load8t(const T* p, const PairLane& pl, float2 v[4]);
+template <>
+__device__ __forceinline__ void load8t<float>(const float* p, const PairLane& pl, float2 v[4]) {
+  load8(p, pl, v);
+}
+template <>
+__device__ __forceinline__ void load8t<__nv_bfloat16>(const __nv_bfloat16* p, const PairLane& pl, float2 v[4]) {
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const uint2 q = *reinterpret_cast<const uint2*>(p + pl.group_state(g));  // 4 bf16
+    v[2 * g] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.x));
+    v[2 * g + 1] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q.y));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void stg_if_t(T* p, float v, bool pred);
+template <>
+__device__ __forceinline__ void stg_if_t<float>(float* p, float v, bool pred) {
+  stg_if(p, v, pred);
+}
+template <>
+__device__ __forceinline__ void stg_if_t<__nv_bfloat16>(__nv_bfloat16* p, float v, bool pred) {
+  const unsigned short bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q st.global.b16 [%0], %1;\n\t}" ::"l"(p), "h"(bits),
       "r"(int(pred)));
 }
 

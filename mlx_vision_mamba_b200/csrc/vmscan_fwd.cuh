@@ -28,18 +28,22 @@
 namespace vmscan {
 
 
-template <int NCW>
+// T: element type of the sequence tensors (float, or __nv_bfloat16 for the
+// bf16 I/O variant); the stage tiles hold T, offsets are in bytes.
+template <int NCW, typename T = float>
 struct FwdCfg {
   static constexpr int DT = 32 * NCW;          // channels per CTA (32 per warp, 2 per lane pair)
   static constexpr int NCT = NCW * 32;         // consumer threads
   static constexpr int NT = NCT + 32;          // + producer warp
   static constexpr int NST = 2;                // TMA pipeline stages
-  static constexpr int TILE = TMAX * DT;       // floats of one (step, channel) tile
-  static constexpr int BCT = TMAX * NS;        // floats of one (step, state) tile
+  static constexpr int TILE = TMAX * DT;       // elements of one (step, channel) tile
+  static constexpr int BCT = TMAX * NS;        // elements of one (step, state) tile
   static constexpr int TOKF = 32;              // row -> token table (int32), padded
-  static constexpr int OFF_Z = 2 * TILE, OFF_B = 3 * TILE, OFF_C = 3 * TILE + BCT, OFF_TOK = 3 * TILE + 2 * BCT;
-  static constexpr int STAGE_F = 3 * TILE + 2 * BCT + TOKF;
-  static constexpr size_t SMEM_BYTES = size_t(NST * STAGE_F) * 4 + 2 * NST * 8 + 16 + 1024;
+  static constexpr int ES = int(sizeof(T));
+  static constexpr int OFF_DT_B = TILE * ES, OFF_Z_B = 2 * TILE * ES, OFF_B_B = 3 * TILE * ES,
+                       OFF_C_B = 3 * TILE * ES + BCT * ES, OFF_TOK_B = 3 * TILE * ES + 2 * BCT * ES;
+  static constexpr int STAGE_B = (OFF_TOK_B + TOKF * 4 + 127) / 128 * 128;
+  static constexpr size_t SMEM_BYTES = size_t(NST) * STAGE_B + 2 * NST * 8 + 16 + 1024;
 };
 
 // Chunked scan over L.  Chunk c holds boxes [c * bpc, min((c + 1) * bpc,
@@ -57,20 +61,20 @@ struct ChunkArgs {
   float* carry_s;           // (batch, nchunks, d_inner)
 };
 
-template <int NCW, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY = false>
-__global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
+template <int NCW, typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY = false>
+__global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
-                    const __grid_constant__ CUtensorMap tm_C, float* __restrict__ y, int64_t syb, int sys,
+                    const __grid_constant__ CUtensorMap tm_C, T* __restrict__ y, int64_t syb, int sys,
                     const float* __restrict__ A, const float* __restrict__ Dskip, float* __restrict__ ckpt,
                     const ChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
-  using Cfg = FwdCfg<NCW>;
+  using Cfg = FwdCfg<NCW, T>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST;
   static_assert(!CARRY || (!HAS_Z && !SAVE_CK && !STORE_Y), "a carry pass stores nothing but the carries");
   constexpr bool LOAD_Z = HAS_Z && STORE_Y;
   extern __shared__ unsigned char smem_raw[];
-  float* sm = smem_align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + NST * Cfg::STAGE_F);
+  unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + NST * Cfg::STAGE_B);
   uint64_t* empty = full + NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + NST);
 
@@ -102,7 +106,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
       prefetch_tmap(&tm_B);
       if (STORE_Y) prefetch_tmap(&tm_C);
     }
-    const uint32_t bytes = uint32_t(g.T) * uint32_t((LOAD_Z ? 3 : 2) * DT + (STORE_Y ? 2 : 1) * NS) * 4u;
+    const uint32_t bytes = uint32_t(g.T) * uint32_t((LOAD_Z ? 3 : 2) * DT + (STORE_Y ? 2 : 1) * NS) * Cfg::ES;
     for (int i = i0; i < i1; ++i) {
       const int st = (i - i0) % NST;
       const uint32_t ph = uint32_t((i - i0) / NST) & 1u;
@@ -112,18 +116,18 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
       const int k = REV ? g.nboxes - 1 - i : i;
       int c[3], nv;
       box_coords(g, k, c, nv);
-      float* base = sm + st * Cfg::STAGE_F;
-      int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK);
+      unsigned char* base = smb + st * Cfg::STAGE_B;
+      int* tok = reinterpret_cast<int*>(base + Cfg::OFF_TOK_B);
       if (STORE_Y && lane < nv) tok[lane] = int(box_row_token(g, c, lane));
       if (lane == TMAX) tok[TMAX] = nv;
       __syncwarp();
       if (lane == 0) {
         mbar_arrive_expect_tx(&full[st], bytes);
         tma_load_5d(base, &tm_u, &full[st], d0, c[0], c[1], c[2], b);
-        tma_load_5d(base + Cfg::TILE, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
-        if (LOAD_Z) tma_load_5d(base + Cfg::OFF_Z, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
-        tma_load_5d(base + Cfg::OFF_B, &tm_B, &full[st], 0, c[0], c[1], c[2], b);
-        if (STORE_Y) tma_load_5d(base + Cfg::OFF_C, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_DT_B, &tm_dt, &full[st], d0, c[0], c[1], c[2], b);
+        if (LOAD_Z) tma_load_5d(base + Cfg::OFF_Z_B, &tm_z, &full[st], d0, c[0], c[1], c[2], b);
+        tma_load_5d(base + Cfg::OFF_B_B, &tm_B, &full[st], 0, c[0], c[1], c[2], b);
+        if (STORE_Y) tma_load_5d(base + Cfg::OFF_C_B, &tm_C, &full[st], 0, c[0], c[1], c[2], b);
       }
     }
     return;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
   float2 dsum = make_float2(0.f, 0.f);  // CARRY: sum of delta over the chunk, both channels
   const int own = c0l + pl.hb;
   const float Down = ev ? Dskip[d0 + own] : 0.f;
-  float* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
+  T* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
   bool alive = true;
 
   struct Carry {
@@ -176,15 +180,20 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles below need the whole warp
     if (alive) {
-      const float* __restrict__ stg = sm + st * Cfg::STAGE_F;
-      const int* tok = reinterpret_cast<const int*>(stg + Cfg::OFF_TOK);
+      const unsigned char* sb = smb + st * Cfg::STAGE_B;
+      const T* __restrict__ su = reinterpret_cast<const T*>(sb);
+      const T* __restrict__ sdt = reinterpret_cast<const T*>(sb + Cfg::OFF_DT_B);
+      const T* __restrict__ sz = reinterpret_cast<const T*>(sb + Cfg::OFF_Z_B);
+      const T* __restrict__ sB = reinterpret_cast<const T*>(sb + Cfg::OFF_B_B);
+      const T* __restrict__ sC = reinterpret_cast<const T*>(sb + Cfg::OFF_C_B);
+      const int* tok = reinterpret_cast<const int*>(sb + Cfg::OFF_TOK_B);
       const int nv = tok[TMAX];
       auto math = [&](int s, Carry& k) {
         const int r = REV ? nv - 1 - s : s;
-        const float2 u2 = lds2(stg + r * DT + c0l);
-        const float2 t2 = lds2(stg + Cfg::TILE + r * DT + c0l);
+        const float2 u2 = ld_pair(su + r * DT + c0l);
+        const float2 t2 = ld_pair(sdt + r * DT + c0l);
         float2 B2[4];
-        load8(stg + Cfg::OFF_B + r * NS, pl, B2);
+        load8t(sB + r * NS, pl, B2);
         const float2 du2 = mul2(t2, u2);
         const float2 dl2 = mul2(t2, bcast2(kLog2e));
         if (CARRY) dsum = add2(dsum, t2);
@@ -199,7 +208,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
         }
         if (STORE_Y) {
           float2 C2[4];
-          load8(stg + Cfg::OFF_C + r * NS, pl, C2);
+          load8t(sC + r * NS, pl, C2);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float2 acc =
@@ -211,9 +220,9 @@ __global__ void __launch_bounds__(FwdCfg<NCW>::NT, 4)
       };
       auto epilogue = [&](const Carry& k) {
         const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
-        float yy = fmaf(stg[k.r * DT + own], Down, ys);
-        if (HAS_Z) yy *= silu_f(stg[Cfg::OFF_Z + k.r * DT + own]);
-        stg_if(ybase + int64_t(tok[k.r]) * sys, yy, ev);
+        float yy = fmaf(ld_one(su + k.r * DT + own), Down, ys);
+        if (HAS_Z) yy *= silu_f(ld_one(sz + k.r * DT + own));
+        stg_if_t(ybase + int64_t(tok[k.r]) * sys, yy, ev);
       };
       Carry ka, kb;
       math(0, ka);

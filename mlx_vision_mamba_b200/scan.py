@@ -43,42 +43,54 @@ def _strides(t: Optional[torch.Tensor]) -> _native.Strides:
     return _native.Strides(t.stride(0), t.stride(1))
 
 
-def _tma_compatible(t: torch.Tensor) -> bool:
+# Sequence tensors travel as fp32 (the reference's precision) or bf16 (the
+# bf16 I/O entry points); TMA strides are whole 16-byte multiples, i.e. 4 fp32
+# or 8 bf16 elements.
+_SEQ_DTYPES = (torch.float32, torch.bfloat16)
+
+
+def _align_elems(dtype: torch.dtype) -> int:
+    return 16 // (4 if dtype == torch.float32 else 2)
+
+
+def _tma_compatible(t: torch.Tensor, dtype: torch.dtype = torch.float32) -> bool:
     """True when the (B, L, C) view meets the TMA rules of include/vmscan.h."""
-    if t.dtype != torch.float32 or t.dim() != 3 or t.stride(2) != 1 and t.size(2) > 1:
+    if t.dtype != dtype or t.dim() != 3 or t.stride(2) != 1 and t.size(2) > 1:
         return False
     if t.data_ptr() % 16:
         return False
+    q = _align_elems(dtype)
     b, l, _ = t.shape
-    if l > 1 and (t.stride(1) <= 0 or t.stride(1) % 4):
+    if l > 1 and (t.stride(1) <= 0 or t.stride(1) % q):
         return False
-    if b > 1 and (t.stride(0) <= 0 or t.stride(0) % 4):
+    if b > 1 and (t.stride(0) <= 0 or t.stride(0) % q):
         return False
     return True
 
 
-def _empty_seq(b: int, l: int, c: int, device) -> torch.Tensor:
-    """Uninitialised (b, l, c) fp32 view whose storage rows are padded to a
-    multiple of 4 channels, as the TMA rules of include/vmscan.h require."""
-    cp = (c + 3) // 4 * 4
-    buf = torch.empty((b, l, cp), dtype=torch.float32, device=device)
+def _empty_seq(b: int, l: int, c: int, device, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Uninitialised (b, l, c) view whose storage rows are padded to a whole
+    16 bytes, as the TMA rules of include/vmscan.h require."""
+    q = _align_elems(dtype)
+    cp = (c + q - 1) // q * q
+    buf = torch.empty((b, l, cp), dtype=dtype, device=device)
     return buf if cp == c else buf[:, :, :c]
 
 
-def _prepare(t: torch.Tensor) -> torch.Tensor:
-    """Return a TMA-compatible fp32 view of t, copying only when needed.
+def _prepare(t: torch.Tensor, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Return a TMA-compatible view of t in `dtype`, copying only when needed.
 
     Strided views such as the reference's `xz[:, :, :d_inner]` slices pass
-    through untouched; a copy is made only for other dtypes, a non-unit
-    channel stride, or strides that are not multiples of 4 elements (then the
-    channel dim is padded to a multiple of 4 in storage).
+    through untouched; a copy is made only for another dtype, a non-unit
+    channel stride, or strides that are not whole 16-byte multiples (then the
+    channel dim is padded in storage).
     """
-    if t.dtype != torch.float32:
-        t = t.float()
-    if _tma_compatible(t):
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if _tma_compatible(t, dtype):
         return t
     b, l, c = t.shape
-    out = _empty_seq(b, l, c, t.device)
+    out = _empty_seq(b, l, c, t.device, dtype)
     out.copy_(t)
     return out
 
@@ -119,14 +131,15 @@ class _SelectiveScanFn(torch.autograd.Function):
     def forward(ctx, x, delta, A, B, C, D, z, direction):
         lib = _native.load()
         bt, l, dn = x.shape
-        u_ = _prepare(x)
-        dt_ = _prepare(delta)
-        B_ = _prepare(B)
-        C_ = _prepare(C)
-        z_ = _prepare(z) if z is not None else None
+        sd = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        u_ = _prepare(x, sd)
+        dt_ = _prepare(delta, sd)
+        B_ = _prepare(B, sd)
+        C_ = _prepare(C, sd)
+        z_ = _prepare(z, sd) if z is not None else None
         A_ = A.detach().float().contiguous()
         D_ = D.detach().float().contiguous()
-        y = _empty_seq(bt, l, dn, x.device)
+        y = _empty_seq(bt, l, dn, x.device, sd)
         need_grad = any(ctx.needs_input_grad[:7])
         dptr = _dir_ptr(direction)
         ckpt = None
@@ -139,18 +152,20 @@ class _SelectiveScanFn(torch.autograd.Function):
         if fws_n < 0:
             _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
         fws = torch.empty(int(fws_n), dtype=torch.uint8, device=x.device) if fws_n > 0 else None
-        st = lib.vmscan_fwd(
+        fwd = lib.vmscan_fwd_bf16 if sd == torch.bfloat16 else lib.vmscan_fwd
+        st = fwd(
             bt, l, dn, D_STATE,
             _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
             _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
             _ptr(z_), _strides(z_), _ptr(y), _strides(y), _ptr(ckpt), dptr,
             _ptr(fws), int(fws_n), _stream(x),
         )
-        _native.check(st, "vmscan_fwd")
+        _native.check(st, "vmscan_fwd_bf16" if sd == torch.bfloat16 else "vmscan_fwd")
         if need_grad:
             ctx.save_for_backward(u_, dt_, A_, B_, C_, D_, z_, ckpt)
         ctx.direction = direction
         ctx.has_z = z is not None
+        ctx.param_dtypes = (A.dtype, D.dtype)
         return y
 
     @staticmethod
@@ -159,21 +174,23 @@ class _SelectiveScanFn(torch.autograd.Function):
         u_, dt_, A_, B_, C_, D_, z_, ckpt = ctx.saved_tensors
         bt, l, dn = u_.shape
         dev = u_.device
-        dy_ = _prepare(dy)
+        sd = u_.dtype
+        dy_ = _prepare(dy, sd)
         f32 = dict(dtype=torch.float32, device=dev)
-        du = _empty_seq(bt, l, dn, dev)
-        ddelta = _empty_seq(bt, l, dn, dev)
+        du = _empty_seq(bt, l, dn, dev, sd)
+        ddelta = _empty_seq(bt, l, dn, dev, sd)
         dA = torch.empty((dn, D_STATE), **f32)
-        dB = torch.empty((bt, l, D_STATE), **f32)
-        dC = torch.empty((bt, l, D_STATE), **f32)
+        dB = torch.empty((bt, l, D_STATE), dtype=sd, device=dev)
+        dC = torch.empty((bt, l, D_STATE), dtype=sd, device=dev)
         dD = torch.empty((dn,), **f32)
-        dz = _empty_seq(bt, l, dn, dev) if ctx.has_z else None
+        dz = _empty_seq(bt, l, dn, dev, sd) if ctx.has_z else None
         dptr = _dir_ptr(ctx.direction)
         ws_bytes = lib.vmscan_bwd_workspace_bytes(bt, l, dn, D_STATE, dptr, 0)
         if ws_bytes < 0:
             _native.check(-ws_bytes, "vmscan_bwd_workspace_bytes")
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
-        st = lib.vmscan_bwd(
+        bwd = lib.vmscan_bwd_bf16 if sd == torch.bfloat16 else lib.vmscan_bwd
+        st = bwd(
             bt, l, dn, D_STATE,
             _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
             _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
@@ -184,8 +201,9 @@ class _SelectiveScanFn(torch.autograd.Function):
             _ptr(dz), _strides(dz),
             dptr, _ptr(ws), ws.numel(), _stream(u_),
         )
-        _native.check(st, "vmscan_bwd")
-        return du, ddelta, dA, dB, dC, dD, dz, None
+        _native.check(st, "vmscan_bwd_bf16" if sd == torch.bfloat16 else "vmscan_bwd")
+        a_dt, d_dt = ctx.param_dtypes
+        return du, ddelta, dA.to(a_dt), dB, dC, dD.to(d_dt), dz, None
 
 
 def selective_scan_cuda(
@@ -209,7 +227,10 @@ def selective_scan_cuda(
         z:     optional (B, L, D_inner) gate; returns y * silu(z)
         direction: optional ScanDirection; tokens are visited in that order
             and y is returned in token order.
-    Returns y (B, L, D_inner), fp32.
+    Returns y (B, L, D_inner): fp32, or bf16 when x is bf16.  With a bf16 x
+    the sequence tensors (x, delta, B, C, z) are read as bf16 (cast if they
+    are not) and y and their gradients are bf16; A, D, the recurrent state and
+    all arithmetic stay fp32.  Any other dtype is computed in fp32.
     """
     _check_inputs(x, delta, A, B, C, D, z)
     return _SelectiveScanFn.apply(x, delta, A, B, C, D, z, direction)

@@ -57,3 +57,34 @@ def assert_parity(name, ours, ref64, ref32=None, rtol=RTOL, atol=ATOL):
         f"{name}: element error/bound = {ratio:.3f}, norm error ratio = {norm_ratio:.3f} "
         f"(fraction within plain 1e-5/1e-6: {strict:.6f})"
     )
+
+
+# bf16 I/O: an fp32 result rounded to bf16 (8 significand bits, round to
+# nearest even) is off by at most 2^-8 of its magnitude on top of the fp32
+# error.
+BF16_ROUND = 2.0**-8
+
+
+def assert_parity_bf16(name, ours, ref64, ref32=None):
+    """Parity of a bf16 output computed in fp32 and rounded once at the store.
+
+    element-wise  |ours - exact| <= (fp32 bound of assert_parity) + 2^-8 |exact|
+    norm-wise     ||ours - exact||_2 <= 2 ||bf16(exact) - exact||_2
+                                        + 2 ||ref32 - exact||_2 + ATOL sqrt(n)
+                  (on average no less accurate than half the accuracy of
+                  rounding the exact result to bf16).
+    """
+    ours = ours.detach().double().cpu()
+    ref64 = ref64.detach().double().cpu()
+    assert ours.shape == ref64.shape, (name, tuple(ours.shape), tuple(ref64.shape))
+    assert torch.isfinite(ours).all(), f"{name}: non-finite values"
+    err = (ours - ref64).abs()
+    bound = ATOL + (RTOL + BF16_ROUND) * ref64.abs()
+    rhs = 2.0 * (ref64.to(torch.bfloat16).double() - ref64).norm().item() + ATOL * math.sqrt(max(err.numel(), 1))
+    if ref32 is not None:
+        ref_err = (ref32.detach().double().cpu() - ref64).abs()
+        bound = bound + 2.0 * (ref_err.max() if ref_err.numel() else 0.0)
+        rhs += 2.0 * ref_err.norm().item()
+    ratio = (err / bound).max().item() if err.numel() else 0.0
+    lhs = err.norm().item()
+    assert ratio <= 1.0 and lhs <= rhs, f"{name}: element error/bound = {ratio:.3f}, norm error ratio = {lhs / rhs:.3f}"
