@@ -89,14 +89,16 @@ def sweep_inputs(batch, seq_len, d_inner, seed=0, dtype=torch.float32, d_state=1
     return {k: v.to(dtype) for k, v in out.items()}
 
 
-def scan_vjp(inputs, gated=True, dtype=torch.float32):
-    """Forward + VJP of the (optionally gated) sequential scan via autograd.
+def scan_vjp(inputs, gated=True, dtype=torch.float32, scan_fn=None):
+    """Forward + VJP of the (optionally gated) scan via autograd; scan_fn is
+    the sequential scan (default) or selective_scan_chunked.
 
     Returns (y, grads) with grads keyed du, ddelta, dA, dB, dC, dD[, dz].
     """
+    scan_fn = scan_fn or selective_scan
     names = ["u", "delta", "A", "B", "C", "D"] + (["z"] if gated else [])
     leaves = {k: inputs[k].detach().to(dtype).clone().requires_grad_(True) for k in names}
-    y = selective_scan(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"])
+    y = scan_fn(leaves["u"], leaves["delta"], leaves["A"], leaves["B"], leaves["C"], leaves["D"])
     if gated:
         y = y * silu(leaves["z"])
     y.backward(inputs["dy"].to(dtype))
