@@ -740,6 +740,50 @@ def run_encoder(dev, rank, world, which, mode, steps, warmup, barrier):
                                      "execution": "one CUDA graph per step"}}
 
 
+def measure_host_link(dev, gib=1, reps=3):
+    """Pinned host <-> device copy bandwidth of this GPU's link (GB/s):
+    upload alone, download alone, and both at once on two streams (the
+    pattern run_e2e uses), each the mean of `reps` copies of `gib` GiB."""
+    import torch
+
+    n = gib * 256 * 1024 * 1024
+    hs = [torch.empty(n, dtype=torch.float32).pin_memory() for _ in range(2)]
+    ds = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+
+    def up():
+        with torch.cuda.stream(s_up):
+            ds[0].copy_(hs[0], non_blocking=True)
+
+    def down():
+        with torch.cuda.stream(s_down):
+            hs[1].copy_(ds[1], non_blocking=True)
+
+    def timed(fns):
+        for f in fns:
+            f()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(comp)
+        s_up.wait_stream(comp)
+        s_down.wait_stream(comp)
+        for _ in range(reps):
+            for f in fns:
+                f()
+        comp.wait_stream(s_up)
+        comp.wait_stream(s_down)
+        e1.record(comp)
+        torch.cuda.synchronize()
+        return n * 4 * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+    res = {"h2d_gbs": timed([up]), "d2h_gbs": timed([down]), "duplex_gbs_each_way": timed([up, down]),
+           "method": f"{gib} GiB pinned copies, mean of {reps}, CUDA events"}
+    del hs, ds
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_e2e(t, dev, K, warmup, world, barrier):
     """Public API (selective_scan_cuda + backward) with pinned host inputs and
     outputs.  Every step copies its own inputs host->device and its output and
@@ -807,8 +851,11 @@ def run_e2e(t, dev, K, warmup, world, barrier):
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
     ms = float(tm.item())
     byt = fwd_bytes(b, l, d) + bwd_bytes(b, l, d)
+    link = measure_host_link(dev)
     return {"value": world * K * byt / (ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms / K, "steps": K,
+            "host_link": link,
+            "copy_gbs_each_way": max(h2d, d2h) / (ms / K / 1e3) / 1e9,
             "api": "mlx_vision_mamba_b200.selective_scan_cuda(...).backward(dy), pinned host buffers, "
                    "uploads / downloads on their own streams (double-buffered, overlapping the previous / next step)"}
 
