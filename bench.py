@@ -294,6 +294,8 @@ def main():
                     help="time forward and VJP separately on the 12 op-sweep points and print a table")
     ap.add_argument("--io", choices=["f32", "bf16"], default="f32",
                     help="with --sweep: sequence tensors in fp32 (the reference's dtype) or bf16")
+    ap.add_argument("--conv", action="store_true",
+                    help="only time the conv1d + SiLU kernels (forward, VJP) at the model's block shape")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
@@ -306,6 +308,11 @@ def main():
         return
     if args.sweep:
         run_sweep(max(args.steps, 20), max(args.warmup, 3), bf16=args.io == "bf16")
+        return
+    if args.conv:
+        import torch
+
+        print(json.dumps({"conv1d_silu": time_conv(torch.device("cuda", 0))}), flush=True)
         return
 
     import torch
@@ -385,6 +392,9 @@ def main():
     # ---- BASELINE config 1 shape: the reference's only published scan numbers ----
     cfg1 = time_config1(dev, stream) if rank == 0 else None
 
+    # ---- the direction-aware conv1d + SiLU kernels at the model's block shape ----
+    conv = time_conv(dev) if rank == 0 else None
+
     # ---- the same workload through the bf16 I/O entry points (not the metric) ----
     bf16_io = time_bf16_io(t, dev, stream, K, args.warmup) if rank == 0 else None
 
@@ -441,6 +451,7 @@ def main():
             "e2e": e2e,
             "config1_scan": cfg1,
             "bf16_io": bf16_io,
+            "conv1d_silu": conv,
             "cpu_baseline": base,
             "vision_mamba_2d_train": model_line,
         }
@@ -573,6 +584,71 @@ def time_bf16_io(t, dev, stream, K, warmup):
     return {"api": "vmscan_fwd_bf16 + vmscan_bwd_bf16", "fwd_ms": f, "bwd_ms": bw, "ms_per_step": f + bw,
             "fwd_gbs": fb / f / 1e6, "bwd_gbs": bb / bw / 1e6, "fwd_frac": fb / f / 1e6 / peak,
             "bwd_frac": bb / bw / 1e6 / peak, "algorithmic_bytes_per_step": fb + bb}
+
+
+def time_conv(dev, iters=20):
+    """Direction-aware causal conv1d + SiLU through the C ABI with
+    preallocated buffers (forward, and VJP incl. the dw/dbias reductions) at
+    the VisionMamba-2D block shape (64, 196, 768, K=4), row-major and
+    column-major scan order on the 14 x 14 grid; median of `iters` launches
+    after 3 warm-up ones, a 256 MB buffer overwritten before each.
+    Algorithmic bytes per (token, channel): forward 8 (read x, write out),
+    VJP 12 (read x and dout, write dx)."""
+    import torch
+
+    from mlx_vision_mamba_b200 import _native, directions_for
+
+    lib = _native.load()
+    b, l, c, k = 64, 196, 768, 4
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(b, l, c, device=dev, generator=g)
+    w = torch.randn(c, k, 1, device=dev, generator=g) * 0.5
+    bias = torch.randn(c, device=dev, generator=g) * 0.1
+    dy = torch.randn(b, l, c, device=dev, generator=g)
+    out, dx = torch.empty_like(x), torch.empty_like(x)
+    dw, db = torch.empty_like(w), torch.empty_like(bias)
+    ws_n = lib.vmscan_conv1d_bwd_workspace_bytes(b, l, c, k)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+    S = _native.Strides(l * c, c)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    st = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(st.cuda_stream)
+    peak, _ = measured_peaks()
+    res = {"shape": f"batch {b}, L {l}, channels {c}, K {k}", "api": "vmscan_conv1d_silu_fwd / _bwd"}
+    for name, d in (("row_major", None), ("col_major", directions_for(4, (14, 14))[2])):
+        dref = ctypes.byref(d.to_native()) if d is not None else None
+
+        def fwd():
+            rc = lib.vmscan_conv1d_silu_fwd(b, l, c, k, x.data_ptr(), S, w.data_ptr(), bias.data_ptr(),
+                                            out.data_ptr(), S, dref, sp)
+            assert rc == 0, rc
+
+        def bwd():
+            rc = lib.vmscan_conv1d_silu_bwd(b, l, c, k, x.data_ptr(), S, w.data_ptr(), bias.data_ptr(),
+                                            dy.data_ptr(), S, dx.data_ptr(), S, dw.data_ptr(), db.data_ptr(), dref,
+                                            ws.data_ptr(), ws_n, sp)
+            assert rc == 0, rc
+
+        tms = {}
+        for fname, fn in (("fwd", fwd), ("bwd", bwd)):
+            ts = []
+            for it in range(iters + 3):
+                flush.fill_(1.0)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                fn()
+                e1.record(st)
+                e1.synchronize()
+                if it >= 3:
+                    ts.append(e0.elapsed_time(e1))
+            tms[fname] = statistics.median(ts)
+        fb, bb = 8 * b * l * c, 12 * b * l * c
+        res[name] = {"fwd_ms": tms["fwd"], "bwd_ms": tms["bwd"], "fwd_gbs": fb / tms["fwd"] / 1e6,
+                     "bwd_gbs": bb / tms["bwd"] / 1e6, "fwd_frac": fb / tms["fwd"] / 1e6 / peak,
+                     "bwd_frac": bb / tms["bwd"] / 1e6 / peak}
+    del x, w, bias, dy, out, dx, ws, flush
+    torch.cuda.empty_cache()
+    return res
 
 
 SWEEP = [(b, l, d) for b in (8, 64) for l in (196, 1024, 4096) for d in (768, 1536)]
