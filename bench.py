@@ -296,6 +296,8 @@ def main():
                     help="with --sweep: sequence tensors in fp32 (the reference's dtype) or bf16")
     ap.add_argument("--conv", action="store_true",
                     help="only time the conv1d + SiLU kernels (forward, VJP) at the model's block shape")
+    ap.add_argument("--dt", action="store_true",
+                    help="only time the dt_proj + softplus kernels (forward, VJP) at the model's block shape")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
     args = ap.parse_args()
@@ -313,6 +315,11 @@ def main():
         import torch
 
         print(json.dumps({"conv1d_silu": time_conv(torch.device("cuda", 0))}), flush=True)
+        return
+    if args.dt:
+        import torch
+
+        print(json.dumps({"dt_softplus": time_dt(torch.device("cuda", 0))}), flush=True)
         return
 
     import torch
@@ -394,6 +401,7 @@ def main():
 
     # ---- the direction-aware conv1d + SiLU kernels at the model's block shape ----
     conv = time_conv(dev) if rank == 0 else None
+    dtk = time_dt(dev) if rank == 0 else None
 
     # ---- the same workload through the bf16 I/O entry points (not the metric) ----
     bf16_io = time_bf16_io(t, dev, stream, K, args.warmup) if rank == 0 else None
@@ -452,6 +460,7 @@ def main():
             "config1_scan": cfg1,
             "bf16_io": bf16_io,
             "conv1d_silu": conv,
+            "dt_softplus": dtk,
             "cpu_baseline": base,
             "vision_mamba_2d_train": model_line,
         }
@@ -647,6 +656,59 @@ def time_conv(dev, iters=20):
                      "bwd_gbs": bb / tms["bwd"] / 1e6, "fwd_frac": fb / tms["fwd"] / 1e6 / peak,
                      "bwd_frac": bb / tms["bwd"] / 1e6 / peak}
     del x, w, bias, dy, out, dx, ws, flush
+    torch.cuda.empty_cache()
+    return res
+
+
+def time_dt(dev, iters=20):
+    """dt_proj + bias + softplus (forward) and its softplus VJP through the C
+    ABI at the VisionMamba-2D block shape: 64 x 196 tokens, dt_rank 24 read
+    from the x_dbc rows (width 56), d_inner 768; median of `iters` launches
+    after 3 warm-up ones, a 256 MB buffer overwritten before each.
+    Algorithmic bytes per (token, channel): forward 4 (write delta), VJP 8
+    (read ddelta, write dpre); the x rows and W add under 1 %."""
+    import torch
+
+    from mlx_vision_mamba_b200 import _native
+
+    lib = _native.load()
+    ntok, r, wide, dn = 64 * 196, 24, 56, 768
+    g = torch.Generator(device=dev).manual_seed(12)
+    xw = torch.randn(ntok, wide, device=dev, generator=g)
+    w = torch.randn(dn, r, device=dev, generator=g) / r**0.5
+    bias = torch.randn(dn, device=dev, generator=g)
+    gin = torch.randn(ntok, dn, device=dev, generator=g)
+    out = torch.empty(ntok, dn, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    st = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(st.cuda_stream)
+    peak, _ = measured_peaks()
+
+    def fwd():
+        assert lib.vmscan_dt_softplus_fwd(ntok, r, dn, xw.data_ptr(), wide, w.data_ptr(), bias.data_ptr(),
+                                          out.data_ptr(), dn, sp) == 0
+
+    def bwd():
+        assert lib.vmscan_dt_softplus_bwd(ntok, r, dn, xw.data_ptr(), wide, w.data_ptr(), bias.data_ptr(),
+                                          gin.data_ptr(), dn, out.data_ptr(), dn, sp) == 0
+
+    res = {"shape": f"{ntok} tokens, dt_rank {r}, d_inner {dn}", "api": "vmscan_dt_softplus_fwd / _bwd"}
+    for name, fn, byt in (("fwd", fwd, 4 * ntok * dn), ("bwd", bwd, 8 * ntok * dn)):
+        ts = []
+        for it in range(iters + 3):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            if it >= 3:
+                ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        res[name + "_ms"] = ms
+        res[name + "_gbs"] = byt / ms / 1e6
+        res[name + "_frac"] = byt / ms / 1e6 / peak
+    del xw, w, bias, gin, out, flush
     torch.cuda.empty_cache()
     return res
 

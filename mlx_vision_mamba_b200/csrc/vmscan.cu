@@ -578,11 +578,13 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
   if ((ntok + DTP_TOKENS - 1) / DTP_TOKENS > 65535)
     return fail(VMSCAN_ERR_SHAPE, "dt_softplus: %lld tokens exceed the launch grid", (long long)ntok);
   VM_TRY(ensure_context(x));
-  const dim3 grid(unsigned((d_inner + DTP_THREADS - 1) / DTP_THREADS), unsigned((ntok + DTP_TOKENS - 1) / DTP_TOKENS));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int R = int(dt_rank), D = int(d_inner);
+  const unsigned ty = unsigned((ntok + DTP_TOKENS - 1) / DTP_TOKENS);
 #define VM_DTP(RP)                                                                                           \
-  dt_softplus_kernel<RP, BWD><<<grid, DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, ntok, D)
+  dt_softplus_kernel<RP, BWD>                                                                                \
+      <<<dim3(unsigned((d_inner + DTP_THREADS * dtp_channels(RP) - 1) / (DTP_THREADS * dtp_channels(RP))), ty), \
+         DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, ntok, D)
   if (R <= 8)
     VM_DTP(8);
   else if (R <= 16)

@@ -10,64 +10,109 @@
 // The remaining gradients (dx = dpre W, dW = dpre^T x, dbias = column sums of
 // dpre) are plain GEMMs / reductions done by the caller.
 //
-// Layout: a CTA owns DTP_THREADS channels x DTP_TOKENS tokens; the tokens'
-// x rows (dt_rank floats, zero-padded to RP) are staged once in shared memory
-// and read as broadcasts; each thread keeps its channel's weight row in
-// registers, so the dt_rank-long dot product costs dt_rank FMAs and no loads.
-// delta / dpre rows are written coalesced (consecutive channels per warp).
+// Layout: a CTA owns DTP_THREADS x (1 or 2) channels x DTP_TOKENS tokens;
+// the tokens' x rows (dt_rank floats, zero-padded to RP) are staged once in
+// shared memory (transposed) and read as broadcasts; each thread keeps its
+// channels' weight rows in registers and forms 4 tokens' dot products as two
+// packed pairs per channel, so a token costs dt_rank / 2 packed FMAs per
+// channel and no global loads.  delta / dpre rows are written coalesced
+// (consecutive channels per warp).
 #pragma once
 
 #include "vmscan_common.cuh"
 
 namespace vmscan {
 
-constexpr int DTP_THREADS = 256;
-constexpr int DTP_TOKENS = 32;
+constexpr int DTP_THREADS = 128;
+constexpr int DTP_TOKENS = 64;
 constexpr int DTP_RMAX = 64;
+constexpr int DTP_U = 4;  // tokens per iteration (two packed pairs)
+static_assert(DTP_TOKENS % DTP_U == 0, "xs holds whole token groups");
 
-// log(1 + exp(v)) as the reference writes it (inf for v beyond expf's range,
-// like the reference); log1pf keeps full precision where exp(v) is small.
-__device__ __forceinline__ float softplus_ref(float v) { return log1pf(__expf(v)); }
+// Channels per thread for a rank bucket: two (d and d + DTP_THREADS, so each
+// shared-memory load of x feeds both) while both weight rows fit in registers.
+__host__ __device__ constexpr int dtp_channels(int RP) { return RP <= 32 ? 2 : 1; }
+
+// log(1 + exp(v)), the reference's own expression (inf for v beyond expf's
+// range, like the reference), on the MUFU: exp2 and log2 (absolute error
+// about 2.4e-7 over the softplus range; the reference's rounding of 1 + exp(v)
+// alone is 6e-8).
+__device__ __forceinline__ float softplus_ref(float v) { return __logf(1.0f + __expf(v)); }
+
+// Shared-memory row of one rank index: DTP_TOKENS tokens, padded so that the
+// transposing writes of the staging loop spread over 8 banks.
+constexpr int DTP_XROW = DTP_TOKENS + 4;
 
 // RP: dt_rank rounded up to a multiple of 4 (<= DTP_RMAX).  BWD: write
-// dpre = gin * sigmoid(pre) instead of softplus(pre).
+// dpre = gin * sigmoid(pre) instead of softplus(pre).  A CTA covers
+// DTP_THREADS * dtp_channels(RP) channels x DTP_TOKENS tokens.
 template <int RP, bool BWD>
 __global__ void __launch_bounds__(DTP_THREADS)
     dt_softplus_kernel(const float* __restrict__ x, int64_t ldx, int R, const float* __restrict__ W,
                        const float* __restrict__ bias, const float* __restrict__ gin, int64_t ldg,
                        float* __restrict__ out, int64_t ldo, int64_t ntok, int Dn) {
-  __shared__ __align__(16) float xs[DTP_TOKENS][RP];
+  constexpr int CH = dtp_channels(RP);
+  // xs[r][t]: x of token t0 + t at rank index r (transposed, so one 128-bit
+  // load gives 4 tokens' values of one r for the packed FMAs below)
+  __shared__ __align__(16) float xs[RP][DTP_XROW];
   const int64_t t0 = int64_t(blockIdx.y) * DTP_TOKENS;
   for (int i = threadIdx.x; i < DTP_TOKENS * RP; i += DTP_THREADS) {
     const int t = i / RP, r = i % RP;
-    xs[t][r] = (t0 + t < ntok && r < R) ? x[(t0 + t) * ldx + r] : 0.f;
+    xs[r][t] = (t0 + t < ntok && r < R) ? x[(t0 + t) * ldx + r] : 0.f;
   }
   __syncthreads();
-  const int d = blockIdx.x * DTP_THREADS + threadIdx.x;
-  if (d >= Dn) return;
-  float w[RP];
+  int dch[CH];
+  bool vch[CH];
+  float w[CH][RP], b[CH];
 #pragma unroll
-  for (int r = 0; r < RP; ++r) w[r] = r < R ? W[int64_t(d) * R + r] : 0.f;
-  const float b = bias[d];
+  for (int c = 0; c < CH; ++c) {
+    dch[c] = blockIdx.x * DTP_THREADS * CH + c * DTP_THREADS + threadIdx.x;
+    vch[c] = dch[c] < Dn;
+#pragma unroll
+    for (int r = 0; r < RP; ++r) w[c][r] = (vch[c] && r < R) ? W[int64_t(dch[c]) * R + r] : 0.f;
+    b[c] = vch[c] ? bias[dch[c]] : 0.f;
+  }
   const int nt = int(min(int64_t(DTP_TOKENS), ntok - t0));
-  for (int t = 0; t < nt; ++t) {
-    // two interleaved chains shorten the dependent FMA sequence
-    float a0 = b, a1 = 0.f;
-#pragma unroll
-    for (int r = 0; r < RP; r += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(&xs[t][r]);
-      a0 = fmaf(xv.x, w[r], a0);
-      a1 = fmaf(xv.y, w[r + 1], a1);
-      a0 = fmaf(xv.z, w[r + 2], a0);
-      a1 = fmaf(xv.w, w[r + 3], a1);
-    }
-    const float pre = a0 + a1;
-    const int64_t tt = t0 + t;
+  // DTP_U = 4 tokens per iteration as two packed pairs (rows past nt are zero
+  // in xs; their results are not stored); the VJP's loads of the incoming
+  // gradient for the 4 tokens are issued first
+  for (int tb = 0; tb < nt; tb += DTP_U) {
+    float g[CH][DTP_U];
     if (BWD) {
-      const float sig = __fdividef(1.0f, 1.0f + __expf(-pre));
-      out[tt * ldo + d] = gin[tt * ldg + d] * sig;
-    } else {
-      out[tt * ldo + d] = softplus_ref(pre);
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+#pragma unroll
+        for (int u = 0; u < DTP_U; ++u)
+          g[c][u] = (vch[c] && tb + u < nt) ? gin[(t0 + tb + u) * ldg + dch[c]] : 0.f;
+    }
+    float2 a01[CH], a23[CH];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) a01[c] = a23[c] = make_float2(b[c], b[c]);
+#pragma unroll
+    for (int r = 0; r < RP; ++r) {
+      const float4 xv = *reinterpret_cast<const float4*>(&xs[r][tb]);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const float2 wr = make_float2(w[c][r], w[c][r]);
+        a01[c] = fma2(make_float2(xv.x, xv.y), wr, a01[c]);
+        a23[c] = fma2(make_float2(xv.z, xv.w), wr, a23[c]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const float pre[DTP_U] = {a01[c].x, a01[c].y, a23[c].x, a23[c].y};
+#pragma unroll
+      for (int u = 0; u < DTP_U; ++u) {
+        if (vch[c] && tb + u < nt) {
+          const int64_t tt = t0 + tb + u;
+          if (BWD) {
+            const float sig = __fdividef(1.0f, 1.0f + __expf(-pre[u]));
+            out[tt * ldo + dch[c]] = g[c][u] * sig;
+          } else {
+            out[tt * ldo + dch[c]] = softplus_ref(pre[u]);
+          }
+        }
+      }
     }
   }
 }
