@@ -52,6 +52,29 @@ def bwd_bytes(b, l, d, n=N_STATE, es=4):
     return es * (7 * b * l * d + 4 * b * l * n) + 4 * (2 * d * n + 2 * d)
 
 
+# MUFU (exp2 / reciprocal) operations per (token, channel) of the gated scan:
+# forward 16 decays exp(delta A) + 2 for the gate's sigmoid; VJP 16 decays in
+# the recompute + 16 in the reverse pass + 2 for the gate.  The B200 SM
+# retires 16 MUFU results per clock.
+MUFU_PER_TD = {"fwd": 18, "bwd": 34}
+MUFU_PER_SM_CLK = 16
+
+
+def mufu_roofline(b, l, d, fwd_ms, bwd_ms, clk, sms=148):
+    """Compute roofline of the scan kernels on the exp unit: MUFU operations
+    per launch / time, against 16 results per SM per clock at the median SM
+    clock sampled during the timed region (the scans are bound by it rather
+    than by HBM)."""
+    mhz = (clk or {}).get("sm_mhz") or 1965.0
+    peak = MUFU_PER_SM_CLK * sms * mhz * 1e6 / 1e12  # T ops/s
+    out = {"unit": "Tops/s", "peak": peak, "peak_source": f"16 per SM per clock x {sms} SMs x {mhz:.0f} MHz"}
+    for name, ms in (("fwd", fwd_ms), ("bwd", bwd_ms)):
+        ops = MUFU_PER_TD[name] * b * l * d
+        out[name] = {"ops_per_launch": ops, "achieved": ops / (ms / 1e3) / 1e12,
+                     "frac": ops / (ms / 1e3) / 1e12 / peak}
+    return out
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -453,6 +476,8 @@ def main():
                 "fwd": {"kernel": "scan_fwd_kernel", "achieved": fwd_gbs, "frac": fwd_gbs / peak,
                         "algorithmic_bytes_per_launch": fb, "traffic": profiled_traffic("scan_fwd_kernel")},
                 "fwd_plus_bwd_frac": value / world / peak,
+                "mufu": mufu_roofline(b, l, d, fwd_ms, bwd_ms, clk,
+                                      sms=torch.cuda.get_device_properties(dev).multi_processor_count),
             },
             "gpu_launches": 4 * K,
             "clocks": clk,
