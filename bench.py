@@ -704,6 +704,7 @@ def time_dt(dev, iters=20):
     bias = torch.randn(dn, device=dev, generator=g)
     gin = torch.randn(ntok, dn, device=dev, generator=g)
     out = torch.empty(ntok, dn, device=dev)
+    part = torch.empty(lib.vmscan_dt_softplus_bias_rows(ntok), dn, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
     st = torch.cuda.current_stream(dev)
     sp = ctypes.c_void_p(st.cuda_stream)
@@ -715,7 +716,7 @@ def time_dt(dev, iters=20):
 
     def bwd():
         assert lib.vmscan_dt_softplus_bwd(ntok, r, dn, xw.data_ptr(), wide, w.data_ptr(), bias.data_ptr(),
-                                          gin.data_ptr(), dn, out.data_ptr(), dn, sp) == 0
+                                          gin.data_ptr(), dn, out.data_ptr(), dn, part.data_ptr(), sp) == 0
 
     res = {"shape": f"{ntok} tokens, dt_rank {r}, d_inner {dn}", "api": "vmscan_dt_softplus_fwd / _bwd"}
     for name, fn, byt in (("fwd", fwd, 4 * ntok * dn), ("bwd", bwd, 8 * ntok * dn)):

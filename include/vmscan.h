@@ -306,16 +306,22 @@ int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
 /*
  * Softplus part of the VJP of vmscan_dt_softplus_fwd: dpre = ddelta *
  * sigmoid(pre) with pre recomputed from x, weight, bias (the gradient the
- * reference's autograd forms through log(1 + exp(.))).  dx = dpre weight,
- * dweight = dpre^T x and dbias = column sums of dpre are left to the caller
- * (plain GEMMs).
+ * reference's autograd forms through log(1 + exp(.))).  dx = dpre weight and
+ * dweight = dpre^T x are left to the caller (plain GEMMs).  When dbias_part
+ * is not NULL it receives, as vmscan_dt_softplus_bias_rows(ntok) x d_inner
+ * contiguous floats, the column sums of dpre over consecutive groups of
+ * tokens; dbias is the sum of its rows (a small reduction for the caller).
  */
 int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
                            const float* x, int64_t ldx,
                            const float* weight, const float* bias,
                            const float* ddelta, int64_t ld_ddelta,
                            float* dpre, int64_t ld_dpre,
+                           float* dbias_part,
                            vmscan_stream_t stream);
+
+/* Rows of the dbias_part array of vmscan_dt_softplus_bwd for ntok tokens. */
+int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
 
 /*
  * Host-only introspection (no CUDA call): writes the token index visited at

@@ -109,7 +109,8 @@ SIGNATURES = {
         [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _p, _S, _p, _p, _D, _p, _sz, _p],
     ),
     "vmscan_dt_softplus_fwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p]),
-    "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p]),
+    "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p]),
+    "vmscan_dt_softplus_bias_rows": (_i64, [_i64]),
     "vmscan_scan_order": (ctypes.c_int, [_i64, _D, ctypes.c_int, _p, _p]),
     "vmscan_device_status": (ctypes.c_int, [_p, ctypes.c_int]),
     "vmscan_wait_timeout_selftest": (ctypes.c_int, [ctypes.c_uint32, _p]),

@@ -567,7 +567,7 @@ namespace {
 template <bool BWD>
 int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
                        const float* weight, const float* bias, const float* gin, int64_t ldg, float* out,
-                       int64_t ldo, vmscan_stream_t stream) {
+                       int64_t ldo, float* bpart, vmscan_stream_t stream) {
   if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr || (BWD && gin == nullptr))
     return VMSCAN_ERR_NULL;
   if (ntok <= 0 || d_inner <= 0 || d_inner > INT32_MAX || dt_rank < 1 || dt_rank > DTP_RMAX)
@@ -584,7 +584,7 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
 #define VM_DTP(RP)                                                                                           \
   dt_softplus_kernel<RP, BWD>                                                                                \
       <<<dim3(unsigned((d_inner + DTP_THREADS * dtp_channels(RP) - 1) / (DTP_THREADS * dtp_channels(RP))), ty), \
-         DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, ntok, D)
+         DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, bpart, ntok, D)
   if (R <= 8)
     VM_DTP(8);
   else if (R <= 16)
@@ -724,14 +724,19 @@ int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const
                            const float* weight, const float* bias, float* delta, int64_t ld_delta,
                            vmscan_stream_t stream) {
   return launch_dt_softplus<false>(ntok, dt_rank, d_inner, x, ldx, weight, bias, nullptr, 0, delta, ld_delta,
-                                   stream);
+                                   nullptr, stream);
+}
+
+int64_t vmscan_dt_softplus_bias_rows(int64_t ntok) {
+  if (ntok <= 0) return -VMSCAN_ERR_SHAPE;
+  return (ntok + DTP_TOKENS - 1) / DTP_TOKENS;
 }
 
 int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
                            const float* weight, const float* bias, const float* ddelta, int64_t ld_ddelta,
-                           float* dpre, int64_t ld_dpre, vmscan_stream_t stream) {
+                           float* dpre, int64_t ld_dpre, float* dbias_part, vmscan_stream_t stream) {
   return launch_dt_softplus<true>(ntok, dt_rank, d_inner, x, ldx, weight, bias, ddelta, ld_ddelta, dpre, ld_dpre,
-                                  stream);
+                                  dbias_part, stream);
 }
 
 int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,

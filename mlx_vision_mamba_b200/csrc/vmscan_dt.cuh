@@ -44,13 +44,15 @@ __device__ __forceinline__ float softplus_ref(float v) { return __logf(1.0f + __
 constexpr int DTP_XROW = DTP_TOKENS + 4;
 
 // RP: dt_rank rounded up to a multiple of 4 (<= DTP_RMAX).  BWD: write
-// dpre = gin * sigmoid(pre) instead of softplus(pre).  A CTA covers
+// dpre = gin * sigmoid(pre) instead of softplus(pre), and when bpart is given
+// the sum of dpre over the CTA's tokens per channel into row blockIdx.y of
+// bpart (the dbias partials; summed over rows by the caller).  A CTA covers
 // DTP_THREADS * dtp_channels(RP) channels x DTP_TOKENS tokens.
 template <int RP, bool BWD>
 __global__ void __launch_bounds__(DTP_THREADS)
     dt_softplus_kernel(const float* __restrict__ x, int64_t ldx, int R, const float* __restrict__ W,
                        const float* __restrict__ bias, const float* __restrict__ gin, int64_t ldg,
-                       float* __restrict__ out, int64_t ldo, int64_t ntok, int Dn) {
+                       float* __restrict__ out, int64_t ldo, float* __restrict__ bpart, int64_t ntok, int Dn) {
   constexpr int CH = dtp_channels(RP);
   // xs[r][t]: x of token t0 + t at rank index r (transposed, so one 128-bit
   // load gives 4 tokens' values of one r for the packed FMAs below)
@@ -73,6 +75,9 @@ __global__ void __launch_bounds__(DTP_THREADS)
     b[c] = vch[c] ? bias[dch[c]] : 0.f;
   }
   const int nt = int(min(int64_t(DTP_TOKENS), ntok - t0));
+  float bsum[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) bsum[c] = 0.f;
   // DTP_U = 4 tokens per iteration as two packed pairs (rows past nt are zero
   // in xs; their results are not stored); the VJP's loads of the incoming
   // gradient for the 4 tokens are issued first
@@ -107,13 +112,20 @@ __global__ void __launch_bounds__(DTP_THREADS)
           const int64_t tt = t0 + tb + u;
           if (BWD) {
             const float sig = __fdividef(1.0f, 1.0f + __expf(-pre[u]));
-            out[tt * ldo + dch[c]] = g[c][u] * sig;
+            const float dp = g[c][u] * sig;
+            out[tt * ldo + dch[c]] = dp;
+            bsum[c] += dp;
           } else {
             out[tt * ldo + dch[c]] = softplus_ref(pre[u]);
           }
         }
       }
     }
+  }
+  if (BWD && bpart != nullptr) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+      if (vch[c]) bpart[int64_t(blockIdx.y) * Dn + dch[c]] = bsum[c];
   }
 }
 

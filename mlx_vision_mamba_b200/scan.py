@@ -340,13 +340,16 @@ class _DtSoftplusFn(torch.autograd.Function):
         dn = w_.shape[0]
         g_in = _token_rows(ddelta)
         dpre = _empty_seq(b, l, dn, x_.device)
+        # dbias: the kernel sums dpre over each group of tokens it handles;
+        # the rows of those partials are added here (a small reduction)
+        part = torch.empty((lib.vmscan_dt_softplus_bias_rows(b * l), dn), dtype=torch.float32, device=x_.device)
         st = lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(x_), x_.stride(1), _ptr(w_), _ptr(b_), _ptr(g_in),
-                                        g_in.stride(1), _ptr(dpre), dpre.stride(1), _stream(x_))
+                                        g_in.stride(1), _ptr(dpre), dpre.stride(1), _ptr(part), _stream(x_))
         _native.check(st, "vmscan_dt_softplus_bwd")
         g2 = dpre.reshape(b * l, dn)
         dx = (g2 @ w_).reshape(b, l, r)
         dw = g2.t() @ x_.reshape(b * l, r)
-        db = g2.sum(0)
+        db = part.sum(0)
         return dx, dw, db
 
 
