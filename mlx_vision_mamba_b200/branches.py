@@ -1,0 +1,206 @@
+"""The K direction branches of a (multi-directional) Mamba block as one
+autograd node.
+
+Between in_proj and out_proj each direction k runs (mamba_block.py:166-190)
+
+    x, z   = split(xz_k)                       (in_proj output, 2 d_inner wide)
+    xc     = silu(conv1d(x))                   along the direction's scan order
+    x_dbc  = x_proj(xc)                        -> (dt, B, C)
+    delta  = softplus(dt_proj(dt))
+    y_k    = selective_scan(xc, delta, -exp(A_log), B, C, D) * silu(z)
+
+and the block's output is out_proj(concat_k y_k) (mamba_block.py:562-566 sums
+the K block outputs; one out_proj GEMM over the concatenated inner dimension
+performs that sum).
+
+Built from separate autograd nodes, PyTorch copies the branch outputs into
+the concatenation, concatenates the gradients of every split (x and z of
+each branch, then the K branches), and adds the scan's du to the x_proj
+input gradient in a separate pass.  Here the branches write y_k straight into
+their slice of one (B, L, K d_inner) output, the VJP writes dx and dz straight
+into their slices of one (B, L, K 2 d_inner) gradient (the kernels take
+strided outputs), the scan's dB / dC land in the slices of the x_proj-output
+gradient, and the x_proj GEMM adds its input gradient onto du in place.  The
+kernels and GEMMs are the same as the per-node path's; branches run on their
+own CUDA streams as there.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _native
+from .direction import ScanDirection
+from .scan import _dir_ptr, _empty_seq, _prepare, _ptr, _strides, _tma_compatible
+
+D_STATE = 16
+PARAMS_PER_BLOCK = 7  # conv weight, conv bias, x_proj weight, dt_proj weight, dt_proj bias, A_log, D
+
+
+def block_params(block) -> List[torch.Tensor]:
+    return [block.conv1d.weight, block.conv1d.bias, block.x_proj.weight, block.dt_proj.weight, block.dt_proj.bias,
+            block.A_log, block.D]
+
+
+def _stream_ptr(s: torch.cuda.Stream) -> ctypes.c_void_p:
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _seq_view(t: torch.Tensor, b: int, l: int) -> torch.Tensor:
+    """(B*L, C) row-major rows (possibly a column slice) as a (B, L, C) view."""
+    return t.view(b, l, t.shape[-1]) if t.is_contiguous() else t.unflatten(0, (b, l))
+
+
+class _BranchesFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xz, meta, *params):
+        lib = _native.load()
+        dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
+        kb = len(dirs)
+        n = D_STATE
+        b, l, _ = xz.shape
+        dev = xz.device
+        wide = r + 2 * n
+        cur = torch.cuda.current_stream(dev)
+        y_all = _empty_seq(b, l, kb * dn, dev)
+        need_grad = any(ctx.needs_input_grad)
+        saved = []
+        for k in range(kb):
+            conv_w, conv_b, xproj_w, dt_w, dt_b, a_log, d_skip = params[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)]
+            s = streams[k]
+            s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                sp = _stream_ptr(s)
+                dptr = _dir_ptr(dirs[k])
+                x = xz[:, :, 2 * dn * k:2 * dn * k + dn]
+                z = xz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
+                if not (_tma_compatible(x) and _tma_compatible(z)):
+                    x, z = _prepare(x), _prepare(z)
+                cw = conv_w.detach().contiguous()
+                cb = conv_b.detach().contiguous()
+                xc = _empty_seq(b, l, dn, dev)
+                _native.check(lib.vmscan_conv1d_silu_fwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
+                                                         _ptr(xc), _strides(xc), dptr, sp), "vmscan_conv1d_silu_fwd")
+                xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
+                dw_ = dt_w.detach().contiguous()
+                db_ = dt_b.detach().contiguous()
+                delta = _empty_seq(b, l, dn, dev)
+                _native.check(lib.vmscan_dt_softplus_fwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
+                                                         _ptr(delta), delta.stride(1), sp), "vmscan_dt_softplus_fwd")
+                a = -torch.exp(a_log.detach())
+                bmat = _prepare(_seq_view(xdbc[:, r:r + n], b, l))
+                cmat = _prepare(_seq_view(xdbc[:, r + n:], b, l))
+                dsk = d_skip.detach().contiguous()
+                y = y_all[:, :, dn * k:dn * (k + 1)]
+                ckpt = None
+                if need_grad:
+                    n_ck = lib.vmscan_ckpt_elems(b, l, dn, D_STATE, dptr)
+                    if n_ck < 0:
+                        _native.check(-n_ck, "vmscan_ckpt_elems")
+                    ckpt = torch.empty(n_ck, dtype=torch.float32, device=dev)
+                fws_n = lib.vmscan_fwd_workspace_bytes(b, l, dn, D_STATE, dptr)
+                if fws_n < 0:
+                    _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
+                fws = torch.empty(int(fws_n), dtype=torch.uint8, device=dev) if fws_n > 0 else None
+                _native.check(lib.vmscan_fwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
+                                             _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
+                                             _ptr(dsk), _ptr(z), _strides(z), _ptr(y), _strides(y), _ptr(ckpt), dptr,
+                                             _ptr(fws), int(fws_n), sp), "vmscan_fwd")
+                saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt))
+        for s in streams[:kb]:
+            cur.wait_stream(s)
+        if need_grad:
+            ctx.saved = saved
+            ctx.xproj = [params[PARAMS_PER_BLOCK * k + 2] for k in range(kb)]
+            ctx.meta = meta
+            ctx.xz_shape = xz.shape
+        return y_all
+
+    @staticmethod
+    def backward(ctx, dy_all):
+        lib = _native.load()
+        meta = ctx.meta
+        dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
+        kb = len(dirs)
+        n = D_STATE
+        b, l, _ = ctx.xz_shape
+        dev = dy_all.device
+        wide = r + 2 * n
+        cur = torch.cuda.current_stream(dev)
+        dxz = _empty_seq(b, l, kb * 2 * dn, dev)
+        grads: List[Optional[torch.Tensor]] = [None] * (PARAMS_PER_BLOCK * kb)
+        for k in range(kb):
+            x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt = ctx.saved[k]
+            xproj_w = ctx.xproj[k].detach()
+            s = streams[k]
+            s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                sp = _stream_ptr(s)
+                dptr = _dir_ptr(dirs[k])
+                dy = _prepare(dy_all[:, :, dn * k:dn * (k + 1)])
+                du = _empty_seq(b, l, dn, dev)
+                ddelta = _empty_seq(b, l, dn, dev)
+                dA = torch.empty((dn, n), dtype=torch.float32, device=dev)
+                dD = torch.empty((dn,), dtype=torch.float32, device=dev)
+                dxdbc = torch.empty((b * l, wide), dtype=torch.float32, device=dev)
+                dB = _seq_view(dxdbc[:, r:r + n], b, l)
+                dC = _seq_view(dxdbc[:, r + n:], b, l)
+                dz = dxz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
+                ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, D_STATE, dptr, 0)
+                if ws_n < 0:
+                    _native.check(-ws_n, "vmscan_bwd_workspace_bytes")
+                ws = torch.empty(max(int(ws_n), 256), dtype=torch.uint8, device=dev)
+                _native.check(lib.vmscan_bwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
+                                             _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
+                                             _ptr(dsk), _ptr(z), _strides(z), _ptr(ckpt), _ptr(dy), _strides(dy),
+                                             _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta), _ptr(dA),
+                                             _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD), _ptr(dz),
+                                             _strides(dz), dptr, _ptr(ws), ws.numel(), sp), "vmscan_bwd")
+                # dt_proj + softplus: dpre, then its GEMMs; dbias from the kernel's partial sums
+                dpre = _empty_seq(b, l, dn, dev)
+                part = torch.empty((lib.vmscan_dt_softplus_bias_rows(b * l), dn), dtype=torch.float32, device=dev)
+                _native.check(lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
+                                                         _ptr(ddelta), ddelta.stride(1), _ptr(dpre), dpre.stride(1),
+                                                         _ptr(part), sp), "vmscan_dt_softplus_bwd")
+                dpre2 = dpre.reshape(b * l, dn)
+                dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
+                g_dt_w = torch.mm(dpre2.t(), xdbc[:, :r])
+                g_dt_b = part.sum(0)
+                # x_proj: its input gradient lands on du in place (du += dx_dbc W)
+                du2 = du.view(b * l, dn)
+                du2.addmm_(dxdbc, xproj_w)
+                g_xproj = torch.mm(dxdbc.t(), xc.reshape(b * l, dn))
+                # conv1d + SiLU: dx straight into its slice of dxz
+                dx = dxz[:, :, 2 * dn * k:2 * dn * k + dn]
+                g_cw = torch.empty_like(cw)
+                g_cb = torch.empty_like(cb)
+                cws_n = lib.vmscan_conv1d_bwd_workspace_bytes(b, l, dn, ksize)
+                if cws_n < 0:
+                    _native.check(-cws_n, "vmscan_conv1d_bwd_workspace_bytes")
+                cws = torch.empty(int(cws_n), dtype=torch.uint8, device=dev)
+                _native.check(lib.vmscan_conv1d_silu_bwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
+                                                         _ptr(du), _strides(du), _ptr(dx), _strides(dx), _ptr(g_cw),
+                                                         _ptr(g_cb), dptr, _ptr(cws), cws.numel(), sp),
+                              "vmscan_conv1d_silu_bwd")
+                # A = -exp(A_log): dA_log = dA * A
+                g_alog = dA * a
+                grads[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)] = [g_cw, g_cb, g_xproj, g_dt_w, g_dt_b, g_alog,
+                                                                          dD]
+        for s in streams[:kb]:
+            cur.wait_stream(s)
+        ctx.saved = None
+        return (dxz, None, *grads)
+
+
+def branches_forward(blocks: Sequence, directions: Sequence[Optional[ScanDirection]], xz: torch.Tensor,
+                     streams: Sequence[torch.cuda.Stream]) -> torch.Tensor:
+    """y = concat_k scan_branch_k(xz_k) for K MambaBlocks sharing one in_proj
+    output xz (B, L, K 2 d_inner), as one autograd node; returns (B, L, K d_inner)."""
+    b0 = blocks[0]
+    meta = {"d_inner": b0.d_inner, "dt_rank": b0.dt_rank, "d_conv": b0.d_conv, "dirs": list(directions),
+            "streams": list(streams)}
+    params = [p for blk in blocks for p in block_params(blk)]
+    return _BranchesFn.apply(xz.contiguous(), meta, *params)

@@ -26,6 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .direction import BACKWARD, ScanDirection, directions_for
+from .branches import branches_forward
 from .scan import conv1d_silu_cuda, dt_softplus_cuda, selective_scan_cuda
 
 GPU_SCAN_MODES = ("cuda_fused", "metal_fused", "metal_train", "metal")
@@ -114,6 +115,9 @@ class MambaBlock(nn.Module):
         self.out_proj = Linear(self.d_inner, d_model, bias=False)
 
     def forward(self, x: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
+        if _fused_branches_ok([self], x):
+            xz = self.in_proj(x)
+            return self.out_proj(branches_forward([self], [direction], xz, _branch_streams(x.device, 1)))
         return self.out_proj(self.scan_branch(self.in_proj(x), direction))
 
     def scan_branch(self, xz: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
@@ -144,12 +148,29 @@ def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[S
         return blocks[0](h, directions[0])
     two_dn = 2 * blocks[0].d_inner
     xz = F.linear(h, torch.cat([b.in_proj.weight for b in blocks], 0))
+    if _fused_branches_ok(blocks, h):
+        # one autograd node for the K branches: outputs and input gradients
+        # written into slices, no concatenation passes (branches.py)
+        y = branches_forward(blocks, directions, xz, _branch_streams(h.device, len(blocks)))
+        return F.linear(y, torch.cat([b.out_proj.weight for b in blocks], 1))
     parts = torch.split(xz, two_dn, dim=-1)
     if h.is_cuda:
         ys = _branches_on_streams(blocks, directions, parts)
     else:
         ys = [b.scan_branch(part, d) for b, d, part in zip(blocks, directions, parts)]
     return F.linear(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
+
+
+def _fused_branches_ok(blocks, h: torch.Tensor) -> bool:
+    """The fused K-branch node applies to CUDA inputs of real MambaBlocks with
+    one geometry and d_inner a multiple of 4 (its in-place x_proj gradient
+    needs contiguous rows)."""
+    if not h.is_cuda or not all(isinstance(b, MambaBlock) for b in blocks):
+        return False
+    b0 = blocks[0]
+    same = all((b.d_inner, b.dt_rank, b.d_conv, b.d_state) == (b0.d_inner, b0.dt_rank, b0.d_conv, b0.d_state)
+               for b in blocks)
+    return same and b0.d_inner % 4 == 0 and b0.d_state == 16
 
 
 _STREAMS = {}
