@@ -824,10 +824,12 @@ def profile_model(warmup):
     rows = sorted(((e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0),
                   reverse=True)
     total = sum(r[0] for r in rows)
-    groups = {"gemm": 0.0, "scan_bwd": 0.0, "scan_fwd": 0.0, "conv": 0.0, "vmscan_reduce": 0.0, "other": 0.0}
+    groups = {"gemm": 0.0, "scan_bwd": 0.0, "scan_fwd": 0.0, "conv": 0.0, "dt_proj": 0.0, "vmscan_reduce": 0.0,
+              "other": 0.0}
     for t_us, _, key in rows:
         k = ("gemm" if "gemm" in key else "scan_bwd" if "scan_bwd_kernel" in key else
              "scan_fwd" if "scan_fwd_kernel" in key else "conv" if "vmscan::conv" in key else
+             "dt_proj" if "vmscan::dt_softplus" in key else
              "vmscan_reduce" if "vmscan::reduce" in key else "other")
         groups[k] += t_us
     print(f"total device time per step: {total / steps / 1e3:.2f} ms")
