@@ -45,6 +45,19 @@ def block_params(block) -> List[torch.Tensor]:
             block.A_log, block.D]
 
 
+def _mm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a^T b for tall a (K, M) and b (K, N) with small M, N (the weight
+    gradients of x_proj and dt_proj, K = batch x tokens): K is split into S
+    equal chunks summed after one batched GEMM, which keeps more of the GPU
+    busy than cuBLAS's single skinny GEMM (measured 83 -> 54 us and 72 -> 46
+    us at K = 12544) and sums in a fixed order."""
+    k = a.shape[0]
+    for s in (16, 8, 4, 2):
+        if k % s == 0 and k // s >= 256:
+            return torch.bmm(a.reshape(s, k // s, a.shape[1]).transpose(1, 2), b.reshape(s, k // s, b.shape[1])).sum(0)
+    return a.t() @ b
+
+
 def _stream_ptr(s: torch.cuda.Stream) -> ctypes.c_void_p:
     return ctypes.c_void_p(s.cuda_stream)
 
@@ -167,12 +180,12 @@ class _BranchesFn(torch.autograd.Function):
                                                          _ptr(part), sp), "vmscan_dt_softplus_bwd")
                 dpre2 = dpre.reshape(b * l, dn)
                 dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
-                g_dt_w = torch.mm(dpre2.t(), xdbc[:, :r])
+                g_dt_w = _mm_tn(dpre2, xdbc[:, :r])
                 g_dt_b = part.sum(0)
                 # x_proj: its input gradient lands on du in place (du += dx_dbc W)
                 du2 = du.view(b * l, dn)
                 du2.addmm_(dxdbc, xproj_w)
-                g_xproj = torch.mm(dxdbc.t(), xc.reshape(b * l, dn))
+                g_xproj = _mm_tn(dxdbc, xc.reshape(b * l, dn))
                 # conv1d + SiLU: dx straight into its slice of dxz
                 dx = dxz[:, :, 2 * dn * k:2 * dn * k + dn]
                 g_cw = torch.empty_like(cw)
