@@ -143,3 +143,50 @@ def test_graphed_training_step_matches_eager():
     torch.testing.assert_close(torch.tensor(losses_g), torch.tensor(losses_e[11:]), rtol=1e-5, atol=1e-6)
     for (k, p), q in zip(eager.named_parameters(), graphed.parameters()):
         torch.testing.assert_close(q.detach(), p.detach(), rtol=1e-5, atol=1e-6, msg=k)
+
+
+@pytest.mark.parametrize("K,grid", [(2, None), (4, (14, 14))])
+def test_fused_branch_node_matches_per_node_autograd(K, grid):
+    """branches.py's single autograd node for the K direction branches (outputs
+    and gradients written into slices, x_proj input gradient added in place,
+    split-K weight gradients) against the same kernels composed as separate
+    autograd nodes (MambaBlock.scan_branch per direction)."""
+    import torch.nn.functional as F
+
+    import mlx_vision_mamba_b200 as vm
+    from mlx_vision_mamba_b200.mamba_block import directions_sum
+
+    torch.manual_seed(1)
+    if K == 2:
+        blk = vm.BidirectionalMambaBlock(64, 16, 4, 2).cuda()
+        blocks, dirs = [blk.forward_mamba, blk.backward_mamba], [None, vm.BACKWARD]
+        L = 100
+    else:
+        blk = vm.MultiDirectionalMambaBlock(64, 16, 4, 2, num_directions=4, grid_shape=grid).cuda()
+        blocks, dirs = list(blk.mamba_blocks), blk.directions
+        L = 196
+    h = torch.randn(2, L, 64, device="cuda")
+    w = torch.randn(2, L, 64, device="cuda")
+
+    def run(fn):
+        blk.zero_grad(set_to_none=True)
+        hh = h.clone().requires_grad_(True)
+        out = fn(hh)
+        (out * w).sum().backward()
+        torch.cuda.synchronize()
+        return out.detach(), hh.grad.detach(), {k: p.grad.detach().clone() for k, p in blk.named_parameters()
+                                                if p.grad is not None}
+
+    def per_node(hh):
+        xz = F.linear(hh, torch.cat([b.in_proj.weight for b in blocks], 0))
+        parts = torch.split(xz, 2 * blocks[0].d_inner, dim=-1)
+        ys = [b.scan_branch(p, d) for b, d, p in zip(blocks, dirs, parts)]
+        return F.linear(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
+
+    y1, dh1, g1 = run(lambda hh: directions_sum(blocks, dirs, hh))
+    y2, dh2, g2 = run(per_node)
+    torch.testing.assert_close(y1, y2, rtol=1e-6, atol=1e-6)  # the same kernels; GEMM algorithms may differ
+    torch.testing.assert_close(dh1, dh2, rtol=1e-5, atol=1e-6)
+    assert g1.keys() == g2.keys()
+    for k in g1:
+        torch.testing.assert_close(g1[k], g2[k], rtol=1e-5, atol=1e-6, msg=k)
