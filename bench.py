@@ -241,6 +241,18 @@ def cpu_oracle_step(sample, threads, seed=0, chunked=False):
     return time.perf_counter() - t0
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (first "model name" line of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(steps=1, warmup=0, budget_s=20.0):
     """Both CPU restatements of the reference (sequential and chunked scan),
     each timed for about half the budget; the faster one is the baseline."""
@@ -264,6 +276,7 @@ def cpu_baseline(steps=1, warmup=0, budget_s=20.0):
         "value": byt / per / 1e9,
         "unit": "GB/s",
         "cores": threads,
+        "cpu_model": cpu_model(),
         "kind": "port",
         "sample": f"oracle {best} scan fwd+VJP (torch CPU fp32, {threads} threads) on batch "
                   f"{s['batch']} of the same workload (L {s['seqlen']}, d_inner {s['d_inner']}), "
