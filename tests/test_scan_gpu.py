@@ -243,3 +243,45 @@ def test_bounded_wait_times_out_reports_and_context_survives():
     inp = scan_ref.sweep_inputs(1, 40, 24, seed=11)
     check_all(inp, True, tag="after timeout")
     assert lib.vmscan_device_status(stream, 1) == 0
+
+
+def test_abi_rejects_views_that_break_the_tma_rules():
+    """The C ABI reads sequence tensors through TMA: a view whose base is not
+    16-byte aligned or whose strides are not whole 16-byte multiples (4 fp32,
+    8 bf16 elements) is rejected with VMSCAN_ERR_ALIGN before any launch (the
+    Python layer copies such views instead, test_unaligned_channel_count_is_padded)."""
+    lib = _native.load()
+    b, l, dn = 2, 32, 64
+    S = lambda st: _native.Strides(*st)  # noqa: E731
+    dev = "cuda"
+    A = -torch.arange(1, 17, dtype=torch.float32, device=dev).repeat(dn, 1)
+    D = torch.ones(dn, device=dev)
+    y = torch.empty(b, l, dn, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    good = torch.randn(b, l, dn, device=dev)
+    bc = torch.randn(b, l, 16, device=dev)
+
+    def fwd(u, su, dt=good, sdt=(l * dn, dn)):
+        return lib.vmscan_fwd(b, l, dn, 16, u, S(su), dt.data_ptr(), S(sdt), A.data_ptr(), bc.data_ptr(),
+                              S((l * 16, 16)), bc.data_ptr(), S((l * 16, 16)), D.data_ptr(), None, S((0, 0)),
+                              y.data_ptr(), S((l * dn, dn)), None, None, None, 0, stream)
+
+    assert fwd(good.data_ptr(), (l * dn, dn)) == 0
+    wide = torch.randn(b, l, dn + 2, device=dev)  # seq stride 66: not a multiple of 4
+    assert fwd(wide.data_ptr(), (l * (dn + 2), dn + 2)) == 4
+    assert b"u" in lib.vmscan_last_error()
+    assert fwd(good.data_ptr() + 4, (l * dn, dn)) == 4  # base one float past a 16-byte boundary
+    assert fwd(good.data_ptr(), (l * dn, dn), dt=wide, sdt=(l * (dn + 2), dn + 2)) == 4
+    assert b"delta" in lib.vmscan_last_error()
+    # bf16: strides must be multiples of 8 elements
+    gb = torch.randn(b, l, dn + 4, device=dev).to(torch.bfloat16)  # seq stride 68: multiple of 4, not 8
+    gd = torch.randn(b, l, dn, device=dev).to(torch.bfloat16)
+    bcb = bc.to(torch.bfloat16)
+    yb = torch.empty(b, l, dn, device=dev, dtype=torch.bfloat16)
+    rc = lib.vmscan_fwd_bf16(b, l, dn, 16, gb.data_ptr(), S((l * (dn + 4), dn + 4)), gd.data_ptr(), S((l * dn, dn)),
+                             A.data_ptr(), bcb.data_ptr(), S((l * 16, 16)), bcb.data_ptr(), S((l * 16, 16)),
+                             D.data_ptr(), None, S((0, 0)), yb.data_ptr(), S((l * dn, dn)), None, None, None, 0,
+                             stream)
+    assert rc == 4
+    torch.cuda.synchronize()
+    assert device_status() == 0
