@@ -98,6 +98,32 @@ def train_step(model, optimizer, x, target) -> torch.Tensor:
     return loss.detach()
 
 
+def _unwrap(model: torch.nn.Module) -> torch.nn.Module:
+    return model.module if isinstance(model, torch.nn.parallel.DistributedDataParallel) else model
+
+
+def save_checkpoint(path: str, model: torch.nn.Module, optimizer=None, step: int = 0) -> None:
+    """torch.save of the model's state dict (unwrapped from DDP, so a checkpoint
+    loads into a single-GPU model too), the optimizer's state and the step.
+    Under a process group only rank 0 writes; all ranks hold the same
+    parameters after DDP's all-reduce."""
+    if dist.is_available() and dist.is_initialized() and dist.get_rank() != 0:
+        return
+    torch.save({"model": _unwrap(model).state_dict(),
+                "optimizer": optimizer.state_dict() if optimizer is not None else None,
+                "step": int(step)}, path)
+
+
+def load_checkpoint(path: str, model: torch.nn.Module, optimizer=None, map_location=None) -> int:
+    """Restores what save_checkpoint wrote (every rank reads the file) and
+    returns the saved step."""
+    ck = torch.load(path, map_location=map_location, weights_only=True)
+    _unwrap(model).load_state_dict(ck["model"])
+    if optimizer is not None and ck.get("optimizer") is not None:
+        optimizer.load_state_dict(ck["optimizer"])
+    return int(ck.get("step", 0))
+
+
 def make_optimizer(model, lr: float = 1e-4, capturable: bool = False):
     """AdamW; `capturable` keeps its step counters on the device so the
     update can be replayed inside a CUDA graph."""
