@@ -1,0 +1,88 @@
+"""Parity at the bench workload's full size (batch 64, L 4096, d_inner 1536,
+gated), where the whole oracle does not fit in host memory, through
+properties that hold at any size:
+
+* per-channel parity: the recurrence never crosses channels, so the fp64
+  oracle run on 8 channels (tile edges included) over all 64 rows and all
+  4096 steps gives the exact y, du, ddelta, dz, dA and dD of those channels;
+* linearity in the cotangent: the VJP is linear in dy, so doubling dy
+  doubles every gradient bit for bit;
+* additivity over channels: dB and dC are sums over channels, so the VJP
+  of the two channel halves adds up to the full VJP's dB and dC.
+"""
+
+import pytest
+import torch
+
+from mlx_vision_mamba_b200 import selective_scan_cuda
+from oracle import scan_ref
+from parity import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+B, L, DN = 64, 4096, 1536
+CHANNELS = [0, 1, 127, 128, 700, 1023, 1534, 1535]
+
+
+def full_inputs():
+    g = torch.Generator(device="cuda").manual_seed(2024)
+    f = dict(device="cuda", dtype=torch.float32)
+    t = {
+        "u": torch.randn(B, L, DN, generator=g, **f),
+        "z": torch.randn(B, L, DN, generator=g, **f),
+        "delta": torch.nn.functional.softplus(0.5 * torch.randn(B, L, DN, generator=g, **f) - 3.0),
+        "A": -torch.arange(1, 17, **f).repeat(DN, 1),
+        "B": torch.randn(B, L, 16, generator=g, **f),
+        "C": torch.randn(B, L, 16, generator=g, **f),
+        "D": torch.ones(DN, **f),
+        "dy": torch.randn(B, L, DN, generator=g, **f),
+    }
+    return t
+
+
+def vjp(t, dy, lo=0, hi=DN):
+    lv = {k: (t[k][..., lo:hi] if t[k].shape[-1] == DN and k != "A" else t[k]).clone().requires_grad_(True)
+          for k in ("u", "delta", "z", "B", "C")}
+    a = t["A"][lo:hi].clone().requires_grad_(True)
+    d = t["D"][lo:hi].clone().requires_grad_(True)
+    y = selective_scan_cuda(lv["u"], lv["delta"], a, lv["B"], lv["C"], d, z=lv["z"])
+    y.backward(dy[..., lo:hi])
+    torch.cuda.synchronize()
+    g = {"du": lv["u"].grad, "ddelta": lv["delta"].grad, "dz": lv["z"].grad, "dB": lv["B"].grad,
+         "dC": lv["C"].grad, "dA": a.grad, "dD": d.grad}
+    return y.detach(), g
+
+
+def test_full_size_properties():
+    t = full_inputs()
+    y, g = vjp(t, t["dy"])
+
+    # per-channel parity against the fp64 oracle (8 channels, all rows and steps)
+    idx = torch.tensor(CHANNELS, device="cuda")
+    sub = {k: t[k].index_select(-1, idx).cpu() for k in ("u", "z", "delta", "dy")}
+    sub.update(A=t["A"][idx].cpu(), D=t["D"][idx].cpu(), B=t["B"].cpu(), C=t["C"].cpu())
+    y64, g64 = scan_ref.scan_vjp(sub, gated=True, dtype=torch.float64)
+    y32, g32 = scan_ref.scan_vjp(sub, gated=True, dtype=torch.float32)
+    ic = idx.cpu()
+    assert_parity("full-size y", y.index_select(-1, idx).cpu(), y64, y32)
+    for k in ("du", "ddelta", "dz"):
+        assert_parity(f"full-size {k}", g[k].index_select(-1, idx).cpu(), g64[k], g32[k])
+    # dA / dD sum 262144 terms per element; PyTorch's fp32 reduction of the
+    # oracle is pairwise and so accurate on these 8 channels that the
+    # norm-wise comparison against it is noise: hold them to the north-star
+    # bound itself (rtol 1e-5, atol 1e-6) element by element
+    assert_parity("full-size dA", g["dA"][idx].cpu(), g64["dA"])
+    assert_parity("full-size dD", g["dD"][idx].cpu(), g64["dD"])
+    del sub, y64, g64, y32, g32
+
+    # linearity in dy: exact for a power-of-two scale
+    _, g2 = vjp(t, 2.0 * t["dy"])
+    for k in g:
+        assert torch.equal(g2[k], 2.0 * g[k]), k
+    del g2
+
+    # additivity of dB / dC over the two channel halves
+    _, ga = vjp(t, t["dy"], 0, DN // 2)
+    _, gb = vjp(t, t["dy"], DN // 2, DN)
+    for k in ("dB", "dC"):
+        torch.testing.assert_close(ga[k] + gb[k], g[k], rtol=1e-5, atol=1e-4, msg=k)
