@@ -2,11 +2,11 @@
 """Benchmark of the selective-scan hot path (fused forward + VJP) on B200.
 
 Workload (one "step"): the fused, gated selective scan forward and its VJP on
-the largest point of the op sweep: batch 64, L 4096,
+the largest point of the reference benchmark's op sweep: batch 64, L 4096,
 d_inner 1536, d_state 16, fp32, seeded synthetic inputs with the sweep's
 distributions.  Inputs (6.4 GB) are far larger than L2, so no flush is needed.
 
-value : algorithmic GB/s of fwd+VJP (bytes per SURVEY formulas) over all
+value : algorithmic GB/s of fwd+VJP (fwd_bytes / bwd_bytes below) over all
         ranks, inputs resident in HBM, kernels called through the C ABI,
         device-timed with CUDA events, max over ranks.
 e2e   : the same metric through the public Python API (selective_scan_cuda +
@@ -322,7 +322,7 @@ def main():
     ap.add_argument("--dinner", type=int, default=WORKLOAD["d_inner"])
     ap.add_argument("--model-eager", action="store_true", help="run the model steps eagerly (no CUDA graph)")
     ap.add_argument("--encoder", choices=["3d", "4d"],
-                    help="only time VisionMamba-3D (config 4, K=6, global batch 16) or -4D (config 5, K=8, global "
+                    help="only time VisionMamba-3D (K=6, global batch 16) or -4D (K=8, global "
                          "batch 8) training and print one JSON line")
     ap.add_argument("--parallel", choices=["dp", "dirshard"], default="dp",
                     help="with --encoder: data parallel, or the scan directions split over the ranks")
@@ -432,7 +432,7 @@ def main():
     bwd_gbs = bb / (bwd_ms / 1e3) / 1e9
     fwd_gbs = fb / (fwd_ms / 1e3) / 1e9
 
-    # ---- BASELINE config 1 shape: the reference's only published scan numbers ----
+    # ---- the MambaBlock shape of the reference's only published scan numbers ----
     cfg1 = time_config1(dev, stream) if rank == 0 else None
 
     # ---- the direction-aware conv1d + SiLU kernels at the model's block shape ----
@@ -566,7 +566,7 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
 
 
 def time_config1(dev, stream, iters=50):
-    """Gated scan forward + VJP at BASELINE config 1's shape (batch 2, L 196,
+    """Gated scan forward + VJP at the reference's published MambaBlock shape (batch 2, L 196,
     d_inner 1536: one MambaBlock of d_model 768), median of `iters` launches
     with a 256 MB L2 flush before each.  The reference publishes 1.2 ms for its
     fused Metal scan at this shape on an Apple M5 Pro (README.md:25); that is
@@ -862,8 +862,8 @@ ENCODERS = {
 
 
 def run_encoder(dev, rank, world, which, mode, steps, warmup, barrier):
-    """VisionMamba-3D (BASELINE config 4: K=6, 128^3 volumes, global batch 16)
-    or -4D (config 5: K=8, 8 frames of 64^3, global batch 8) training steps,
+    """VisionMamba-3D (K=6, 128^3 volumes, global batch 16)
+    or -4D (K=8, 8 frames of 64^3, global batch 8) training steps,
     one CUDA graph per step.  "dp": the global batch split over the ranks,
     gradients averaged by DDP.  "dirshard": every rank takes the whole batch
     and runs its share of each layer's scan directions; the direction sums and

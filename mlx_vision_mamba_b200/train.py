@@ -1,8 +1,8 @@
 """Data-parallel training step for the VisionMamba encoders.
 
 The reference has no training loop or distributed code (it runs one MLX
-device); this is the harness of the BASELINE configs 3-5: a VisionMamba
-forward, an MSE loss against a target of the feature shape, backward and an
+device); this is the harness of the VisionMamba 2D / 3D / 4D training
+configurations: a VisionMamba forward, an MSE loss against a target of the feature shape, backward and an
 AdamW update, with the global batch split across one process per GPU and the
 gradients averaged by DistributedDataParallel (bucketed NCCL all-reduce over
 NVLink, overlapped with the backward).  Every function here is model-agnostic
@@ -22,7 +22,7 @@ import torch.nn.functional as F
 
 @dataclass(frozen=True)
 class EncoderConfig:
-    """A VisionMamba training configuration."""
+    """A VisionMamba training configuration (2D K=4, 3D K=6 or 4D K=8 benchmark step)."""
 
     name: str
     input_shape: Tuple[int, ...]  # per-sample input, channel-last
