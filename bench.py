@@ -85,7 +85,7 @@ def measured_peaks():
 
 
 def profiled_traffic(kernel):
-    """Per-launch DRAM bytes of `kernel` on the bench workload from profiles/traffic.md, if recorded."""
+    """Per-launch DRAM bytes of `kernel` on the bench workload from profiles/scan_dram_traffic_b64_l4096_d1536.md, if recorded."""
     p = os.path.join(ROOT, "profiles", "traffic.md")
     if not os.path.exists(p):
         return None
