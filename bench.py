@@ -86,7 +86,7 @@ def measured_peaks():
 
 def profiled_traffic(kernel):
     """Per-launch DRAM bytes of `kernel` on the bench workload from profiles/scan_dram_traffic_b64_l4096_d1536.md, if recorded."""
-    p = os.path.join(ROOT, "profiles", "traffic.md")
+    p = os.path.join(ROOT, "profiles", "scan_dram_traffic_b64_l4096_d1536.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
