@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
 
   struct Carry {
     float yp[2];  // C . h over the lane's 8 states, per channel
+    float uo;     // own channel u (already in registers: no second shared load)
     int r;
   };
 
@@ -215,12 +216,13 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
                 add2(fma2(C2[1], h[c][1], mul2(C2[0], h[c][0])), fma2(C2[3], h[c][3], mul2(C2[2], h[c][2])));
             k.yp[c] = acc.x + acc.y;
           }
+          k.uo = pl.hb ? u2.y : u2.x;
           k.r = r;
         }
       };
       auto epilogue = [&](const Carry& k) {
         const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
-        float yy = fmaf(ld_one(su + k.r * DT + own), Down, ys);
+        float yy = fmaf(k.uo, Down, ys);
         if (HAS_Z) yy *= silu_f(ld_one(sz + k.r * DT + own));
         stg_if_t(ybase + int64_t(tok[k.r]) * sys, yy, ev);
       };

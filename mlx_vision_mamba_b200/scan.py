@@ -129,9 +129,18 @@ def _check_inputs(x, delta, A, B, C, D, z):
 class _SelectiveScanFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, delta, A, B, C, D, z, direction):
-        lib = _native.load()
         bt, l, dn = x.shape
         sd = torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+        ctx.has_z = z is not None
+        ctx.param_dtypes = (A.dtype, D.dtype)
+        ctx.empty = bt * l * dn == 0
+        if ctx.empty:
+            # nothing to scan: zero-size y (or, for D_inner > 0 with no tokens,
+            # no rows); every gradient is zero, dA / dD included
+            ctx.shapes = (x.shape, A.shape, B.shape, D.shape)
+            ctx.sd = sd
+            return torch.zeros((bt, l, dn), dtype=sd, device=x.device)
+        lib = _native.load()
         u_ = _prepare(x, sd)
         dt_ = _prepare(delta, sd)
         B_ = _prepare(B, sd)
@@ -164,12 +173,18 @@ class _SelectiveScanFn(torch.autograd.Function):
         if need_grad:
             ctx.save_for_backward(u_, dt_, A_, B_, C_, D_, z_, ckpt)
         ctx.direction = direction
-        ctx.has_z = z is not None
-        ctx.param_dtypes = (A.dtype, D.dtype)
         return y
 
     @staticmethod
     def backward(ctx, dy):
+        if ctx.empty:
+            xs, As, Bs, Ds = ctx.shapes
+            dev = dy.device
+            seq = torch.zeros(xs, dtype=ctx.sd, device=dev)
+            a_dt, d_dt = ctx.param_dtypes
+            return (seq, seq.clone(), torch.zeros(As, dtype=a_dt, device=dev),
+                    torch.zeros(Bs, dtype=ctx.sd, device=dev), torch.zeros(Bs, dtype=ctx.sd, device=dev),
+                    torch.zeros(Ds, dtype=d_dt, device=dev), seq.clone() if ctx.has_z else None, None)
         lib = _native.load()
         u_, dt_, A_, B_, C_, D_, z_, ckpt = ctx.saved_tensors
         bt, l, dn = u_.shape
@@ -231,8 +246,16 @@ def selective_scan_cuda(
     the sequence tensors (x, delta, B, C, z) are read as bf16 (cast if they
     are not) and y and their gradients are bf16; A, D, the recurrent state and
     all arithmetic stay fp32.  Any other dtype is computed in fp32.
+    A zero batch, sequence length or channel count launches nothing: y is
+    zero-size and every gradient is zero.
     """
     _check_inputs(x, delta, A, B, C, D, z)
+    if direction is not None and direction.grid:
+        n = 1
+        for g in direction.grid:
+            n *= g
+        if n != x.shape[1]:
+            raise ValueError(f"direction grid {direction.grid} does not cover {x.shape[1]} tokens")
     return _SelectiveScanFn.apply(x, delta, A, B, C, D, z, direction)
 
 

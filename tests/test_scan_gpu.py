@@ -186,6 +186,28 @@ def test_errors_are_raised_not_hidden():
         selective_scan_cuda(t["u"], t["delta"], t["A"][:, :8], t["B"][..., :8], t["C"][..., :8], t["D"])
 
 
+@pytest.mark.parametrize("b,l,dn", [(0, 16, 32), (2, 0, 32), (2, 16, 0)])
+@pytest.mark.parametrize("gated", [False, True])
+def test_empty_inputs_give_empty_outputs_and_zero_grads(b, l, dn, gated):
+    g = torch.Generator().manual_seed(0)
+    keys = NAMES + (["z"] if gated else [])
+    shapes = {"u": (b, l, dn), "delta": (b, l, dn), "A": (dn, 16), "B": (b, l, 16), "C": (b, l, 16),
+              "D": (dn,), "z": (b, l, dn)}
+    lv = {k: torch.randn(shapes[k], generator=g).cuda().requires_grad_(True) for k in keys}
+    y = selective_scan_cuda(lv["u"], lv["delta"], lv["A"], lv["B"], lv["C"], lv["D"], z=lv.get("z"))
+    assert tuple(y.shape) == (b, l, dn) and y.dtype == torch.float32
+    y.backward(torch.ones_like(y))
+    for k in keys:
+        assert lv[k].grad is not None and tuple(lv[k].grad.shape) == shapes[k], k
+        assert not lv[k].grad.any(), k
+    assert device_status() == 0
+    # a direction whose grid does not cover the sequence is refused, empty or not
+    with pytest.raises(ValueError, match="does not cover"):
+        selective_scan_cuda(lv["u"], lv["delta"], lv["A"], lv["B"], lv["C"], lv["D"],
+                            direction=ScanDirection(grid=(4, 4), axes=(1, 0)) if l == 0 else
+                            ScanDirection(grid=(4, 5), axes=(1, 0)))
+
+
 def test_device_status_is_clean():
     inp = scan_ref.sweep_inputs(2, 64, 64, seed=1)
     cuda_vjp(inp, True, ScanDirection(reverse=True))
