@@ -61,3 +61,11 @@ def test_conv_directions(K, grid):
         L *= gd
     for k, d in enumerate(directions_for(K, grid)):
         run(2, L, 16, 4, d, seed=100 * K + k)
+
+
+@pytest.mark.parametrize("direction", [None, 1])
+def test_conv_full_grid(direction):
+    """VisionMamba-2D's batch-64 block shape (1344 CTAs, dw/dbias partials of
+    448 (batch, chunk) rows), row-major and column-major scan order."""
+    d = directions_for(4, (14, 14))[direction] if direction is not None else None
+    run(64, 196, 768, 4, d, seed=7 + (direction or 0))

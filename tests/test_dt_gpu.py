@@ -23,6 +23,7 @@ def dt_oracle(x, w, b, dy, dtype):
     "b,l,r,dn,wide,scale",
     [
         (2, 196, 24, 768, 56, 1.0),   # VisionMamba: d_model 384 -> dt_rank 24, x_dbc width 24 + 32
+        (64, 196, 24, 768, 56, 1.0),  # its batch-64 training shape: 196 dbias partial rows
         (1, 196, 48, 1536, 80, 1.0),  # the published MambaBlock shape: d_model 768 -> dt_rank 48
         (3, 37, 5, 10, 5, 1.0),       # ragged: odd rank, channels off every tile, dense rows
         (1, 64, 64, 300, 64, 3.0),    # largest rank, pre-activations far into both tails
