@@ -58,9 +58,21 @@ __global__ void __launch_bounds__(DTP_THREADS)
   // load gives 4 tokens' values of one r for the packed FMAs below)
   __shared__ __align__(16) float xs[RP][DTP_XROW];
   const int64_t t0 = int64_t(blockIdx.y) * DTP_TOKENS;
-  for (int i = threadIdx.x; i < DTP_TOKENS * RP; i += DTP_THREADS) {
+  // staging: every thread's DTP_TOKENS * RP / DTP_THREADS loads are issued
+  // before the first shared-memory store, so their latencies overlap
+  constexpr int NSTG = DTP_TOKENS * RP / DTP_THREADS;
+  static_assert(DTP_TOKENS * RP % DTP_THREADS == 0, "whole staging rounds");
+  float xv[NSTG];
+#pragma unroll
+  for (int j = 0; j < NSTG; ++j) {
+    const int i = threadIdx.x + j * DTP_THREADS;
     const int t = i / RP, r = i % RP;
-    xs[r][t] = (t0 + t < ntok && r < R) ? x[(t0 + t) * ldx + r] : 0.f;
+    xv[j] = (t0 + t < ntok && r < R) ? x[(t0 + t) * ldx + r] : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < NSTG; ++j) {
+    const int i = threadIdx.x + j * DTP_THREADS;
+    xs[i % RP][i / RP] = xv[j];
   }
   __syncthreads();
   int dch[CH];
@@ -79,17 +91,19 @@ __global__ void __launch_bounds__(DTP_THREADS)
 #pragma unroll
   for (int c = 0; c < CH; ++c) bsum[c] = 0.f;
   // DTP_U = 4 tokens per iteration as two packed pairs (rows past nt are zero
-  // in xs; their results are not stored); the VJP's loads of the incoming
-  // gradient for the 4 tokens are issued first
+  // in xs; their results are not stored); the VJP loads the incoming gradient
+  // of the next 4 tokens while it works on the current ones
+  float g[CH][DTP_U], gn[CH][DTP_U];
+  auto load_g = [&](int tb, float (&dst)[CH][DTP_U]) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+      for (int u = 0; u < DTP_U; ++u)
+        dst[c][u] = (vch[c] && tb + u < nt) ? gin[(t0 + tb + u) * ldg + dch[c]] : 0.f;
+  };
+  if (BWD) load_g(0, g);
   for (int tb = 0; tb < nt; tb += DTP_U) {
-    float g[CH][DTP_U];
-    if (BWD) {
-#pragma unroll
-      for (int c = 0; c < CH; ++c)
-#pragma unroll
-        for (int u = 0; u < DTP_U; ++u)
-          g[c][u] = (vch[c] && tb + u < nt) ? gin[(t0 + tb + u) * ldg + dch[c]] : 0.f;
-    }
+    if (BWD) load_g(tb + DTP_U, gn);
     float2 a01[CH], a23[CH];
 #pragma unroll
     for (int c = 0; c < CH; ++c) a01[c] = a23[c] = make_float2(b[c], b[c]);
@@ -120,6 +134,12 @@ __global__ void __launch_bounds__(DTP_THREADS)
           }
         }
       }
+    }
+    if (BWD) {
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+#pragma unroll
+        for (int u = 0; u < DTP_U; ++u) g[c][u] = gn[c][u];
     }
   }
   if (BWD && bpart != nullptr) {
