@@ -126,8 +126,12 @@ def load_checkpoint(path: str, model: torch.nn.Module, optimizer=None, map_locat
 
 def make_optimizer(model, lr: float = 1e-4, capturable: bool = False):
     """AdamW; `capturable` keeps its step counters on the device so the
-    update can be replayed inside a CUDA graph."""
-    return torch.optim.AdamW(model.parameters(), lr=lr, weight_decay=0.05, capturable=capturable)
+    update can be replayed inside a CUDA graph.  Parameters on the GPU use
+    PyTorch's fused AdamW (one pass over parameters, gradients and moments
+    instead of the multi-tensor implementation's several)."""
+    params = list(model.parameters())
+    fused = bool(params) and all(p.is_cuda for p in params)
+    return torch.optim.AdamW(params, lr=lr, weight_decay=0.05, capturable=capturable, fused=fused)
 
 
 class GraphedTrainStep:
