@@ -84,19 +84,36 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernels on the bench workload, from the ncu capture summarised in
+# profiles/scan_dram_traffic_b64_l4096_d1536.md (captured at L 512 on the same
+# grid; every tensor grows in proportion to L, so scaled by 8).  A constant
+# of this file, not read from the summary at run time.
+NCU_TRAFFIC = {
+    "vmscan_bwd": 13072800000,
+    "scan_fwd_kernel": 7819200000,
+}
+
+
 def profiled_traffic(kernel):
-    """Per-launch DRAM bytes of `kernel` on the bench workload from profiles/scan_dram_traffic_b64_l4096_d1536.md, if recorded."""
-    p = os.path.join(ROOT, "profiles", "scan_dram_traffic_b64_l4096_d1536.md")
-    if not os.path.exists(p):
+    """Per-launch DRAM bytes of `kernel` on the default bench workload, or None
+    for another workload (not captured)."""
+    if (WORKLOAD["batch"], WORKLOAD["seqlen"], WORKLOAD["d_inner"]) != (64, 4096, 1536):
         return None
-    for line in open(p):
-        cells = [c.strip() for c in line.strip().strip("|").split("|")]
-        if len(cells) >= 3 and cells[0] == kernel:
-            try:
-                return float(cells[2])
-            except ValueError:
-                return None
-    return None
+    return NCU_TRAFFIC.get(kernel)
+
+
+def check_status(where):
+    """Fail the run if a scan kernel gave up a bounded device wait (its outputs
+    would be wrong): vmscan_device_status synchronises and clears the sticky
+    status word."""
+    import torch
+
+    from mlx_vision_mamba_b200 import device_status
+
+    st = device_status(torch.device("cuda", torch.cuda.current_device()), clear=True)
+    if st != 0:
+        raise RuntimeError(f"{where}: a device-side wait timed out (vmscan status {st}); result discarded")
 
 
 class ClockSampler:
@@ -417,6 +434,7 @@ def main():
     e1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
+    check_status("timed fwd+VJP")
     barrier()
     total_ms = e0.elapsed_time(e1)
     fwd_ms = statistics.mean(ev[i][0].elapsed_time(ev[i][1]) for i in range(K))
@@ -451,9 +469,28 @@ def main():
 
     # ---- VisionMamba-2D training throughput (second half of the metric) ----
     model_line = None
+    model_scaling = None
     if not args.no_model:
-        model_line = run_model(dev, rank, world, steps=max(3, min(K, 10)), warmup=3, barrier=barrier,
+        msteps = max(3, min(K, 10))
+        model_line = run_model(dev, rank, world, steps=msteps, warmup=3, barrier=barrier,
                                graphed=not args.model_eager)
+        one = model_line
+        if world > 1:
+            # the 1-GPU point of the same curve, in the same job: rank 0 trains
+            # on the whole global batch alone while the other ranks wait
+            one = run_model(dev, 0, 1, steps=msteps, warmup=3, barrier=None, graphed=not args.model_eager,
+                            single=True) if rank == 0 else None
+            barrier()
+        if rank == 0:
+            model_scaling = {
+                "model": "VisionMamba-2D K=4 training (fwd, MSE, bwd, AdamW), global batch 64, strong scaling",
+                "n_gpus": world, "img_per_s": model_line["img_per_s"], "ms_per_step": model_line["ms_per_step"],
+                "per_gpu_batch": model_line["per_gpu_batch"],
+                "one_gpu_img_per_s": one["img_per_s"], "one_gpu_ms_per_step": one["ms_per_step"],
+                "speedup_vs_one_gpu": model_line["img_per_s"] / one["img_per_s"],
+                "efficiency_vs_one_gpu": model_line["img_per_s"] / one["img_per_s"] / world,
+                "one_gpu_source": "this run" if world == 1 else "this job, rank 0 alone on the whole batch",
+            }
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -501,17 +538,21 @@ def main():
             "dt_softplus": dtk,
             "cpu_baseline": base,
             "vision_mamba_2d_train": model_line,
+            "model_scaling": model_scaling,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
+def run_model(dev, rank, world, steps, warmup, barrier, graphed=True, single=False):
     """VisionMamba-2D (K=4, 224x224x1, patch 16, E 384, depth 6) training steps:
     forward, MSE, backward (DDP all-reduce over NCCL when world > 1), AdamW.
     Global batch 64 split over the ranks (strong scaling), fp32 (TF32 off).
-    `graphed`: the whole step is one CUDA graph replay (train.GraphedTrainStep)."""
+    `graphed`: the whole step is one CUDA graph replay (train.GraphedTrainStep).
+    `single`: this rank alone trains on the whole global batch (the 1-GPU
+    point of the strong-scaling curve, measured inside a multi-GPU job; no
+    DDP, no collective, no barrier)."""
     import torch
     import torch.distributed as dist
 
@@ -520,14 +561,17 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     cfg = train.VISION_MAMBA_2D
+    if single:
+        rank, world, barrier = 0, 1, (lambda: None)
     a, b = train.shard(cfg.global_batch, rank, world)
+    wrap = (lambda m: m) if single else (lambda m: train.wrap_data_parallel(m, dev))
     side = torch.cuda.Stream(dev)
     if graphed:
         with torch.cuda.stream(side):  # DDP is constructed on the capture's side stream
-            model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+            model = wrap(train.build_encoder(cfg, dev, seed=0))
         torch.cuda.current_stream(dev).wait_stream(side)
     else:
-        model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
+        model = wrap(train.build_encoder(cfg, dev, seed=0))
     opt = train.make_optimizer(model, capturable=graphed)
     x, tgt = train.synthetic_batch(cfg, b - a, dev, seed=100 + rank)
     if graphed:
@@ -548,7 +592,9 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True):
     torch.cuda.synchronize()
     loss = float(loss.item())
     if gstep is not None:
-        gstep.close()
+        gstep.close()  # checks the scan kernels' device status
+    else:
+        check_status("VisionMamba-2D eager steps")
     ms = e0.elapsed_time(e1)
     tm = torch.tensor([ms], device=dev)
     if world > 1:
@@ -1022,6 +1068,7 @@ def run_e2e(t, dev, K, warmup, world, barrier):
     comp.wait_stream(s_out)
     e1.record(comp)
     torch.cuda.synchronize()
+    check_status("e2e fwd+VJP")
     ms = e0.elapsed_time(e1)
     tm = torch.tensor([ms], device=dev)
     if world > 1:

@@ -232,9 +232,10 @@ int vmscan_bwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_st
  * a problem whose vmscan_bwd_workspace_bytes(..., recompute_ckpt = (ckpt ==
  * NULL)) exceeds it returns VMSCAN_ERR_SCRATCH without launching anything.
  * Inputs and outputs are the caller's, exactly as for vmscan_bwd.  The call
- * allocates and frees nothing.  The first call on a device looks up that
- * device's address of the array (once per device, cached); make that first
- * call before any stream capture.  All calls on a device share the one array
+ * allocates and frees nothing.  Every call looks up the array's address in
+ * the CUDA context current for the call (cudaGetSymbolAddress, as the other
+ * entry points do for the status word), so nothing is cached across contexts.
+ * All calls on a device share the one array
  * and it keeps the previous call's contents; nothing in it needs to start at
  * zero (every byte read is written earlier in the same call), but calls whose
  * kernels overlap on the GPU (different streams, or another thread) race on

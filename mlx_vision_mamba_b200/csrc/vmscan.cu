@@ -843,30 +843,24 @@ int vmscan_scan_order(int64_t seqlen, const vmscan_direction* dir, int mode, int
 const char* vmscan_last_error(void) { return g_last_error; }
 
 namespace {
-// Per-device address of g_vmscan_noalloc_scratch, looked up once per device
-// with that device current.
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {};
-
+// Address of g_vmscan_noalloc_scratch in the CUDA context that is current for
+// this call.  The address belongs to a context (not to a device index): a
+// thread may bind a non-primary context, and a context can be destroyed and
+// created again.  So it is looked up on every call, as status_ptr() does for
+// the status word, never cached.
 int noalloc_scratch_addr(const void* devbuf, void** out) {
   VM_TRY(ensure_context(devbuf));
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-    return fail(VMSCAN_ERR_LAUNCH, "cudaGetDevice failed");
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return fail(VMSCAN_ERR_LAUNCH, "cudaGetDevice failed");
   cudaPointerAttributes attr;
   if (cudaPointerGetAttributes(&attr, devbuf) != cudaSuccess || attr.device != dev)
     return fail(VMSCAN_ERR_LAUNCH, "the current device (%d) does not own the input buffers", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_vmscan_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return fail(VMSCAN_ERR_LAUNCH, "cudaGetSymbolAddress(scratch) on device %d failed: %s", dev,
-                  cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_vmscan_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return fail(VMSCAN_ERR_LAUNCH, "cudaGetSymbolAddress(scratch) on device %d failed: %s", dev,
+                cudaGetErrorString(e));
+  *out = p;
   return VMSCAN_OK;
 }
 }  // namespace

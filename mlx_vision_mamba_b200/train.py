@@ -134,6 +134,18 @@ def make_optimizer(model, lr: float = 1e-4, capturable: bool = False):
     return torch.optim.AdamW(params, lr=lr, weight_decay=0.05, capturable=capturable, fused=fused)
 
 
+def check_device_status(device=None) -> None:
+    """Raise if a kernel of libvmscan.so gave up a bounded device-side wait
+    since the last check (VMSCAN_ERR_TIMEOUT): its outputs are then wrong.
+    Synchronises the device's current stream; clears the status."""
+    from . import _native
+    from .scan import device_status
+
+    st = device_status(device, clear=True)
+    if st != 0:
+        raise _native.VmscanError(st, "device status after training steps")
+
+
 class GraphedTrainStep:
     """The whole training step (forward, MSE, backward with DDP's gradient
     all-reduce, AdamW update) captured once into a CUDA graph and replayed:
@@ -144,19 +156,31 @@ class GraphedTrainStep:
     be wrapped by `wrap_data_parallel` inside `side_stream` (DDP's documented
     requirement for capture) and the optimizer built with `capturable=True`.
     `warmup` eager steps run on the side stream first (DDP needs at least 11
-    before its buckets are final).  Release the step (`close()`) before
-    destroying a process group whose collectives it captured.
+    before its buckets are final); the parameters, buffers and optimizer state
+    are restored afterwards, so the first replay is the model's first update.
+    Every `status_every` replays (and in `close()`) the device status of the
+    scan kernels is checked, which raises on a timed-out device wait.
+    Release the step (`close()`) before destroying a process group whose
+    collectives it captured.
     """
 
-    def __init__(self, model, optimizer, x, target, side_stream=None, warmup: int = 11):
+    def __init__(self, model, optimizer, x, target, side_stream=None, warmup: int = 11, status_every: int = 100):
         self.model, self.optimizer = model, optimizer
+        self.device = x.device
+        self.status_every = int(status_every)
+        self.replays = 0
         self.x = x.detach().clone()
         self.target = target.detach().clone()
+        saved = _snapshot(model, optimizer)
         stream = side_stream if side_stream is not None else torch.cuda.Stream(device=x.device)
         stream.wait_stream(torch.cuda.current_stream(x.device))
         with torch.cuda.stream(stream):
             for _ in range(warmup):
                 train_step(model, optimizer, self.x, self.target)
+            # the warm-up steps only settle DDP's buckets and create the
+            # optimizer state; undo their updates in place (the graph
+            # captures these tensors' addresses)
+            _restore(model, optimizer, saved)
         torch.cuda.current_stream(x.device).wait_stream(stream)
         optimizer.zero_grad(set_to_none=True)
         self.graph = torch.cuda.CUDAGraph()
@@ -172,7 +196,44 @@ class GraphedTrainStep:
         if target is not None:
             self.target.copy_(target, non_blocking=True)
         self.graph.replay()
+        self.replays += 1
+        if self.status_every > 0 and self.replays % self.status_every == 0:
+            check_device_status(self.device)
         return self.loss
 
     def close(self) -> None:
+        if self.graph is not None:
+            check_device_status(self.device)
         self.graph = None
+
+
+def _snapshot(model, optimizer):
+    """Copies of the parameters, buffers and optimizer state (tensors cloned)."""
+    with torch.no_grad():
+        params = [p.detach().clone() for p in model.parameters()]
+        bufs = [b.detach().clone() for b in model.buffers()]
+        state = {p: {k: (v.detach().clone() if torch.is_tensor(v) else v) for k, v in st.items()}
+                 for p, st in optimizer.state.items()}
+    return params, bufs, state
+
+
+def _restore(model, optimizer, saved) -> None:
+    """Puts back what `_snapshot` saved, in place.  Optimizer state created
+    after the snapshot (a fresh optimizer's first steps) is reset to zero,
+    the value a fresh AdamW starts from."""
+    params, bufs, state = saved
+    with torch.no_grad():
+        for p, v in zip(model.parameters(), params):
+            p.copy_(v)
+        for b, v in zip(model.buffers(), bufs):
+            b.copy_(v)
+        for p, st in optimizer.state.items():
+            old = state.get(p, {})
+            for k, v in st.items():
+                if torch.is_tensor(v):
+                    if k in old:
+                        v.copy_(old[k])
+                    else:
+                        v.zero_()
+                elif k in old:
+                    st[k] = old[k]

@@ -9,6 +9,23 @@ if ROOT not in sys.path:
 
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
+
+def _keep_freed_heap_memory():
+    """Let glibc keep freed large blocks in the heap instead of returning them
+    to the OS: the CPU oracle allocates many large temporaries in a row, and
+    faulting fresh pages in for each one dominated its run time."""
+    try:
+        import ctypes
+
+        libc = ctypes.CDLL("libc.so.6")
+        libc.mallopt(-3, 32 << 20)  # M_MMAP_THRESHOLD: the largest value glibc accepts on 64-bit
+        libc.mallopt(-1, 1 << 30)   # M_TRIM_THRESHOLD
+    except OSError:
+        pass
+
+
+_keep_freed_heap_memory()
+
 # Parity tolerance of the north star: fp32 outputs and gradients within
 # 1e-5 relative / 1e-6 absolute of the reference.
 RTOL = 1e-5
@@ -28,3 +45,18 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """Write the per-tensor parity figures gathered by tests/parity.py to the
+    JSON file named by VMSCAN_PARITY_TABLE (unset: nothing is written)."""
+    path = os.environ.get("VMSCAN_PARITY_TABLE")
+    if not path:
+        return
+    import json
+
+    from parity import RECORDS
+
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    with open(path, "w") as f:
+        json.dump(RECORDS, f, indent=0)

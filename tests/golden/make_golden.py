@@ -13,8 +13,9 @@ autograd through the reference code.  Each case is saved as a small .pt file
 of inputs, parameters (by MLX name), outputs and gradients, in fp32.
 
 The fixtures pin the CPU oracle (tests/test_oracle_golden.py) and the CUDA
-path (tests/test_golden_gpu.py) to the reference's behaviour, including its
-direction permutations and operation order.
+path (the fixture cases of tests/test_scan_gpu.py and tests/test_block_gpu.py)
+to the reference's behaviour, including its direction permutations and
+operation order.
 """
 
 from __future__ import annotations

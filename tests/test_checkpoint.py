@@ -47,3 +47,31 @@ def test_resume_continues_the_run(tmp_path):
     assert train.load_checkpoint(path, m2, opt2, map_location=dev) == 2
     resumed = [train.train_step(m2, opt2, x, tgt).item() for _ in range(2)]
     assert resumed == losses
+
+
+def test_warmup_snapshot_restores_model_and_optimizer_cpu():
+    """GraphedTrainStep's warm-up undo (train._snapshot / _restore) on CPU: after
+    steps that create the optimizer state, the parameters are back to their
+    values and the fresh state reads as a new AdamW's (zero moments and step),
+    so the next update equals a fresh optimizer's first update."""
+    lin = torch.nn.Linear(8, 4)
+    opt = torch.optim.AdamW(lin.parameters(), lr=1e-2)
+    ref = torch.nn.Linear(8, 4)
+    ref.load_state_dict(lin.state_dict())
+    ref_opt = torch.optim.AdamW(ref.parameters(), lr=1e-2)
+    x = torch.randn(5, 8)
+    saved = train._snapshot(lin, opt)
+    for _ in range(3):
+        opt.zero_grad()
+        lin(x).square().sum().backward()
+        opt.step()
+    assert not torch.equal(lin.weight, ref.weight)
+    train._restore(lin, opt, saved)
+    assert torch.equal(lin.weight, ref.weight) and torch.equal(lin.bias, ref.bias)
+    for st in opt.state.values():
+        assert all(float(v.abs().sum()) == 0.0 for v in st.values() if torch.is_tensor(v))
+    for m, o in ((lin, opt), (ref, ref_opt)):
+        o.zero_grad()
+        m(x).square().sum().backward()
+        o.step()
+    assert torch.equal(lin.weight, ref.weight) and torch.equal(lin.bias, ref.bias)

@@ -80,3 +80,18 @@ def test_chunked_oracle_equals_sequential_in_fp32():
     a = scan_ref.selective_scan(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"])
     c = scan_ref.selective_scan_chunked(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"])
     torch.testing.assert_close(c, a, rtol=1e-6, atol=1e-6)
+
+
+def test_oracle_in_pieces_equals_one_call():
+    """tests/parity.oracle_vjp split over channels or batch rows gives the
+    one-call oracle's result (fp64; pieces summed for dB / dC or dA / dD)."""
+    from parity import oracle_vjp
+
+    inp = scan_ref.sweep_inputs(3, 20, 40, seed=7)
+    y, g = scan_ref.scan_vjp(inp, gated=True, dtype=torch.float64)
+    for split, piece in (("channels", 16), ("batch", 2)):
+        ys, gs = oracle_vjp(inp, torch.float64, split=split, piece=piece)
+        torch.testing.assert_close(ys, y, rtol=1e-13, atol=1e-13)
+        assert gs.keys() == g.keys()
+        for k in g:
+            torch.testing.assert_close(gs[k], g[k], rtol=1e-12, atol=1e-12, msg=f"{split} {k}")

@@ -5,6 +5,9 @@ properties that hold at any size:
 * per-channel parity: the recurrence never crosses channels, so the fp64
   oracle run on 8 channels (tile edges included) over all 64 rows and all
   4096 steps gives the exact y, du, ddelta, dz, dA and dD of those channels;
+* whole rows: batch rows 0 and 63 over all 1536 channels and all 4096
+  steps against the fp64 oracle, including dB and dC, which sum over every
+  channel of a (row, step);
 * linearity in the cotangent: the VJP is linear in dy, so doubling dy
   doubles every gradient bit for bit;
 * additivity over channels: dB and dC are sums over channels, so the VJP
@@ -16,7 +19,7 @@ import torch
 
 from mlx_vision_mamba_b200 import selective_scan_cuda
 from oracle import scan_ref
-from parity import assert_parity
+from parity import assert_parity, oracle_vjp
 
 pytestmark = pytest.mark.gpu
 
@@ -61,9 +64,8 @@ def test_full_size_properties():
     idx = torch.tensor(CHANNELS, device="cuda")
     sub = {k: t[k].index_select(-1, idx).cpu() for k in ("u", "z", "delta", "dy")}
     sub.update(A=t["A"][idx].cpu(), D=t["D"][idx].cpu(), B=t["B"].cpu(), C=t["C"].cpu())
-    y64, g64 = scan_ref.scan_vjp(sub, gated=True, dtype=torch.float64)
+    y64, g64 = oracle_vjp(sub, torch.float64, split="batch", piece=8)
     y32, g32 = scan_ref.scan_vjp(sub, gated=True, dtype=torch.float32)
-    ic = idx.cpu()
     assert_parity("full-size y", y.index_select(-1, idx).cpu(), y64, y32)
     for k in ("du", "ddelta", "dz"):
         assert_parity(f"full-size {k}", g[k].index_select(-1, idx).cpu(), g64[k], g32[k])
@@ -74,6 +76,17 @@ def test_full_size_properties():
     assert_parity("full-size dA", g["dA"][idx].cpu(), g64["dA"])
     assert_parity("full-size dD", g["dD"][idx].cpu(), g64["dD"])
     del sub, y64, g64, y32, g32
+
+    # two whole batch rows: every channel, every step, dB / dC included
+    for row in (0, B - 1):
+        sub = {k: t[k][row:row + 1].cpu() for k in ("u", "z", "delta", "dy", "B", "C")}
+        sub.update(A=t["A"].cpu(), D=t["D"].cpu())
+        y64, g64 = oracle_vjp(sub, torch.float64, split="channels", piece=256)
+        y32, g32 = scan_ref.scan_vjp(sub, gated=True, dtype=torch.float32)
+        assert_parity(f"full-size row {row} y", y[row:row + 1].cpu(), y64, y32)
+        for k in ("du", "ddelta", "dz", "dB", "dC"):
+            assert_parity(f"full-size row {row} {k}", g[k][row:row + 1].cpu(), g64[k], g32[k])
+        del sub, y64, g64, y32, g32
 
     # linearity in dy: exact for a power-of-two scale
     _, g2 = vjp(t, 2.0 * t["dy"])
