@@ -126,12 +126,36 @@ __device__ __forceinline__ float dbc_reduce_scatter(const float2 vb[4], const fl
 }
 
 // Per-thread state of the VJP that lives across boxes.
+//
+// dA and dD sum batch x L terms per element, which in a plain running sum
+// would cost accuracy at elements whose exact value cancels to near zero.
+// dD is summed with Kahan compensation every step (dDcomp).  dA is summed in
+// short partials (two reverse steps) that are folded into the running total
+// by Fast2Sum; the rounding error of each fold starts the next partial
+// (dAerr carries it across boxes), so only the products' own roundings
+// remain.
 struct BwdLane {
   float2 Ar[2][4];     // A of the lane's 8 states (slot order), per channel
   float2 P[2][4];      // dA_{t+1} * dh_{t+1} carried backwards
   float2 dAacc[2][4];  // running dA partials
+  float2 dAerr[2][4];  // rounding error of the last fold into dAacc
   float dDacc;         // running dD partial of the own channel
+  float dDcomp;        // its Kahan compensation
 };
+
+// Folds the short dA partial into the running total (Fast2Sum); the partial
+// is left holding the fold's rounding error.
+__device__ __forceinline__ void fold_dA(BwdLane& L, float2 (&part)[2][4]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 s = add2(L.dAacc[c][j], part[c][j]);
+      const float2 t = add2(s, make_float2(-L.dAacc[c][j].x, -L.dAacc[c][j].y));
+      part[c][j] = add2(part[c][j], make_float2(-t.x, -t.y));
+      L.dAacc[c][j] = s;
+    }
+}
 
 // What a reverse step hands to its epilogue.  The epilogue (cross-lane sums,
 // stores) of step s runs after the state math of step s - 1, so its shuffle
@@ -145,7 +169,7 @@ struct RevCarry {
 
 // State math of one reverse step (row r) with the history h_{s-1} in hp.
 template <typename T, bool HAS_Z>
-__device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], float2 (&dAbox)[2][4], float& dDbox,
+__device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], float2 (&dAbox)[2][4],
                                              const uint32_t (&hp)[16], const BwdStage<T>& S, int r, int c0l,
                                              const PairLane& pl, RevCarry& k) {
   constexpr int DT = BwdCfg<T>::DT;
@@ -189,7 +213,11 @@ __device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], flo
   k.uo = pl.hb ? u2.y : u2.x;
   k.to = pl.hb ? t2.y : t2.x;
   k.r = r;
-  dDbox = fmaf(k.dyo, k.uo, dDbox);
+  // dD += dy' u, Kahan-compensated
+  const float yk = fmaf(k.dyo, k.uo, -L.dDcomp);
+  const float tk = L.dDacc + yk;
+  L.dDcomp = (tk - L.dDacc) - yk;
+  L.dDacc = tk;
 }
 
 // Epilogue of a reverse step: du / ddelta of the own channel, dB / dC row partial.
@@ -300,14 +328,13 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
   __syncwarp();
 
   // ---- reverse adjoint over the box ----
-  // dA / dD are summed per box first and folded into the running totals
-  // once per box: L/16 + 16 additions per total instead of L in a row.
+  // dA partials of two steps at a time, folded into the running totals
+  // (fold_dA); the first starts at the error left by the previous box's last fold
   float2 dAbox[2][4];
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) dAbox[c][j] = make_float2(0.f, 0.f);
-  float dDbox = 0.f;
+    for (int j = 0; j < 4; ++j) dAbox[c][j] = L.dAerr[c][j];
   float2 hs[2][4];
 #pragma unroll
   for (int c = 0; c < 2; ++c)
@@ -324,31 +351,32 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
   tmem_ld16(taddr + 16 * s, XA);
   tmem_wait_ld16(XA);
   if (s > 0) tmem_ld16(taddr + 16 * (s - 1), XB);
-  bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XA, S, row(s), c0l, pl, ka);
+  bwd_rev_math<T, HAS_Z>(L, hs, dAbox, XA, S, row(s), c0l, pl, ka);
   if (s > 0) tmem_wait_ld16(XB);
 #pragma unroll 1
   for (--s; s >= 1; s -= 2) {
     tmem_ld16(taddr + 16 * (s - 1), XA);
-    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XB, S, row(s), c0l, pl, kb);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, XB, S, row(s), c0l, pl, kb);
     bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
     tmem_wait_ld16(XA);
     tmem_ld16(taddr + 16 * max(s - 2, 0), XB);
-    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XA, S, row(s - 1), c0l, pl, ka);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, XA, S, row(s - 1), c0l, pl, ka);
     bwd_rev_epilogue(kb, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
+    fold_dA(L, dAbox);
     tmem_wait_ld16(XB);
   }
   if (s == 0) {
-    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, dDbox, XB, S, row(0), c0l, pl, kb);
+    bwd_rev_math<T, HAS_Z>(L, hs, dAbox, XB, S, row(0), c0l, pl, kb);
     bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
     bwd_rev_epilogue(kb, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
   } else {
     bwd_rev_epilogue(ka, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
   }
+  fold_dA(L, dAbox);
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) L.dAacc[c][j] = add2(L.dAacc[c][j], dAbox[c][j]);
-  L.dDacc += dDbox;
+    for (int j = 0; j < 4; ++j) L.dAerr[c][j] = dAbox[c][j];
 }
 
 // Chunked VJP over L.  Chunk c holds forward boxes [c * bpc, min((c + 1) *
@@ -474,7 +502,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
       L.Ar[c][2 * gi + 1] = make_float2(a4.z, a4.w);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) L.P[c][j] = L.dAacc[c][j] = make_float2(0.f, 0.f);
+    for (int j = 0; j < 4; ++j) L.P[c][j] = L.dAacc[c][j] = L.dAerr[c][j] = make_float2(0.f, 0.f);
     // a chunk other than the last starts from the adjoint carry of the chunks after it
     if (cidx + 1 < chunk.nchunks && vc) {
       const float* src = chunk.p_in + ((size_t(b) * chunk.nchunks + cidx) * g.d_inner + dc + c) * NS;
@@ -487,6 +515,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     }
   }
   L.dDacc = 0.f;
+  L.dDcomp = 0.f;
   const int own = dc + pl.hb;
   const float Down = ev ? Dskip[own] : 0.f;
   T* du_b = du_out + b * sdub + own;
@@ -533,6 +562,11 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     }
   }
 
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) L.dAacc[c][j] = add2(L.dAacc[c][j], L.dAerr[c][j]);
+  L.dDacc -= L.dDcomp;
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     if (c ? v1 : v0) {
@@ -751,20 +785,30 @@ __global__ void reduce_dbc_kernel(const float* __restrict__ wpart, T* __restrict
     dC[b * sCb + tok * sCs + (slot - NS)] = acc;
 }
 
-// dA (d_inner x 16) and dD (d_inner): sum the per-batch-row partials in order.
+// dA (d_inner x 16) and dD (d_inner): sum the per-(batch row, chunk)
+// partials in order, compensated (each addition's exact rounding error from
+// TwoSum is accumulated and added once at the end).
 __global__ void reduce_dad_kernel(const float* __restrict__ wA, const float* __restrict__ wD,
                                   float* __restrict__ dA, float* __restrict__ dD, int batch, int d_inner) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const size_t nA = size_t(d_inner) * NS;
   if (idx < nA) {
-    float acc = 0.f;
-    for (int b = 0; b < batch; ++b) acc += wA[size_t(b) * nA + idx];
-    dA[idx] = acc;
+    float acc = 0.f, comp = 0.f;
+    for (int b = 0; b < batch; ++b) {
+      float x = wA[size_t(b) * nA + idx];
+      two_sum1(acc, x);
+      comp += x;
+    }
+    dA[idx] = acc + comp;
   }
   if (idx < d_inner) {
-    float acc = 0.f;
-    for (int b = 0; b < batch; ++b) acc += wD[size_t(b) * d_inner + idx];
-    dD[idx] = acc;
+    float acc = 0.f, comp = 0.f;
+    for (int b = 0; b < batch; ++b) {
+      float x = wD[size_t(b) * d_inner + idx];
+      two_sum1(acc, x);
+      comp += x;
+    }
+    dD[idx] = acc + comp;
   }
 }
 

@@ -311,6 +311,16 @@ struct PairLane {
 
 __device__ __forceinline__ float2 sel2(bool p, float2 a, float2 b) { return p ? a : b; }
 
+// TwoSum (Knuth): acc <- fl(acc + x) and x <- the exact rounding error of
+// that addition, for any magnitudes (6 additions, no branch).
+__device__ __forceinline__ void two_sum1(float& acc, float& x) {
+  const float s = acc + x;
+  const float bb = s - acc;
+  const float err = (acc - (s - bb)) + (x - bb);
+  acc = s;
+  x = err;
+}
+
 __device__ __forceinline__ float2 shfl_xor2(float2 v, int m) {
   return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
