@@ -325,6 +325,26 @@ def workload_name():
             f"d_inner {w['d_inner']} d_state {N_STATE} (per GPU)")
 
 
+def launch_only(reps, bf16):
+    """REPS forward + VJP pairs through the C ABI on the sweep's seeded inputs,
+    untimed: the launches a small `ncu` capture selects from.  Returns the
+    process exit code (1 if a bounded device wait gave up)."""
+    import torch
+
+    dev = torch.device("cuda", 0)
+    b, l, d = WORKLOAD["batch"], WORKLOAD["seqlen"], WORKLOAD["d_inner"]
+    runner = AbiScan(make_inputs(b, l, d, dev, seed=3), bf16=bf16)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    for _ in range(reps):
+        runner.fwd(stream)
+        runner.bwd(stream)
+    torch.cuda.synchronize()
+    st = runner.lib.vmscan_device_status(stream, 1)
+    print(json.dumps({"launch_only": {"batch": b, "seqlen": l, "d_inner": d, "io": "bf16" if bf16 else "f32",
+                                      "reps": reps, "device_status": st}}), flush=True)
+    return 1 if st else 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,11 +373,20 @@ def main():
                     help="only time the dt_proj + softplus kernels (forward, VJP) at the model's block shape")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
+    ap.add_argument("--gemm", action="store_true",
+                    help="only time the tensor-core projection GEMMs at the VisionMamba-2D shapes against "
+                         "PyTorch's fp32 GEMM")
+    ap.add_argument("--launch-only", type=int, metavar="REPS",
+                    help="run REPS forward + VJP pairs through the C ABI at --batch/--seqlen/--dinner (--io "
+                         "picks fp32 or bf16 I/O), untimed, and exit nonzero if the device status is set "
+                         "(small ncu captures)")
     args = ap.parse_args()
     WORKLOAD.update(batch=args.batch, seqlen=args.seqlen, d_inner=args.dinner)
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.launch_only:
+        sys.exit(launch_only(args.launch_only, args.io == "bf16"))
     if args.model_profile:
         profile_model(args.warmup)
         return
@@ -373,6 +402,11 @@ def main():
         import torch
 
         print(json.dumps({"dt_softplus": time_dt(torch.device("cuda", 0))}), flush=True)
+        return
+    if args.gemm:
+        import torch
+
+        print(json.dumps({"projection_gemm": time_gemm(torch.device("cuda", 0))}), flush=True)
         return
 
     import torch
@@ -796,6 +830,66 @@ def time_dt(dev, iters=20):
     del xw, w, bias, gin, out, flush
     torch.cuda.empty_cache()
     return res
+
+
+def time_gemm(dev, iters=20):
+    """The block's projection GEMMs at the VisionMamba-2D shapes (64 x 196
+    tokens, E 384, K=4 directions: in_proj 384 -> 6144, out_proj 3072 -> 384;
+    forward, input gradient, weight gradient) on the tensor cores
+    (vmscan_gemm_tf32x3 from split operands; the split passes timed
+    separately) against PyTorch's fp32 GEMM with TF32 off.  Median of `iters`
+    after 3 warm-ups.  TFLOP/s counts the fp32 GEMM's 2 M N K."""
+    import torch
+
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    old_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device=dev).manual_seed(21)
+    st = torch.cuda.current_stream(dev)
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        bf16_peak = json.load(f).get("bf16_tflops")
+
+    def med(fn):
+        ts = []
+        for it in range(iters + 3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            if it >= 3:
+                ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    t = 64 * 196
+    rows = []
+    for name, fin, fout in (("in_proj", 384, 6144), ("out_proj", 3072, 384)):
+        x = torch.randn(t, fin, device=dev, generator=g)
+        w = torch.randn(fout, fin, device=dev, generator=g) / fin ** 0.5
+        dy = torch.randn(t, fout, device=dev, generator=g)
+        xs, ws, ds = tf32_split(x), tf32_split(w), tf32_split(dy)
+        cases = (
+            ("fwd", t, fout, fin, lambda: gemm_tf32x3(xs, False, ws, False, t, fout, fin), lambda: x @ w.t(),
+             lambda: tf32_split(x)),
+            ("dx", t, fin, fout, lambda: gemm_tf32x3(ds, False, ws, True, t, fin, fout), lambda: dy @ w,
+             lambda: tf32_split(dy)),
+            ("dw", fout, fin, t, lambda: gemm_tf32x3(ds, True, xs, True, fout, fin, t), lambda: dy.t() @ x, None),
+        )
+        for kind, m, n, k, ours, theirs, split in cases:
+            ms_ours, ms_torch = med(ours), med(theirs)
+            flops = 2.0 * m * n * k
+            row = {"gemm": f"{name} {kind}", "m": m, "n": n, "k": k, "ms": ms_ours, "tflops": flops / ms_ours / 1e9,
+                   "torch_fp32_ms": ms_torch, "torch_fp32_tflops": flops / ms_torch / 1e9,
+                   "speedup": ms_torch / ms_ours}
+            if split is not None:
+                row["split_ms"] = med(split)
+            rows.append(row)
+        del x, w, dy, xs, ws, ds
+    torch.cuda.empty_cache()
+    torch.backends.cuda.matmul.allow_tf32 = old_tf32
+    return {"api": "vmscan_gemm_tf32x3 (+ vmscan_tf32_split)", "tensor_peak_note":
+            f"3 tf32 MMAs per output; measured bf16 peak {bf16_peak} TFLOP/s (tf32 is half)", "shapes": rows}
 
 
 SWEEP = [(b, l, d) for b in (8, 64) for l in (196, 1024, 4096) for d in (768, 1536)]

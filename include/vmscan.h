@@ -325,6 +325,34 @@ int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
 int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
 
 /*
+ * Projection GEMMs of the block on the tensor cores with fp32 accuracy
+ * (in_proj and out_proj, mamba_block.py:165,191, the out_proj over the
+ * concatenated directions performing the sum of :562-566, and their input
+ * and weight gradients).
+ *
+ * vmscan_tf32_split writes hi = tf32(x) and lo = tf32(x - hi) (round to
+ * nearest) for n floats (n % 4 == 0, 16-byte aligned buffers); x = hi + lo to
+ * about 2^-22 |x|.
+ *
+ * vmscan_gemm_tf32x3 computes C[m, n] = sum_k A(m, k) B(n, k) for row-major C
+ * (row stride ldc) from the split operands:
+ *   A(m, k) = a[m * lda + k] (a_mn_major == 0) or a[k * lda + m] (!= 0),
+ *   B(n, k) = b[n * ldb + k] (b_mn_major == 0) or b[k * ldb + n] (!= 0),
+ * as A_hi B_hi + (A_hi B_lo + A_lo B_hi) with the large and the correction
+ * products in separate fp32 accumulators.  lda, ldb: multiples of 4, all
+ * operand pointers 16-byte aligned.  When the output tiles would not fill the
+ * GPU, K is split and the partials are summed in a fixed order; that needs
+ * vmscan_gemm_workspace_bytes(M, N, K) bytes of workspace (0: none).
+ */
+int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_stream_t stream);
+int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
+                       const float* a_hi, const float* a_lo, int64_t lda, int a_mn_major,
+                       const float* b_hi, const float* b_lo, int64_t ldb, int b_mn_major,
+                       float* c, int64_t ldc, void* workspace, int64_t workspace_bytes,
+                       vmscan_stream_t stream);
+
+/*
  * Host-only introspection (no CUDA call): writes the token index visited at
  * every scan step of `dir` into tokens[0..seqlen), computed the way the
  * kernels compute it.  mode 0 enumerates the TMA boxes (box coordinates +

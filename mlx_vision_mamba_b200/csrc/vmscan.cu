@@ -19,6 +19,7 @@
 #include "vmscan_conv.cuh"
 #include "vmscan_dt.cuh"
 #include "vmscan_fwd.cuh"
+#include "vmscan_gemm.cuh"
 
 using namespace vmscan;
 
@@ -603,6 +604,74 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
 
 }  // namespace
 
+namespace {
+
+constexpr int kGemmBN = 128;
+
+// 2-D tensor map of a row-major (rows x cols) fp32 matrix with row stride ld
+// (elements): box {32, box_rows}, zero fill outside, 128-byte swizzle of
+// 16-byte chunks (K-major operand tiles) or of 32-byte chunks (mn: MN-major).
+int encode_gemm_map(CUtensorMap* m, const char* what, const float* p, int64_t cols, int64_t rows, int64_t ld,
+                    int box_rows, bool mn) {
+  if (p == nullptr) return fail(VMSCAN_ERR_NULL, "gemm: %s is NULL", what);
+  if (!aligned16(p) || ld % 4 != 0 || ld < cols)
+    return fail(VMSCAN_ERR_ALIGN, "gemm: %s (base %p, row stride %lld for %lld columns) must be 16-byte aligned "
+                "with a row stride that is a multiple of 4 elements", what, p, (long long)ld, (long long)cols);
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(VMSCAN_ERR_DRIVER, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
+  cuuint32_t box[2] = {32u, cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(VMSCAN_ERR_DRIVER, "cuTensorMapEncodeTiled(gemm %s) -> CUresult %d; dims {%lld, %lld} ld %lld",
+                what, int(r), (long long)cols, (long long)rows, (long long)ld);
+  return VMSCAN_OK;
+}
+
+// K splits of a GEMM: 1 while the output tiles fill the SMs, otherwise enough
+// splits to fill them with at least 8 k-blocks each (at most 8 splits).
+struct GemmPlan {
+  int tiles_n, tiles_m, splits, kb_per_split;
+  size_t ws_bytes;
+};
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
+  GemmPlan p;
+  p.tiles_n = int((N + kGemmBN - 1) / kGemmBN);
+  p.tiles_m = int((M + GM_BM - 1) / GM_BM);
+  const int nkb = int((K + GM_BK - 1) / GM_BK);
+  const int64_t tiles = int64_t(p.tiles_n) * p.tiles_m;
+  const int sms = sm_count();
+  int s = 1;
+  if (tiles < sms) s = int(std::min<int64_t>({int64_t(sms) / tiles, int64_t(nkb / 8), 8}));
+  s = std::max(s, 1);
+  p.kb_per_split = (nkb + s - 1) / s;
+  p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
+  p.ws_bytes = p.splits > 1 ? align256(size_t(p.splits) * size_t(M) * size_t(N) * 4) : 0;
+  return p;
+}
+
+template <bool A_MN, bool B_MN>
+int launch_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                const GemmPlan& p, const GemmArgs& a, cudaStream_t s) {
+  using Cfg = GemmCfg<kGemmBN>;
+  auto kern = gemm_tf32x3_kernel<kGemmBN, A_MN, B_MN>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
+    return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(gemm_tf32x3_kernel) failed");
+  int* st = status_ptr();
+  if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
+  kern<<<dim3(unsigned(p.tiles_n), unsigned(p.tiles_m), unsigned(p.splits)), GM_THREADS, Cfg::SMEM_BYTES, s>>>(
+      ahi, alo, bhi, blo, a, st);
+  return check_launch();
+}
+
+}  // namespace
+
 // The failure path of every bounded wait, exercised on purpose: one warp
 // waits on an mbarrier that nothing arrives on, gives up after `tries`
 // polls, records VMSCAN_ERR_TIMEOUT in the sticky status and returns; no
@@ -883,6 +952,74 @@ int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d
   return vmscan_bwd(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy, sdy,
                     du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, scratch,
                     size_t(VMSCAN_NOALLOC_SCRATCH_BYTES), stream);
+}
+
+int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_stream_t stream) {
+  if (n == 0) return VMSCAN_OK;
+  if (x == nullptr || hi == nullptr || lo == nullptr) return VMSCAN_ERR_NULL;
+  if (n < 0 || n % 4 != 0) return fail(VMSCAN_ERR_SHAPE, "tf32_split: n = %lld must be a multiple of 4", (long long)n);
+  if (!aligned16(x) || !aligned16(hi) || !aligned16(lo))
+    return fail(VMSCAN_ERR_ALIGN, "tf32_split: buffers must be 16-byte aligned");
+  VM_TRY(ensure_context(x));
+  const int64_t n4 = n / 4;
+  const unsigned blocks = unsigned(std::min<int64_t>((n4 + 255) / 256, int64_t(sm_count()) * 8));
+  tf32_split_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo), n4);
+  return check_launch();
+}
+
+int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return -VMSCAN_ERR_SHAPE;
+  return int64_t(gemm_plan(M, N, K).ws_bytes);
+}
+
+int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const float* a_lo, int64_t lda,
+                       int a_mn_major, const float* b_hi, const float* b_lo, int64_t ldb, int b_mn_major, float* c,
+                       int64_t ldc, void* workspace, int64_t workspace_bytes, vmscan_stream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld, N %lld, K %lld", (long long)M, (long long)N, (long long)K);
+  if (c == nullptr) return VMSCAN_ERR_NULL;
+  if (ldc < N) return fail(VMSCAN_ERR_SHAPE, "gemm: ldc %lld < N %lld", (long long)ldc, (long long)N);
+  if (int64_t((M + GM_BM - 1) / GM_BM) > 65535)
+    return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld exceeds the launch grid", (long long)M);
+  VM_TRY(ensure_context(c));
+  CUtensorMap ahi, alo, bhi, blo;
+  // A(m, k): K-major a[m * lda + k] (rows M), MN-major a[k * lda + m] (rows K)
+  const int64_t acols = a_mn_major ? M : K, arows = a_mn_major ? K : M;
+  const int64_t bcols = b_mn_major ? N : K, brows = b_mn_major ? K : N;
+  const int abox = a_mn_major ? 32 : GM_BM, bbox = b_mn_major ? 32 : kGemmBN;
+  VM_TRY(encode_gemm_map(&ahi, "a_hi", a_hi, acols, arows, lda, abox, a_mn_major != 0));
+  VM_TRY(encode_gemm_map(&alo, "a_lo", a_lo, acols, arows, lda, abox, a_mn_major != 0));
+  VM_TRY(encode_gemm_map(&bhi, "b_hi", b_hi, bcols, brows, ldb, bbox, b_mn_major != 0));
+  VM_TRY(encode_gemm_map(&blo, "b_lo", b_lo, bcols, brows, ldb, bbox, b_mn_major != 0));
+  const GemmPlan p = gemm_plan(M, N, K);
+  if (p.splits > 1 && (workspace == nullptr || workspace_bytes < int64_t(p.ws_bytes)))
+    return fail(VMSCAN_ERR_WORKSPACE, "gemm: %d K splits need %zu bytes of workspace", p.splits, p.ws_bytes);
+  if (p.splits > 1 && !aligned16(workspace)) return fail(VMSCAN_ERR_ALIGN, "gemm: workspace not 16-byte aligned");
+  GemmArgs a;
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.kb_per_split = p.kb_per_split;
+  a.C = p.splits > 1 ? static_cast<float*>(workspace) : c;
+  a.ldc = p.splits > 1 ? N : ldc;
+  a.split_stride = M * N;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc;
+  if (a_mn_major && b_mn_major)
+    rc = launch_gemm<true, true>(ahi, alo, bhi, blo, p, a, s);
+  else if (a_mn_major)
+    rc = launch_gemm<true, false>(ahi, alo, bhi, blo, p, a, s);
+  else if (b_mn_major)
+    rc = launch_gemm<false, true>(ahi, alo, bhi, blo, p, a, s);
+  else
+    rc = launch_gemm<false, false>(ahi, alo, bhi, blo, p, a, s);
+  if (rc != VMSCAN_OK || p.splits == 1) return rc;
+  const int64_t total = M * N;
+  const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 8));
+  gemm_splitk_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), c, ldc, int(M), int(N),
+                                                   p.splits, M * N);
+  return check_launch();
 }
 
 int vmscan_wait_timeout_selftest(uint32_t tries, vmscan_stream_t stream) {

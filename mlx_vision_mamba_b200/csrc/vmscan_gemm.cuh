@@ -1,0 +1,363 @@
+// vmscan_gemm.cuh — fp32-accurate projection GEMMs on the sm_100a tensor
+// cores (tcgen05, kind::tf32) for the Mamba block's in_proj / out_proj
+// (mlx_vision_mamba/mamba_block.py:165,191 and the direction sum :562-566).
+//
+// Precision.  TF32 keeps 11 significant bits.  Each fp32 operand x is split
+// into hi = rna_tf32(x) and lo = rna_tf32(x - hi) (x - hi is exact), so x =
+// hi + lo to about 2^-22 |x|, and
+//     C = A_hi B_hi + (A_hi B_lo + A_lo B_hi)
+// drops only A_lo B_lo (~2^-22 of a product).  The large products and the
+// two correction products accumulate in separate TMEM accumulators, summed
+// once in fp32 by the epilogue, so the rounding of the running sum acts on
+// the large products alone, as it does in an fp32 FFMA loop.  The split is a
+// separate elementwise pass (tf32_split_kernel) whose outputs the GEMM reads.
+//
+// Design.  One CTA per 128 x BN tile of C (or per tile and K split), 256
+// threads: warp 0 lane 0 issues the TMA loads of the hi / lo tiles of A and
+// B into an NST-stage ring of mbarriers; warp 1 owns the TMEM allocation and
+// its lane 0 issues the tcgen05.mma instructions (3 per K=8 step) and the
+// tcgen05.commit that releases each stage; warps 4..7 (one per TMEM lane
+// quarter) read the two accumulators back with tcgen05.ld, add them and
+// store the tile.  Operand tiles use a 128-byte swizzle; an operand is
+// either K-major (rows of K contiguous, one TMA box of 32 x rows, 16-byte
+// chunks swizzled) or MN-major (rows of M or N contiguous: 32-element column
+// blocks of 32 K rows each, 4 KB apart, 32-byte chunks swizzled).  Every wait is bounded: on time-out the kernel
+// records VMSCAN_ERR_TIMEOUT in the device status and drains.
+#pragma once
+
+#include "vmscan_common.cuh"
+
+namespace vmscan {
+
+constexpr int GM_BM = 128;
+constexpr int GM_BK = 32;  // fp32 elements per k-block: one 128-byte swizzle row
+constexpr int GM_THREADS = 256;
+constexpr int GM_EPI_WARP0 = 4;  // warps 4..7 read TMEM lane quarters 0..3
+
+template <int BN>
+struct GemmCfg {
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN: multiple of 32 up to 256");
+  static constexpr int A_TILE_B = GM_BM * GM_BK * 4;  // 16 KB
+  static constexpr int B_TILE_B = BN * GM_BK * 4;
+  static constexpr int OFF_ALO = A_TILE_B, OFF_BHI = 2 * A_TILE_B, OFF_BLO = 2 * A_TILE_B + B_TILE_B;
+  static constexpr int STAGE_B = 2 * A_TILE_B + 2 * B_TILE_B;
+  static constexpr int NST = (196 * 1024) / STAGE_B;
+  static_assert(NST >= 2, "at least two stages");
+  // accumulators: two large-product buffers (columns 0, BN), correction products (2 BN)
+  static_assert(3 * BN <= 512, "three accumulators of BN columns");
+  static constexpr uint32_t TMEM_COLS = 3 * BN <= 256 ? 256u : 512u;
+  static constexpr int OFF_BAR = NST * STAGE_B;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 4) * 8 + 16 + 1024;
+};
+
+// ---- tcgen05 helpers ----
+
+// Shared-memory matrix descriptor (sm_100 format, version 1).  lbo / sbo in
+// bytes; layout 2 = 128-byte swizzle of 16-byte chunks (K-major tiles), 1 =
+// 128-byte swizzle of 32-byte chunks (the layout 32-bit MN-major tiles need).
+__device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  uint64_t d = uint64_t((saddr >> 4) & 0x3FFFu);
+  d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+  d |= uint64_t(1) << 46;  // descriptor version
+  d |= uint64_t(layout) << 61;
+  return d;
+}
+
+// Instruction descriptor: D fp32, A and B tf32, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int n, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(GM_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread
+// has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t r[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// fp32 -> tf32, round to nearest (ties away from zero), kept in an fp32 container.
+__device__ __forceinline__ float to_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi / lo split of n fp32 values (see the file comment).  n % 4 == 0 and
+// 16-byte aligned pointers take the vector path; the host guarantees both.
+__global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
+                                  int64_t n4) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = x[i];
+    float4 h, l;
+    h.x = to_tf32_rna(v.x);
+    h.y = to_tf32_rna(v.y);
+    h.z = to_tf32_rna(v.z);
+    h.w = to_tf32_rna(v.w);
+    l.x = to_tf32_rna(v.x - h.x);
+    l.y = to_tf32_rna(v.y - h.y);
+    l.z = to_tf32_rna(v.z - h.z);
+    l.w = to_tf32_rna(v.w - h.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// Loads the hi and lo tiles of one operand for k-block kb.  K-major: one box
+// {32 k, rows} at (k0, r0).  MN-major: nbox <= rows/32 boxes {32 mn, 32 k} at
+// (r0 + 32 j, k0), 4 KB apart; boxes that would lie wholly past the operand's
+// last row are not issued (their smem rows only feed outputs that are not
+// stored).  Boxes that straddle the edge are zero-filled by the TMA.
+template <int ROWS, bool MN>
+__device__ __forceinline__ void gemm_load_operand(unsigned char* hi_dst, unsigned char* lo_dst, const CUtensorMap* mhi,
+                                                  const CUtensorMap* mlo, uint64_t* bar, int r0, int k0, int nbox) {
+  if (!MN) {
+    tma_load_2d(hi_dst, mhi, bar, k0, r0);
+    tma_load_2d(lo_dst, mlo, bar, k0, r0);
+  } else {
+#pragma unroll
+    for (int j = 0; j < ROWS / 32; ++j) {
+      if (j < nbox) {
+        tma_load_2d(hi_dst + j * 4096, mhi, bar, r0 + 32 * j, k0);
+        tma_load_2d(lo_dst + j * 4096, mlo, bar, r0 + 32 * j, k0);
+      }
+    }
+  }
+}
+
+// Boxes of an MN-major operand tile starting at row r0 of `rows` that hold at
+// least one row (all ROWS/32 for a K-major operand, which loads one box).
+template <int ROWS, bool MN>
+__device__ __forceinline__ int gemm_nbox(int r0, int rows) {
+  return MN ? min(ROWS / 32, (rows - r0 + 31) / 32) : ROWS / 32;
+}
+
+// Descriptor of the kk-th K=8 step of an operand tile.  K-major: rows of
+// 128 bytes (32 k), 8-row atoms 1 KB apart (SBO), the step advances 32 bytes
+// along the row.  MN-major: 32-element column blocks of GM_BK rows 4 KB apart
+// (LBO), 4-row atoms of the 32-byte-chunk swizzle 512 bytes apart (SBO), the
+// step advances 8 rows.
+template <bool MN>
+__device__ __forceinline__ uint64_t gemm_desc(uint32_t tile, int kk) {
+  return MN ? umma_sdesc(tile + uint32_t(kk) * 1024u, uint32_t(GM_BK) * 128u, 512u, 1u)
+            : umma_sdesc(tile + uint32_t(kk) * 32u, 16u, 1024u, 2u);
+}
+
+struct GemmArgs {
+  int M, N, K;
+  int kb_per_split;  // k-blocks per CTA (grid z = number of K splits)
+  float* C;          // output (splits == 1) or the split partials (M x N each, row stride N)
+  int64_t ldc;
+  int64_t split_stride;  // elements between split partials
+};
+
+// C[m, n] = sum_k A[m, k] B[n, k] for the tile (blockIdx.x -> n, blockIdx.y -> m).
+//
+// Accumulation.  The tensor core's fp32 accumulation rounds toward zero
+// (measured on B200: with exactly representable TF32 inputs the error of a
+// chain of n MMAs has a mean of about -1.3e-8 n of the output's RMS, growing
+// with n).  So the large products of each k-block go into a fresh TMEM
+// accumulator (two buffers, alternating) and the epilogue warps add every
+// k-block's result into fp32 registers (round to nearest) while the next
+// k-block runs; the correction products (2^-11 of the size) accumulate in one
+// TMEM accumulator over the whole K range.
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+                       const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+                       const GemmArgs args, int* __restrict__ status) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int NST = Cfg::NST;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smb + Cfg::OFF_BAR);
+  uint64_t* empty = full + NST;
+  uint64_t* accf = empty + NST;  // [2]: k-block result ready in buffer b
+  uint64_t* acce = accf + 2;     // [2]: buffer b drained by the 4 epilogue warps
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(acce + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2) + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GM_BM;
+  const int nkb_total = (args.K + GM_BK - 1) / GM_BK;
+  const int kb0 = blockIdx.z * args.kb_per_split;
+  const int nkb = max(0, min(args.kb_per_split, nkb_total - kb0));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_fence_before_sync();
+  }
+  __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  // TMEM columns: large-product buffers at 0 and BN, correction products at 2 BN
+  const uint32_t col_small = 2u * uint32_t(BN);
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    prefetch_tmap(&ta_hi);
+    prefetch_tmap(&ta_lo);
+    prefetch_tmap(&tb_hi);
+    prefetch_tmap(&tb_lo);
+    const int nba = gemm_nbox<GM_BM, A_MN>(m0, args.M), nbb = gemm_nbox<BN, B_MN>(n0, args.N);
+    // bytes landing per stage: hi + lo of every issued box (32 x 32 fp32 = 4 KB)
+    const uint32_t tx = 2u * 4096u * uint32_t(nba + nbb);
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % NST;
+      if (i >= NST && !mbar_wait<true>(&empty[s], uint32_t((i / NST) - 1) & 1u, abort_flag, status)) break;
+      unsigned char* st = smb + s * Cfg::STAGE_B;
+      mbar_arrive_expect_tx(&full[s], tx);
+      const int k0 = (kb0 + i) * GM_BK;
+      gemm_load_operand<GM_BM, A_MN>(st, st + Cfg::OFF_ALO, &ta_hi, &ta_lo, &full[s], m0, k0, nba);
+      gemm_load_operand<BN, B_MN>(st + Cfg::OFF_BHI, st + Cfg::OFF_BLO, &tb_hi, &tb_lo, &full[s], n0, k0, nbb);
+      issued = i + 1;
+    }
+    // Drain: the last load of every stage has landed before the CTA may exit
+    // (on the normal path the MMA warp consumed them all already).
+    for (int i = max(0, issued - NST); i < issued; ++i)
+      (void)mbar_wait<true>(&full[i % NST], uint32_t(i / NST) & 1u, abort_flag, status);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN);
+    const uint32_t d_small = tmem_base + col_small;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % NST, b = i & 1;
+      // buffer b last held k-block i - 2: wait until the epilogue has read it
+      if (i >= 2 && !mbar_wait(&acce[b], uint32_t((i >> 1) - 1) & 1u, abort_flag, status)) break;
+      if (!mbar_wait(&full[s], uint32_t(i / NST) & 1u, abort_flag, status)) break;
+      tmem_fence_after_sync();
+      const uint32_t st = smem_u32(smb + s * Cfg::STAGE_B);
+      const uint32_t d_big = tmem_base + uint32_t(b * BN);
+#pragma unroll
+      for (int kk = 0; kk < GM_BK / 8; ++kk) {
+        const uint64_t ahi = gemm_desc<A_MN>(st, kk), alo = gemm_desc<A_MN>(st + Cfg::OFF_ALO, kk);
+        const uint64_t bhi = gemm_desc<B_MN>(st + Cfg::OFF_BHI, kk), blo = gemm_desc<B_MN>(st + Cfg::OFF_BLO, kk);
+        umma_tf32(d_big, ahi, bhi, idesc, kk > 0 ? 1u : 0u);
+        umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_tf32(d_small, alo, bhi, idesc, 1u);
+      }
+      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      umma_commit(&accf[b]);   // and buffer b holds this k-block's large products
+    }
+  } else if (warp >= GM_EPI_WARP0) {
+    // ---- epilogue: per k-block TMEM -> fp32 registers, then the tile -> global ----
+    const int q = warp - GM_EPI_WARP0;  // TMEM lane quarter
+    const int row = m0 + 32 * q + lane;
+    const uint32_t lane_addr = tmem_base + (uint32_t(32 * q) << 16);
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nkb; ++i) {
+      const int b = i & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], uint32_t(i >> 1) & 1u, abort_flag, status));
+      if (!ok) break;
+      tmem_fence_after_sync();
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + uint32_t(b * BN + c), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c + j] += __uint_as_float(r[j]);
+      }
+      tmem_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
+    }
+    ok = ok && nkb > 0;
+    float* out = args.C + int64_t(blockIdx.z) * args.split_stride + int64_t(row) * args.ldc;
+    const bool row_ok = ok && row < args.M;
+    const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0) &&
+                     (args.split_stride % 4 == 0);
+    // the last k-block's commit also covered every correction-product MMA
+#pragma unroll
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(lane_addr + col_small + uint32_t(c), r);
+      tmem_wait_ld();
+      if (!row_ok) continue;
+      const int col0 = n0 + c;
+      if (vec && col0 + 32 <= args.N) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 v;
+          v.x = acc[c + j] + __uint_as_float(r[j]);
+          v.y = acc[c + j + 1] + __uint_as_float(r[j + 1]);
+          v.z = acc[c + j + 2] + __uint_as_float(r[j + 2]);
+          v.w = acc[c + j + 3] + __uint_as_float(r[j + 3]);
+          *reinterpret_cast<float4*>(out + col0 + j) = v;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < args.N) out[col0 + j] = acc[c + j] + __uint_as_float(r[j]);
+      }
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tmem_fence_after_sync();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// Sums the K-split partials in split order: C = sum_s P_s (P_s: M x N, row
+// stride N, split_stride apart).
+__global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ C, int64_t ldc, int M,
+                                          int N, int splits, int64_t split_stride) {
+  const int64_t total = int64_t(M) * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    float acc = part[i];
+    for (int s = 1; s < splits; ++s) acc += part[int64_t(s) * split_stride + i];
+    const int64_t m = i / N, n = i % N;
+    C[m * ldc + n] = acc;
+  }
+}
+
+}  // namespace vmscan

@@ -139,3 +139,22 @@ def test_plain_sequence_geometry():
     assert geom[11] == 16 and geom[12] == 13  # T, nboxes
     got, _ = _order(ScanDirection(reverse=True), 33, 0)
     assert got == list(range(32, -1, -1))
+
+
+def test_gemm_host_validation_and_plan():
+    """The tensor-core GEMM's host checks and its K-split plan (no CUDA work:
+    every call returns before encoding a tensor map)."""
+    lib = _native.load()
+    P = ctypes.c_void_p
+    assert lib.vmscan_gemm_tf32x3(0, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, None, 0, None) == 2
+    assert lib.vmscan_gemm_tf32x3(8, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, None, 8, None, 0, None) == 1
+    assert lib.vmscan_gemm_tf32x3(8, 16, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, None, 0, None) == 2
+    assert lib.vmscan_tf32_split(6, P(16), P(16), P(16), None) == 2
+    assert lib.vmscan_tf32_split(8, None, P(16), P(16), None) == 1
+    assert lib.vmscan_tf32_split(0, None, None, None, None) == 0
+    assert lib.vmscan_gemm_workspace_bytes(0, 8, 8) == -2
+    # output tiles that fill the GPU: no split, no workspace
+    assert lib.vmscan_gemm_workspace_bytes(12544, 6144, 384) == 0
+    # out_proj weight gradient of the 2D model: 3 x 24 tiles, split over K
+    ws = lib.vmscan_gemm_workspace_bytes(384, 3072, 12544)
+    assert ws >= 2 * 384 * 3072 * 4 and ws % 256 == 0

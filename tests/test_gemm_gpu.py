@@ -1,0 +1,102 @@
+"""Tensor-core projection GEMM (vmscan_gemm_tf32x3 through the C ABI) against
+fp64, with PyTorch's fp32 SIMT GEMM as the fp32 reference (TF32 off): the
+same parity rule as every other kernel (tests/parity.py).  Covers the four
+operand layouts, ragged tile edges, the K-split path, and the shapes of the
+VisionMamba-2D in_proj / out_proj and their gradients."""
+
+import pytest
+import torch
+
+from parity import assert_parity
+
+from mlx_vision_mamba_b200 import device_status
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_tf32():
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def _operand(rows, cols, mn, gen, scale=1.0):
+    """A logical (rows x cols) operand stored row-major, or transposed (MN-major)."""
+    x = torch.randn(rows, cols, generator=gen, dtype=torch.float64) * scale
+    stored = x.t().contiguous() if mn else x.contiguous()
+    return x, stored
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("m,n,k", [(200, 96, 72), (128, 128, 32), (260, 160, 100), (1568, 512, 384)])
+def test_gemm_layouts(m, n, k, a_mn, b_mn):
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    gen = torch.Generator().manual_seed(m * 7 + n * 3 + k + 2 * a_mn + b_mn)
+    a, a_st = _operand(m, k, a_mn, gen)
+    b, b_st = _operand(n, k, b_mn, gen)
+    dev = torch.device("cuda", 0)
+    a32 = a_st.float().to(dev)
+    b32 = b_st.float().to(dev)
+    c = gemm_tf32x3(tf32_split(a32), a_mn, tf32_split(b32), b_mn, m, n, k)
+    assert device_status(dev, clear=True) == 0, "a bounded device wait of the GEMM gave up"
+    exact = a.float().double() @ b.float().double().t()
+    ref32 = (a.float() @ b.float().t())
+    assert_parity(f"gemm {m}x{n}x{k} a_mn={a_mn} b_mn={b_mn}", c.cpu(), exact, ref32)
+
+
+def test_gemm_splitk_out_proj_weight_grad():
+    """dW of the 2D model's out_proj: M 384, N 3072, K 12544 (72 tiles, split over K)."""
+    from mlx_vision_mamba_b200 import _native
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    lib = _native.load()
+    m, n, k = 384, 3072, 12544
+    assert lib.vmscan_gemm_workspace_bytes(m, n, k) > 0
+    gen = torch.Generator().manual_seed(5)
+    dev = torch.device("cuda", 0)
+    dy = torch.randn(k, m, generator=gen).to(dev)
+    y = torch.randn(k, n, generator=gen).to(dev)
+    c = gemm_tf32x3(tf32_split(dy), True, tf32_split(y), True, m, n, k)
+    exact = dy.double().t() @ y.double()
+    ref32 = dy.t() @ y
+    assert_parity("gemm splitK 384x3072x12544", c, exact, ref32)
+    c2 = gemm_tf32x3(tf32_split(dy), True, tf32_split(y), True, m, n, k)
+    assert torch.equal(c, c2), "split-K sum is not deterministic"
+
+
+@pytest.mark.parametrize("t,fin,fout", [(12544, 384, 6144), (12544, 3072, 384), (392, 768, 3072)])
+def test_linear_tc_fwd_bwd(t, fin, fout):
+    """linear_tc forward, input and weight gradient at the in_proj / out_proj
+    shapes of VisionMamba-2D (t = 64 x 196 tokens) and config 1 (2 x 196)."""
+    from mlx_vision_mamba_b200.linear import linear_tc
+
+    gen = torch.Generator().manual_seed(t + fin + fout)
+    dev = torch.device("cuda", 0)
+    x = torch.randn(t, fin, generator=gen).to(dev)
+    w = (torch.rand(fout, fin, generator=gen) * 2 - 1).mul_(fin ** -0.5).to(dev)
+    dy = torch.randn(t, fout, generator=gen).to(dev)
+    xg = x.clone().requires_grad_(True)
+    wg = w.clone().requires_grad_(True)
+    y = linear_tc(xg, wg)
+    y.backward(dy)
+    x64, w64, dy64 = x.double(), w.double(), dy.double()
+    assert_parity(f"linear_tc y {t}x{fin}->{fout}", y.detach(), x64 @ w64.t(), x @ w.t())
+    assert_parity(f"linear_tc dx {t}x{fin}->{fout}", xg.grad, dy64 @ w64, dy @ w)
+    assert_parity(f"linear_tc dw {t}x{fin}->{fout}", wg.grad, dy64.t() @ x64, dy.t() @ x)
+
+
+def test_tf32_split_exact():
+    """hi + lo reproduces x to 2^-21 relative, hi and lo carry at most 11 significant bits."""
+    from mlx_vision_mamba_b200.linear import tf32_split
+
+    gen = torch.Generator().manual_seed(11)
+    x = (torch.randn(1 << 16, generator=gen) * torch.exp(torch.randn(1 << 16, generator=gen) * 4)).cuda()
+    hi, lo = tf32_split(x)
+    low13 = (1 << 13) - 1
+    assert int((hi.view(torch.int32) & low13).abs().sum()) == 0
+    assert int((lo.view(torch.int32) & low13).abs().sum()) == 0
+    err = (hi.double() + lo.double() - x.double()).abs()
+    assert bool((err <= x.double().abs() * 2.0 ** -21).all())
