@@ -3,8 +3,8 @@
 Class names, constructor arguments, parameter names and parameter shapes follow
 the reference (MLX layouts, e.g. conv1d.weight is (d_inner, d_conv, 1)), so an
 MLX checkpoint's arrays load by name.  The selective scan, its SiLU gate and the
-causal conv1d+SiLU run in the sm_100a kernels of libvmscan.so; the projections
-are cuBLAS GEMMs.  Multi-directional scans never build permuted copies: each
+causal conv1d+SiLU run in the sm_100a kernels of libvmscan.so; in_proj and
+out_proj run on its tensor-core GEMM (linear.py), x_proj on cuBLAS.  Multi-directional scans never build permuted copies: each
 direction is a descriptor passed to the kernels (direction.py).
 
 Deliberate deviations from the reference, all documented:
@@ -27,6 +27,7 @@ import torch.nn.functional as F
 
 from .direction import BACKWARD, ScanDirection, directions_for
 from .branches import branches_forward
+from .linear import linear_tc, supported as _tc_supported
 from .scan import conv1d_silu_cuda, dt_softplus_cuda, selective_scan_cuda
 
 GPU_SCAN_MODES = ("cuda_fused", "metal_fused", "metal_train", "metal")
@@ -116,9 +117,10 @@ class MambaBlock(nn.Module):
 
     def forward(self, x: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
         if _fused_branches_ok([self], x):
-            xz = self.in_proj(x)
-            return self.out_proj(branches_forward([self], [direction], xz, _branch_streams(x.device, 1)))
-        return self.out_proj(self.scan_branch(self.in_proj(x), direction))
+            xz = project(x, self.in_proj.weight)
+            y = branches_forward([self], [direction], xz, _branch_streams(x.device, 1))
+            return project(y, self.out_proj.weight)
+        return project(self.scan_branch(project(x, self.in_proj.weight), direction), self.out_proj.weight)
 
     def scan_branch(self, xz: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
         """Everything between in_proj and out_proj (mamba_block.py:166-190): xz is
@@ -137,6 +139,14 @@ class MambaBlock(nn.Module):
         return selective_scan_cuda(x_branch, delta, A, B_proj, C_proj, self.D, z=z, direction=direction)
 
 
+def project(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """x @ weight.T (in_proj / out_proj, no bias): on CUDA the fp32-accurate
+    tensor-core GEMM of linear.py, elsewhere F.linear."""
+    if _tc_supported(x, weight):
+        return linear_tc(x, weight)
+    return F.linear(x, weight)
+
+
 def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[ScanDirection]], h: torch.Tensor):
     """sum_k blocks[k](h, directions[k]) with the projections batched over the
     directions: one in_proj GEMM against the K blocks' concatenated weights
@@ -147,18 +157,18 @@ def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[S
     if len(blocks) == 1:
         return blocks[0](h, directions[0])
     two_dn = 2 * blocks[0].d_inner
-    xz = F.linear(h, torch.cat([b.in_proj.weight for b in blocks], 0))
+    xz = project(h, torch.cat([b.in_proj.weight for b in blocks], 0))
     if _fused_branches_ok(blocks, h):
         # one autograd node for the K branches: outputs and input gradients
         # written into slices, no concatenation passes (branches.py)
         y = branches_forward(blocks, directions, xz, _branch_streams(h.device, len(blocks)))
-        return F.linear(y, torch.cat([b.out_proj.weight for b in blocks], 1))
+        return project(y, torch.cat([b.out_proj.weight for b in blocks], 1))
     parts = torch.split(xz, two_dn, dim=-1)
     if h.is_cuda:
         ys = _branches_on_streams(blocks, directions, parts)
     else:
         ys = [b.scan_branch(part, d) for b, d, part in zip(blocks, directions, parts)]
-    return F.linear(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
+    return project(torch.cat(ys, -1), torch.cat([b.out_proj.weight for b in blocks], 1))
 
 
 def _fused_branches_ok(blocks, h: torch.Tensor) -> bool:
