@@ -340,8 +340,9 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
  *   B(n, k) = b[n * ldb + k] (b_mn_major == 0) or b[k * ldb + n] (!= 0),
  * as A_hi B_hi + (A_hi B_lo + A_lo B_hi) with the large and the correction
  * products in separate fp32 accumulators.  lda, ldb: multiples of 4, all
- * operand pointers 16-byte aligned.  When the output tiles would not fill the
- * GPU, K is split and the partials are summed in a fixed order; that needs
+ * operand pointers 16-byte aligned.  accumulate != 0 adds the product to C
+ * (C += A B^T).  When the output tiles would not fill the GPU, K is split and
+ * the partials are summed in a fixed order; that needs
  * vmscan_gemm_workspace_bytes(M, N, K) bytes of workspace (0: none).
  */
 int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_stream_t stream);
@@ -349,7 +350,7 @@ int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
                        const float* a_hi, const float* a_lo, int64_t lda, int a_mn_major,
                        const float* b_hi, const float* b_lo, int64_t ldb, int b_mn_major,
-                       float* c, int64_t ldc, void* workspace, int64_t workspace_bytes,
+                       float* c, int64_t ldc, int accumulate, void* workspace, int64_t workspace_bytes,
                        vmscan_stream_t stream);
 
 /*

@@ -115,7 +115,8 @@ SIGNATURES = {
     "vmscan_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "vmscan_gemm_tf32x3": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _p, _p, _i64, ctypes.c_int, _p, _p, _i64, ctypes.c_int, _p, _i64, _p, _i64, _p],
+        [_i64, _i64, _i64, _p, _p, _i64, ctypes.c_int, _p, _p, _i64, ctypes.c_int, _p, _i64, ctypes.c_int, _p, _i64,
+         _p],
     ),
     "vmscan_scan_order": (ctypes.c_int, [_i64, _D, ctypes.c_int, _p, _p]),
     "vmscan_device_status": (ctypes.c_int, [_p, ctypes.c_int]),

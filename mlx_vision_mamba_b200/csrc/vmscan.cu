@@ -606,7 +606,9 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
 
 namespace {
 
-constexpr int kGemmBN = 128;
+// Output tile width: the narrowest of 32, 64, 128 columns that covers N
+// (the skinny x_proj / dt_proj products), 128 otherwise.
+int gemm_bn(int64_t N) { return N <= 32 ? 32 : (N <= 64 ? 64 : 128); }
 
 // 2-D tensor map of a row-major (rows x cols) fp32 matrix with row stride ld
 // (elements): box {32, box_rows}, zero fill outside, 128-byte swizzle of
@@ -636,13 +638,14 @@ int encode_gemm_map(CUtensorMap* m, const char* what, const float* p, int64_t co
 // K splits of a GEMM: 1 while the output tiles fill the SMs, otherwise enough
 // splits to fill them with at least 8 k-blocks each (at most 8 splits).
 struct GemmPlan {
-  int tiles_n, tiles_m, splits, kb_per_split;
+  int bn, tiles_n, tiles_m, splits, kb_per_split;
   size_t ws_bytes;
 };
 
 GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   GemmPlan p;
-  p.tiles_n = int((N + kGemmBN - 1) / kGemmBN);
+  p.bn = gemm_bn(N);
+  p.tiles_n = int((N + p.bn - 1) / p.bn);
   p.tiles_m = int((M + GM_BM - 1) / GM_BM);
   const int nkb = int((K + GM_BK - 1) / GM_BK);
   const int64_t tiles = int64_t(p.tiles_n) * p.tiles_m;
@@ -656,11 +659,11 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   return p;
 }
 
-template <bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN>
 int launch_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
                 const GemmPlan& p, const GemmArgs& a, cudaStream_t s) {
-  using Cfg = GemmCfg<kGemmBN>;
-  auto kern = gemm_tf32x3_kernel<kGemmBN, A_MN, B_MN>;
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tf32x3_kernel<BN, A_MN, B_MN>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(gemm_tf32x3_kernel) failed");
   int* st = status_ptr();
@@ -668,6 +671,14 @@ int launch_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
   kern<<<dim3(unsigned(p.tiles_n), unsigned(p.tiles_m), unsigned(p.splits)), GM_THREADS, Cfg::SMEM_BYTES, s>>>(
       ahi, alo, bhi, blo, a, st);
   return check_launch();
+}
+
+template <bool A_MN, bool B_MN>
+int launch_gemm_bn(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
+                   const GemmPlan& p, const GemmArgs& a, cudaStream_t s) {
+  if (p.bn == 32) return launch_gemm<32, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
+  if (p.bn == 64) return launch_gemm<64, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
+  return launch_gemm<128, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
 }
 
 }  // namespace
@@ -975,7 +986,8 @@ int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 
 int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const float* a_lo, int64_t lda,
                        int a_mn_major, const float* b_hi, const float* b_lo, int64_t ldb, int b_mn_major, float* c,
-                       int64_t ldc, void* workspace, int64_t workspace_bytes, vmscan_stream_t stream) {
+                       int64_t ldc, int accumulate, void* workspace, int64_t workspace_bytes,
+                       vmscan_stream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
     return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld, N %lld, K %lld", (long long)M, (long long)N, (long long)K);
   if (c == nullptr) return VMSCAN_ERR_NULL;
@@ -987,12 +999,12 @@ int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const
   // A(m, k): K-major a[m * lda + k] (rows M), MN-major a[k * lda + m] (rows K)
   const int64_t acols = a_mn_major ? M : K, arows = a_mn_major ? K : M;
   const int64_t bcols = b_mn_major ? N : K, brows = b_mn_major ? K : N;
-  const int abox = a_mn_major ? 32 : GM_BM, bbox = b_mn_major ? 32 : kGemmBN;
+  const GemmPlan p = gemm_plan(M, N, K);
+  const int abox = a_mn_major ? 32 : GM_BM, bbox = b_mn_major ? 32 : p.bn;
   VM_TRY(encode_gemm_map(&ahi, "a_hi", a_hi, acols, arows, lda, abox, a_mn_major != 0));
   VM_TRY(encode_gemm_map(&alo, "a_lo", a_lo, acols, arows, lda, abox, a_mn_major != 0));
   VM_TRY(encode_gemm_map(&bhi, "b_hi", b_hi, bcols, brows, ldb, bbox, b_mn_major != 0));
   VM_TRY(encode_gemm_map(&blo, "b_lo", b_lo, bcols, brows, ldb, bbox, b_mn_major != 0));
-  const GemmPlan p = gemm_plan(M, N, K);
   if (p.splits > 1 && (workspace == nullptr || workspace_bytes < int64_t(p.ws_bytes)))
     return fail(VMSCAN_ERR_WORKSPACE, "gemm: %d K splits need %zu bytes of workspace", p.splits, p.ws_bytes);
   if (p.splits > 1 && !aligned16(workspace)) return fail(VMSCAN_ERR_ALIGN, "gemm: workspace not 16-byte aligned");
@@ -1001,24 +1013,25 @@ int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const
   a.N = int(N);
   a.K = int(K);
   a.kb_per_split = p.kb_per_split;
+  a.accumulate = (accumulate && p.splits == 1) ? 1 : 0;
   a.C = p.splits > 1 ? static_cast<float*>(workspace) : c;
   a.ldc = p.splits > 1 ? N : ldc;
   a.split_stride = M * N;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc;
   if (a_mn_major && b_mn_major)
-    rc = launch_gemm<true, true>(ahi, alo, bhi, blo, p, a, s);
+    rc = launch_gemm_bn<true, true>(ahi, alo, bhi, blo, p, a, s);
   else if (a_mn_major)
-    rc = launch_gemm<true, false>(ahi, alo, bhi, blo, p, a, s);
+    rc = launch_gemm_bn<true, false>(ahi, alo, bhi, blo, p, a, s);
   else if (b_mn_major)
-    rc = launch_gemm<false, true>(ahi, alo, bhi, blo, p, a, s);
+    rc = launch_gemm_bn<false, true>(ahi, alo, bhi, blo, p, a, s);
   else
-    rc = launch_gemm<false, false>(ahi, alo, bhi, blo, p, a, s);
+    rc = launch_gemm_bn<false, false>(ahi, alo, bhi, blo, p, a, s);
   if (rc != VMSCAN_OK || p.splits == 1) return rc;
   const int64_t total = M * N;
   const unsigned blocks = unsigned(std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 8));
   gemm_splitk_reduce_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(workspace), c, ldc, int(M), int(N),
-                                                   p.splits, M * N);
+                                                   p.splits, M * N, accumulate ? 1 : 0);
   return check_launch();
 }
 

@@ -36,16 +36,16 @@ constexpr int GM_EPI_WARP0 = 4;  // warps 4..7 read TMEM lane quarters 0..3
 
 template <int BN>
 struct GemmCfg {
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN: multiple of 32 up to 256");
+  static_assert(BN == 32 || BN == 64 || BN == 128, "BN: 32, 64 or 128");
   static constexpr int A_TILE_B = GM_BM * GM_BK * 4;  // 16 KB
   static constexpr int B_TILE_B = BN * GM_BK * 4;
   static constexpr int OFF_ALO = A_TILE_B, OFF_BHI = 2 * A_TILE_B, OFF_BLO = 2 * A_TILE_B + B_TILE_B;
   static constexpr int STAGE_B = 2 * A_TILE_B + 2 * B_TILE_B;
-  static constexpr int NST = (196 * 1024) / STAGE_B;
+  static constexpr int NST = (196 * 1024) / STAGE_B < 6 ? (196 * 1024) / STAGE_B : 6;
   static_assert(NST >= 2, "at least two stages");
   // accumulators: two large-product buffers (columns 0, BN), correction products (2 BN)
   static_assert(3 * BN <= 512, "three accumulators of BN columns");
-  static constexpr uint32_t TMEM_COLS = 3 * BN <= 256 ? 256u : 512u;
+  static constexpr uint32_t TMEM_COLS = 3 * BN <= 128 ? 128u : (3 * BN <= 256 ? 256u : 512u);
   static constexpr int OFF_BAR = NST * STAGE_B;
   static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 4) * 8 + 16 + 1024;
 };
@@ -177,6 +177,7 @@ __device__ __forceinline__ uint64_t gemm_desc(uint32_t tile, int kk) {
 struct GemmArgs {
   int M, N, K;
   int kb_per_split;  // k-blocks per CTA (grid z = number of K splits)
+  int accumulate;    // C += A B (one split only) instead of C = A B
   float* C;          // output (splits == 1) or the split partials (M x N each, row stride N)
   int64_t ldc;
   int64_t split_stride;  // elements between split partials
@@ -330,12 +331,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           v.y = acc[c + j + 1] + __uint_as_float(r[j + 1]);
           v.z = acc[c + j + 2] + __uint_as_float(r[j + 2]);
           v.w = acc[c + j + 3] + __uint_as_float(r[j + 3]);
-          *reinterpret_cast<float4*>(out + col0 + j) = v;
+          float4* dst = reinterpret_cast<float4*>(out + col0 + j);
+          if (args.accumulate) {
+            const float4 o = *dst;
+            v.x += o.x;
+            v.y += o.y;
+            v.z += o.z;
+            v.w += o.w;
+          }
+          *dst = v;
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (col0 + j < args.N) out[col0 + j] = acc[c + j] + __uint_as_float(r[j]);
+          if (col0 + j < args.N) {
+            const float v = acc[c + j] + __uint_as_float(r[j]);
+            out[col0 + j] = args.accumulate ? out[col0 + j] + v : v;
+          }
       }
     }
   }
@@ -348,15 +360,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 }
 
 // Sums the K-split partials in split order: C = sum_s P_s (P_s: M x N, row
-// stride N, split_stride apart).
+// stride N, split_stride apart), or C += that sum.
 __global__ void gemm_splitk_reduce_kernel(const float* __restrict__ part, float* __restrict__ C, int64_t ldc, int M,
-                                          int N, int splits, int64_t split_stride) {
+                                          int N, int splits, int64_t split_stride, int accumulate) {
   const int64_t total = int64_t(M) * N;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     float acc = part[i];
     for (int s = 1; s < splits; ++s) acc += part[int64_t(s) * split_stride + i];
     const int64_t m = i / N, n = i % N;
-    C[m * ldc + n] = acc;
+    C[m * ldc + n] = accumulate ? C[m * ldc + n] + acc : acc;
   }
 }
 

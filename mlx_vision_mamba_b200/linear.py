@@ -42,23 +42,29 @@ def tf32_split(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
 
 
 def gemm_tf32x3(a: Tuple[torch.Tensor, torch.Tensor], a_mn: bool, b: Tuple[torch.Tensor, torch.Tensor], b_mn: bool,
-                m: int, n: int, k: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                m: int, n: int, k: int, out: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
     """C (m x n, row-major) = A B^T from split operands: A(i, j) is a[i, j]
     (a_mn False, a is m x k) or a[j, i] (a_mn True, a is k x m); B(i, j) is
-    b[i, j] (b is n x k) or b[j, i] (b is k x n)."""
+    b[i, j] (b is n x k) or b[j, i] (b is k x n).  The operands may be column
+    slices of wider rows (their row stride is passed); `out` (m x n, unit
+    column stride, any row stride) receives C, or C is added to it when
+    `accumulate`."""
     lib = _native.load()
     a_hi, a_lo = a
     b_hi, b_lo = b
     dev = a_hi.device
     if out is None:
         out = torch.empty((m, n), dtype=torch.float32, device=dev)
+    assert out.shape == (m, n) and out.stride(1) == 1, "gemm_tf32x3: out must be (m, n) with unit column stride"
+    for t in (a_hi, a_lo, b_hi, b_lo):
+        assert t.stride(-1) == 1, "gemm_tf32x3: operands need unit column stride"
     ws_n = lib.vmscan_gemm_workspace_bytes(m, n, k)
     if ws_n < 0:
         _native.check(-ws_n, "vmscan_gemm_workspace_bytes")
     ws = torch.empty(int(ws_n), dtype=torch.uint8, device=dev) if ws_n > 0 else None
     _native.check(lib.vmscan_gemm_tf32x3(m, n, k, _ptr(a_hi), _ptr(a_lo), a_hi.stride(0), int(a_mn), _ptr(b_hi),
-                                         _ptr(b_lo), b_hi.stride(0), int(b_mn), _ptr(out), out.stride(0), _ptr(ws),
-                                         int(ws_n), _stream(dev)), "vmscan_gemm_tf32x3")
+                                         _ptr(b_lo), b_hi.stride(0), int(b_mn), _ptr(out), out.stride(0),
+                                         int(accumulate), _ptr(ws), int(ws_n), _stream(dev)), "vmscan_gemm_tf32x3")
     return out
 
 

@@ -146,9 +146,9 @@ def test_gemm_host_validation_and_plan():
     every call returns before encoding a tensor map)."""
     lib = _native.load()
     P = ctypes.c_void_p
-    assert lib.vmscan_gemm_tf32x3(0, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, None, 0, None) == 2
-    assert lib.vmscan_gemm_tf32x3(8, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, None, 8, None, 0, None) == 1
-    assert lib.vmscan_gemm_tf32x3(8, 16, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, None, 0, None) == 2
+    assert lib.vmscan_gemm_tf32x3(0, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, 0, None, 0, None) == 2
+    assert lib.vmscan_gemm_tf32x3(8, 8, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, None, 8, 0, None, 0, None) == 1
+    assert lib.vmscan_gemm_tf32x3(8, 16, 8, P(16), P(16), 8, 0, P(16), P(16), 8, 0, P(16), 8, 0, None, 0, None) == 2
     assert lib.vmscan_tf32_split(6, P(16), P(16), P(16), None) == 2
     assert lib.vmscan_tf32_split(8, None, P(16), P(16), None) == 1
     assert lib.vmscan_tf32_split(0, None, None, None, None) == 0

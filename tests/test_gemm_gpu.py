@@ -100,3 +100,40 @@ def test_tf32_split_exact():
     assert int((lo.view(torch.int32) & low13).abs().sum()) == 0
     err = (hi.double() + lo.double() - x.double()).abs()
     assert bool((err <= x.double().abs() * 2.0 ** -21).all())
+
+
+def test_gemm_skinny_slices_and_accumulate():
+    """The x_proj / dt_proj products of the 2D block (narrow 32- and 64-column
+    tiles): operands that are column slices of wider rows, an output slice,
+    and C += A B^T."""
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    gen = torch.Generator().manual_seed(17)
+    dev = torch.device("cuda", 0)
+    t, dn, r, wide = 12544, 768, 24, 56
+    xc = torch.randn(t, dn, generator=gen).to(dev)
+    wx = (torch.randn(wide, dn, generator=gen) / dn ** 0.5).to(dev)
+    dpre = torch.randn(t, dn, generator=gen).to(dev)
+    wdt = (torch.randn(dn, r, generator=gen) / r ** 0.5).to(dev)
+    xdbc = torch.randn(t, wide, generator=gen).to(dev)
+    du0 = torch.randn(t, dn, generator=gen).to(dev)
+    xc_s, xdbc_s, dpre_s = tf32_split(xc), tf32_split(xdbc), tf32_split(dpre)
+    # x_proj forward (N 56: 64-column tiles)
+    y = gemm_tf32x3(xc_s, False, tf32_split(wx), False, t, wide, dn)
+    assert_parity("skinny x_proj fwd", y, xc.double() @ wx.double().t(), xc @ wx.t())
+    # dt_proj input gradient into a column slice (N 24: 32-column tiles, ldc 56)
+    out = torch.full((t, wide), 7.0, device=dev)
+    gemm_tf32x3(dpre_s, False, tf32_split(wdt), True, t, r, dn, out=out[:, :r])
+    assert_parity("skinny dt dx", out[:, :r], dpre.double() @ wdt.double(), dpre @ wdt)
+    assert bool((out[:, r:] == 7.0).all()), "columns outside the output slice were written"
+    # dt_proj weight gradient with B a column slice (row stride 56), K split
+    g = gemm_tf32x3(dpre_s, True, (xdbc_s[0][:, :r], xdbc_s[1][:, :r]), True, dn, r, t)
+    assert_parity("skinny dt dW", g, dpre.double().t() @ xdbc[:, :r].double(), dpre.t() @ xdbc[:, :r])
+    # x_proj input gradient accumulated onto du
+    du = du0.clone()
+    gemm_tf32x3(xdbc_s, False, tf32_split(wx), True, t, dn, wide, out=du, accumulate=True)
+    assert_parity("skinny x_proj dx accumulate", du, du0.double() + xdbc.double() @ wx.double(),
+                  du0 + xdbc @ wx)
+    # x_proj weight gradient (M 56 < one tile)
+    gx = gemm_tf32x3(xdbc_s, True, xc_s, True, wide, dn, t)
+    assert_parity("skinny x_proj dW", gx, xdbc.double().t() @ xc.double(), xdbc.t() @ xc)
