@@ -345,6 +345,34 @@ def launch_only(reps, bf16):
     return 1 if st else 0
 
 
+def launch_only_gemm(reps, which):
+    """REPS launches of one projection GEMM of the VisionMamba-2D block (64 x
+    196 tokens, E 384, K=4) on split operands made once beforehand, untimed."""
+    import torch
+
+    from mlx_vision_mamba_b200 import device_status
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4)
+    t = 64 * 196
+    name, kind = which.rsplit("_", 1)
+    fin, fout = (384, 6144) if name == "in_proj" else (3072, 384)
+    x = tf32_split(torch.randn(t, fin, device=dev, generator=g))
+    w = tf32_split(torch.randn(fout, fin, device=dev, generator=g) / fin ** 0.5)
+    dy = tf32_split(torch.randn(t, fout, device=dev, generator=g))
+    for _ in range(reps):
+        if kind == "fwd":
+            gemm_tf32x3(x, False, w, False, t, fout, fin)
+        elif kind == "dx":
+            gemm_tf32x3(dy, False, w, True, t, fin, fout)
+        else:
+            gemm_tf32x3(dy, True, x, True, fout, fin, t)
+    st = device_status(dev, clear=True)
+    print(json.dumps({"launch_only": {"gemm": which, "reps": reps, "device_status": st}}), flush=True)
+    return 1 if st else 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -378,14 +406,19 @@ def main():
                          "PyTorch's fp32 GEMM")
     ap.add_argument("--launch-only", type=int, metavar="REPS",
                     help="run REPS forward + VJP pairs through the C ABI at --batch/--seqlen/--dinner (--io "
-                         "picks fp32 or bf16 I/O), untimed, and exit nonzero if the device status is set "
-                         "(small ncu captures)")
+                         "picks fp32 or bf16 I/O), or with --launch-gemm REPS projection GEMMs, untimed, and exit "
+                         "nonzero if the device status is set (small ncu captures)")
+    ap.add_argument("--launch-gemm", choices=["in_proj_fwd", "in_proj_dx", "in_proj_dw", "out_proj_fwd",
+                                              "out_proj_dx", "out_proj_dw"],
+                    help="with --launch-only: the VisionMamba-2D projection GEMM to launch")
     args = ap.parse_args()
     WORKLOAD.update(batch=args.batch, seqlen=args.seqlen, d_inner=args.dinner)
     if args.impl == "reference":
         run_reference(args)
         return
     if args.launch_only:
+        if args.launch_gemm:
+            sys.exit(launch_only_gemm(args.launch_only, args.launch_gemm))
         sys.exit(launch_only(args.launch_only, args.io == "bf16"))
     if args.model_profile:
         profile_model(args.warmup)
