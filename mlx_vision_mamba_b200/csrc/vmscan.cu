@@ -668,8 +668,9 @@ int launch_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMa
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(gemm_tf32x3_kernel) failed");
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
-  kern<<<dim3(unsigned(p.tiles_n), unsigned(p.tiles_m), unsigned(p.splits)), GM_THREADS, Cfg::SMEM_BYTES, s>>>(
-      ahi, alo, bhi, blo, a, st);
+  const int64_t items = int64_t(p.tiles_n) * p.tiles_m * p.splits;
+  const unsigned grid = unsigned(std::min<int64_t>(items, sm_count()));
+  kern<<<grid, GM_THREADS, Cfg::SMEM_BYTES, s>>>(ahi, alo, bhi, blo, a, st);
   return check_launch();
 }
 
@@ -992,8 +993,8 @@ int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const
     return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld, N %lld, K %lld", (long long)M, (long long)N, (long long)K);
   if (c == nullptr) return VMSCAN_ERR_NULL;
   if (ldc < N) return fail(VMSCAN_ERR_SHAPE, "gemm: ldc %lld < N %lld", (long long)ldc, (long long)N);
-  if (int64_t((M + GM_BM - 1) / GM_BM) > 65535)
-    return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld exceeds the launch grid", (long long)M);
+  if ((M + GM_BM - 1) / GM_BM * ((N + 31) / 32) * 8 > INT32_MAX)
+    return fail(VMSCAN_ERR_SHAPE, "gemm: M %lld x N %lld has too many tiles", (long long)M, (long long)N);
   VM_TRY(ensure_context(c));
   CUtensorMap ahi, alo, bhi, blo;
   // A(m, k): K-major a[m * lda + k] (rows M), MN-major a[k * lda + m] (rows K)
@@ -1012,6 +1013,7 @@ int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const
   a.M = int(M);
   a.N = int(N);
   a.K = int(K);
+  a.splits = p.splits;
   a.kb_per_split = p.kb_per_split;
   a.accumulate = (accumulate && p.splits == 1) ? 1 : 0;
   a.C = p.splits > 1 ? static_cast<float*>(workspace) : c;

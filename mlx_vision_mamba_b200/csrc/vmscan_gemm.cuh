@@ -12,13 +12,13 @@
 // the large products alone, as it does in an fp32 FFMA loop.  The split is a
 // separate elementwise pass (tf32_split_kernel) whose outputs the GEMM reads.
 //
-// Design.  One CTA per 128 x BN tile of C (or per tile and K split), 256
-// threads: warp 0 lane 0 issues the TMA loads of the hi / lo tiles of A and
-// B into an NST-stage ring of mbarriers; warp 1 owns the TMEM allocation and
-// its lane 0 issues the tcgen05.mma instructions (3 per K=8 step) and the
-// tcgen05.commit that releases each stage; warps 4..7 (one per TMEM lane
-// quarter) read the two accumulators back with tcgen05.ld, add them and
-// store the tile.  Operand tiles use a 128-byte swizzle; an operand is
+// Design.  A persistent CTA per SM walks the 128 x BN output tiles (and K
+// splits), 320 threads: warp 0 lane 0 issues the TMA loads of the hi / lo
+// tiles of A and B into an NST-stage ring of mbarriers; warp 1 owns the TMEM
+// allocation and its lane 0 issues the tcgen05.mma instructions (3 per K=8
+// step) and the tcgen05.commit that releases each stage; warps 2..9 (two per
+// TMEM lane quarter, half the columns each) read the accumulators back with
+// tcgen05.ld, add them and store the tile.  Operand tiles use a 128-byte swizzle; an operand is
 // either K-major (rows of K contiguous, one TMA box of 32 x rows, 16-byte
 // chunks swizzled) or MN-major (rows of M or N contiguous: 32-element column
 // blocks of 32 K rows each, 4 KB apart, 32-byte chunks swizzled).  Every wait is bounded: on time-out the kernel
@@ -31,8 +31,9 @@ namespace vmscan {
 
 constexpr int GM_BM = 128;
 constexpr int GM_BK = 32;  // fp32 elements per k-block: one 128-byte swizzle row
-constexpr int GM_THREADS = 256;
-constexpr int GM_EPI_WARP0 = 4;  // warps 4..7 read TMEM lane quarters 0..3
+constexpr int GM_THREADS = 320;
+constexpr int GM_EPI_WARP0 = 2;  // warps 2..9: two epilogue warps per TMEM lane quarter
+constexpr int GM_EPI_WARPS = 8;
 
 template <int BN>
 struct GemmCfg {
@@ -43,11 +44,10 @@ struct GemmCfg {
   static constexpr int STAGE_B = 2 * A_TILE_B + 2 * B_TILE_B;
   static constexpr int NST = (196 * 1024) / STAGE_B < 6 ? (196 * 1024) / STAGE_B : 6;
   static_assert(NST >= 2, "at least two stages");
-  // accumulators: two large-product buffers (columns 0, BN), correction products (2 BN)
-  static_assert(3 * BN <= 512, "three accumulators of BN columns");
-  static constexpr uint32_t TMEM_COLS = 3 * BN <= 128 ? 128u : (3 * BN <= 256 ? 256u : 512u);
+  // accumulators: two large-product buffers (columns 0, BN), two correction buffers (2 BN, 3 BN)
+  static constexpr uint32_t TMEM_COLS = 4 * BN <= 128 ? 128u : (4 * BN <= 256 ? 256u : 512u);
   static constexpr int OFF_BAR = NST * STAGE_B;
-  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 4) * 8 + 16 + 1024;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 6) * 8 + 16 + 1024;
 };
 
 // ---- tcgen05 helpers ----
@@ -176,14 +176,66 @@ __device__ __forceinline__ uint64_t gemm_desc(uint32_t tile, int kk) {
 
 struct GemmArgs {
   int M, N, K;
-  int kb_per_split;  // k-blocks per CTA (grid z = number of K splits)
+  int splits;        // K splits (work items = output tiles x splits)
+  int kb_per_split;  // k-blocks per split
   int accumulate;    // C += A B (one split only) instead of C = A B
   float* C;          // output (splits == 1) or the split partials (M x N each, row stride N)
   int64_t ldc;
   int64_t split_stride;  // elements between split partials
 };
 
-// C[m, n] = sum_k A[m, k] B[n, k] for the tile (blockIdx.x -> n, blockIdx.y -> m).
+// Waits for this thread's outstanding tcgen05.ld and ties the 32 loaded
+// registers to the wait, so no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t r[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+// Loads NC (16, 32 or 64) consecutive TMEM columns of this thread's lane into
+// r and waits for them.
+template <int NC>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, uint32_t (&r)[NC]) {
+  static_assert(NC == 16 || NC == 32 || NC == 64, "16, 32 or 64 columns");
+  if constexpr (NC == 16) {
+    tmem_ld16(taddr, r);
+    tmem_wait_ld16(r);
+  } else if constexpr (NC == 32) {
+    tmem_ld32(taddr, r);
+    tmem_wait_ld32(r);
+  } else {
+    tmem_ld32(taddr, r);
+    tmem_ld32(taddr + 32u, r + 32);
+    tmem_wait_ld32(r);
+    tmem_wait_ld32(r + 32);
+  }
+}
+
+// Work items of a launch: (output tile, K split) pairs, n fastest, so that
+// the CTAs working at the same time share A row blocks (and B) in L2.
+struct GemmItem {
+  int m0, n0, split, kb0, nkb;
+};
+
+__device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int w, int bn, int tiles_n) {
+  GemmItem it;
+  const int splits = a.splits;
+  it.split = w % splits;
+  const int t = w / splits;
+  it.n0 = (t % tiles_n) * bn;
+  it.m0 = (t / tiles_n) * GM_BM;
+  const int nkb_total = (a.K + GM_BK - 1) / GM_BK;
+  it.kb0 = it.split * a.kb_per_split;
+  it.nkb = max(0, min(a.kb_per_split, nkb_total - it.kb0));
+  return it;
+}
+
+// Persistent GEMM: each CTA walks the work items blockIdx.x, + gridDim.x, ...
+// and every role keeps one running k-block count g over them, which drives
+// the stage ring (g % NST) and the large-product buffers (g & 1).
 //
 // Accumulation.  The tensor core's fp32 accumulation rounds toward zero
 // (measured on B200: with exactly representable TF32 inputs the error of a
@@ -192,7 +244,12 @@ struct GemmArgs {
 // accumulator (two buffers, alternating) and the epilogue warps add every
 // k-block's result into fp32 registers (round to nearest) while the next
 // k-block runs; the correction products (2^-11 of the size) accumulate in one
-// TMEM accumulator over the whole K range.
+// TMEM accumulator per work item (two, alternating between items, so that an
+// item's store overlaps the next item's MMAs).
+//
+// Roles (GM_THREADS = 320): warp 0 lane 0 TMA producer, warp 1 TMEM owner and
+// (lane 0) MMA issuer, warps 2..9 epilogue: warp w reads TMEM lane quarter
+// w % 4 and column half (w - 2) / 4 of the tile.
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
@@ -200,20 +257,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                        const GemmArgs args, int* __restrict__ status) {
   using Cfg = GemmCfg<BN>;
   constexpr int NST = Cfg::NST;
+  constexpr int HC = BN / 2;  // columns per epilogue warp
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
   uint64_t* full = reinterpret_cast<uint64_t*>(smb + Cfg::OFF_BAR);
   uint64_t* empty = full + NST;
-  uint64_t* accf = empty + NST;  // [2]: k-block result ready in buffer b
-  uint64_t* acce = accf + 2;     // [2]: buffer b drained by the 4 epilogue warps
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(acce + 2);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2) + 1;
+  uint64_t* accf = empty + NST;  // [2]: k-block result ready in large-product buffer b
+  uint64_t* acce = accf + 2;     // [2]: large-product buffer b drained by the 8 epilogue warps
+  uint64_t* sme = acce + 2;      // [2]: correction buffer c drained by the 8 epilogue warps
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sme + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sme + 2) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * GM_BM;
-  const int nkb_total = (args.K + GM_BK - 1) / GM_BK;
-  const int kb0 = blockIdx.z * args.kb_per_split;
-  const int nkb = max(0, min(args.kb_per_split, nkb_total - kb0));
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int tiles_m = (args.M + GM_BM - 1) / GM_BM;
+  const int items = tiles_m * tiles_n * args.splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -222,7 +280,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 4);
+      mbar_init(&acce[b], GM_EPI_WARPS);
+      mbar_init(&sme[b], GM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -234,8 +293,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   __syncthreads();
   tmem_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-  // TMEM columns: large-product buffers at 0 and BN, correction products at 2 BN
-  const uint32_t col_small = 2u * uint32_t(BN);
+  // TMEM columns: large-product buffers at 0 and BN, correction buffers at 2 BN and 3 BN
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
@@ -243,95 +301,116 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     prefetch_tmap(&ta_lo);
     prefetch_tmap(&tb_hi);
     prefetch_tmap(&tb_lo);
-    const int nba = gemm_nbox<GM_BM, A_MN>(m0, args.M), nbb = gemm_nbox<BN, B_MN>(n0, args.N);
-    // bytes landing per stage: hi + lo of every issued box (32 x 32 fp32 = 4 KB)
-    const uint32_t tx = 2u * 4096u * uint32_t(nba + nbb);
-    int issued = 0;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % NST;
-      if (i >= NST && !mbar_wait<true>(&empty[s], uint32_t((i / NST) - 1) & 1u, abort_flag, status)) break;
-      unsigned char* st = smb + s * Cfg::STAGE_B;
-      mbar_arrive_expect_tx(&full[s], tx);
-      const int k0 = (kb0 + i) * GM_BK;
-      gemm_load_operand<GM_BM, A_MN>(st, st + Cfg::OFF_ALO, &ta_hi, &ta_lo, &full[s], m0, k0, nba);
-      gemm_load_operand<BN, B_MN>(st + Cfg::OFF_BHI, st + Cfg::OFF_BLO, &tb_hi, &tb_lo, &full[s], n0, k0, nbb);
-      issued = i + 1;
+    int g = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
+      const GemmItem it = gemm_item(args, w, BN, tiles_n);
+      const int nba = gemm_nbox<GM_BM, A_MN>(it.m0, args.M), nbb = gemm_nbox<BN, B_MN>(it.n0, args.N);
+      // bytes landing per stage: hi + lo of every issued box (32 x 32 fp32 = 4 KB)
+      const uint32_t tx = 2u * 4096u * uint32_t(nba + nbb);
+      for (int i = 0; i < it.nkb; ++i, ++g) {
+        const int s = g % NST;
+        if (g >= NST && !mbar_wait<true>(&empty[s], uint32_t((g / NST) - 1) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        unsigned char* st = smb + s * Cfg::STAGE_B;
+        mbar_arrive_expect_tx(&full[s], tx);
+        const int k0 = (it.kb0 + i) * GM_BK;
+        gemm_load_operand<GM_BM, A_MN>(st, st + Cfg::OFF_ALO, &ta_hi, &ta_lo, &full[s], it.m0, k0, nba);
+        gemm_load_operand<BN, B_MN>(st + Cfg::OFF_BHI, st + Cfg::OFF_BLO, &tb_hi, &tb_lo, &full[s], it.n0, k0,
+                                    nbb);
+      }
     }
     // Drain: the last load of every stage has landed before the CTA may exit
     // (on the normal path the MMA warp consumed them all already).
-    for (int i = max(0, issued - NST); i < issued; ++i)
+    for (int i = max(0, g - NST); i < g; ++i)
       (void)mbar_wait<true>(&full[i % NST], uint32_t(i / NST) & 1u, abort_flag, status);
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN);
-    const uint32_t d_small = tmem_base + col_small;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % NST, b = i & 1;
-      // buffer b last held k-block i - 2: wait until the epilogue has read it
-      if (i >= 2 && !mbar_wait(&acce[b], uint32_t((i >> 1) - 1) & 1u, abort_flag, status)) break;
-      if (!mbar_wait(&full[s], uint32_t(i / NST) & 1u, abort_flag, status)) break;
-      tmem_fence_after_sync();
-      const uint32_t st = smem_u32(smb + s * Cfg::STAGE_B);
-      const uint32_t d_big = tmem_base + uint32_t(b * BN);
+    int g = 0, j = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
+      const GemmItem it = gemm_item(args, w, BN, tiles_n);
+      const int c = j & 1;
+      // correction buffer c last held item j - 2: wait until the epilogue read it
+      if (j >= 2 && !mbar_wait(&sme[c], uint32_t((j >> 1) - 1) & 1u, abort_flag, status)) break;
+      const uint32_t d_small = tmem_base + uint32_t((2 + c) * BN);
+      for (int i = 0; i < it.nkb; ++i, ++g) {
+        const int s = g % NST, b = g & 1;
+        // buffer b last held k-block g - 2: wait until the epilogue has read it
+        if (g >= 2 && !mbar_wait(&acce[b], uint32_t((g >> 1) - 1) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&full[s], uint32_t(g / NST) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tmem_fence_after_sync();
+        const uint32_t st = smem_u32(smb + s * Cfg::STAGE_B);
+        const uint32_t d_big = tmem_base + uint32_t(b * BN);
 #pragma unroll
-      for (int kk = 0; kk < GM_BK / 8; ++kk) {
-        const uint64_t ahi = gemm_desc<A_MN>(st, kk), alo = gemm_desc<A_MN>(st + Cfg::OFF_ALO, kk);
-        const uint64_t bhi = gemm_desc<B_MN>(st + Cfg::OFF_BHI, kk), blo = gemm_desc<B_MN>(st + Cfg::OFF_BLO, kk);
-        umma_tf32(d_big, ahi, bhi, idesc, kk > 0 ? 1u : 0u);
-        umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_tf32(d_small, alo, bhi, idesc, 1u);
+        for (int kk = 0; kk < GM_BK / 8; ++kk) {
+          const uint64_t ahi = gemm_desc<A_MN>(st, kk), alo = gemm_desc<A_MN>(st + Cfg::OFF_ALO, kk);
+          const uint64_t bhi = gemm_desc<B_MN>(st + Cfg::OFF_BHI, kk), blo = gemm_desc<B_MN>(st + Cfg::OFF_BLO, kk);
+          umma_tf32(d_big, ahi, bhi, idesc, kk > 0 ? 1u : 0u);
+          umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_tf32(d_small, alo, bhi, idesc, 1u);
+        }
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        umma_commit(&accf[b]);   // and buffer b holds this k-block's large products
       }
-      umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
-      umma_commit(&accf[b]);   // and buffer b holds this k-block's large products
     }
   } else if (warp >= GM_EPI_WARP0) {
-    // ---- epilogue: per k-block TMEM -> fp32 registers, then the tile -> global ----
-    const int q = warp - GM_EPI_WARP0;  // TMEM lane quarter
-    const int row = m0 + 32 * q + lane;
-    const uint32_t lane_addr = tmem_base + (uint32_t(32 * q) << 16);
-    float acc[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-    bool ok = true;
-    for (int i = 0; i < nkb; ++i) {
-      const int b = i & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], uint32_t(i >> 1) & 1u, abort_flag, status));
-      if (!ok) break;
-      tmem_fence_after_sync();
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(lane_addr + uint32_t(b * BN + c), r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c + j] += __uint_as_float(r[j]);
-      }
-      tmem_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[b]);
-    }
-    ok = ok && nkb > 0;
-    float* out = args.C + int64_t(blockIdx.z) * args.split_stride + int64_t(row) * args.ldc;
-    const bool row_ok = ok && row < args.M;
+    // ---- epilogue: per k-block TMEM -> fp32 registers, per item the tile -> global ----
+    const int q = warp & 3;                          // TMEM lane quarter
+    const int h = (warp - GM_EPI_WARP0) >> 2;        // column half
+    const uint32_t lane_addr = tmem_base + (uint32_t(32 * q) << 16) + uint32_t(h * HC);
     const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0) &&
                      (args.split_stride % 4 == 0);
-    // the last k-block's commit also covered every correction-product MMA
+    int g = 0, j = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
+      const GemmItem it = gemm_item(args, w, BN, tiles_n);
+      float acc[HC];
 #pragma unroll
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(lane_addr + col_small + uint32_t(c), r);
-      tmem_wait_ld();
-      if (!row_ok) continue;
-      const int col0 = n0 + c;
-      if (vec && col0 + 32 <= args.N) {
+      for (int x = 0; x < HC; ++x) acc[x] = 0.f;
+      for (int i = 0; i < it.nkb; ++i, ++g) {
+        const int b = g & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], uint32_t(g >> 1) & 1u, abort_flag, status));
+        if (!ok) break;
+        tmem_fence_after_sync();
+        uint32_t r[HC];
+        tmem_load_cols<HC>(lane_addr + uint32_t(b * BN), r);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
+        for (int x = 0; x < HC; ++x) acc[x] += __uint_as_float(r[x]);
+        tmem_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[b]);
+      }
+      if (!ok || it.nkb == 0) break;
+      // the item's last k-block commit also covered all of its correction-product MMAs
+      const int c = j & 1;
+      uint32_t r[HC];
+      tmem_load_cols<HC>(lane_addr + uint32_t((2 + c) * BN), r);
+      tmem_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sme[c]);
+      const int row = it.m0 + 32 * q + lane;
+      if (row >= args.M) continue;
+      float* out = args.C + int64_t(it.split) * args.split_stride + int64_t(row) * args.ldc;
+      const int col0 = it.n0 + h * HC;
+      if (vec && col0 + HC <= args.N) {
+#pragma unroll
+        for (int x = 0; x < HC; x += 4) {
           float4 v;
-          v.x = acc[c + j] + __uint_as_float(r[j]);
-          v.y = acc[c + j + 1] + __uint_as_float(r[j + 1]);
-          v.z = acc[c + j + 2] + __uint_as_float(r[j + 2]);
-          v.w = acc[c + j + 3] + __uint_as_float(r[j + 3]);
-          float4* dst = reinterpret_cast<float4*>(out + col0 + j);
+          v.x = acc[x] + __uint_as_float(r[x]);
+          v.y = acc[x + 1] + __uint_as_float(r[x + 1]);
+          v.z = acc[x + 2] + __uint_as_float(r[x + 2]);
+          v.w = acc[x + 3] + __uint_as_float(r[x + 3]);
+          float4* dst = reinterpret_cast<float4*>(out + col0 + x);
           if (args.accumulate) {
             const float4 o = *dst;
             v.x += o.x;
@@ -343,10 +422,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (col0 + j < args.N) {
-            const float v = acc[c + j] + __uint_as_float(r[j]);
-            out[col0 + j] = args.accumulate ? out[col0 + j] + v : v;
+        for (int x = 0; x < HC; ++x)
+          if (col0 + x < args.N) {
+            const float v = acc[x] + __uint_as_float(r[x]);
+            out[col0 + x] = args.accumulate ? out[col0 + x] + v : v;
           }
       }
     }
