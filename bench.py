@@ -401,6 +401,9 @@ def main():
                     help="only time the dt_proj + softplus kernels (forward, VJP) at the model's block shape")
     ap.add_argument("--model-profile", action="store_true",
                     help="print the per-kernel device-time table of one VisionMamba-2D training step and exit")
+    ap.add_argument("--model-batch", type=int,
+                    help="with --model-profile, or alone: images per VisionMamba-2D step on one GPU (e.g. 8 = one "
+                         "GPU's share of the 8-GPU run); alone it prints only the model line")
     ap.add_argument("--gemm", action="store_true",
                     help="only time the tensor-core projection GEMMs at the VisionMamba-2D shapes against "
                          "PyTorch's fp32 GEMM")
@@ -421,7 +424,14 @@ def main():
             sys.exit(launch_only_gemm(args.launch_only, args.launch_gemm))
         sys.exit(launch_only(args.launch_only, args.io == "bf16"))
     if args.model_profile:
-        profile_model(args.warmup)
+        profile_model(args.warmup, args.model_batch)
+        return
+    if args.model_batch:
+        import torch
+
+        line = run_model(torch.device("cuda", 0), 0, 1, steps=20, warmup=max(args.warmup, 3),
+                         barrier=lambda: None, graphed=not args.model_eager, batch=args.model_batch)
+        print(json.dumps({"vision_mamba_2d_train_batch": line}), flush=True)
         return
     if args.sweep:
         run_sweep(max(args.steps, 20), max(args.warmup, 3), bf16=args.io == "bf16")
@@ -612,14 +622,16 @@ def main():
         dist.destroy_process_group()
 
 
-def run_model(dev, rank, world, steps, warmup, barrier, graphed=True, single=False):
+def run_model(dev, rank, world, steps, warmup, barrier, graphed=True, single=False, batch=None):
     """VisionMamba-2D (K=4, 224x224x1, patch 16, E 384, depth 6) training steps:
     forward, MSE, backward (DDP all-reduce over NCCL when world > 1), AdamW.
     Global batch 64 split over the ranks (strong scaling), fp32 (TF32 off).
     `graphed`: the whole step is one CUDA graph replay (train.GraphedTrainStep).
     `single`: this rank alone trains on the whole global batch (the 1-GPU
     point of the strong-scaling curve, measured inside a multi-GPU job; no
-    DDP, no collective, no barrier)."""
+    DDP, no collective, no barrier).  `batch` (single GPU only): images per
+    step instead of the global batch, e.g. 8 to time one GPU's share of the
+    8-GPU step without the all-reduce; img/s then counts those images."""
     import torch
     import torch.distributed as dist
 
@@ -631,6 +643,9 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True, single=Fal
     if single:
         rank, world, barrier = 0, 1, (lambda: None)
     a, b = train.shard(cfg.global_batch, rank, world)
+    if batch is not None:
+        assert world == 1 or single, "batch overrides apply to single-GPU runs"
+        a, b = 0, int(batch)
     wrap = (lambda m: m) if single else (lambda m: train.wrap_data_parallel(m, dev))
     side = torch.cuda.Stream(dev)
     if graphed:
@@ -670,8 +685,9 @@ def run_model(dev, rank, world, steps, warmup, barrier, graphed=True, single=Fal
     n_params = sum(p.numel() for p in model.parameters())
     del model, opt
     torch.cuda.empty_cache()
-    return {"img_per_s": cfg.global_batch * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
-            "warmup": warmup, "global_batch": cfg.global_batch, "per_gpu_batch": b - a, "scaling": "strong",
+    imgs = cfg.global_batch if batch is None else b - a
+    return {"img_per_s": imgs * steps / (ms / 1e3), "ms_per_step": ms / steps, "steps": steps,
+            "warmup": warmup, "global_batch": imgs, "per_gpu_batch": b - a, "scaling": "strong",
             "dtype": "f32 (TF32 off)", "params": n_params, "loss": loss,
             "execution": "one CUDA graph per step (forward, backward, all-reduce, AdamW)" if graphed else "eager",
             "parallelism": f"DDP NCCL all-reduce x{world}" if world > 1 else "single GPU",
@@ -780,7 +796,7 @@ def time_conv(dev, iters=20):
 
         def fwd():
             rc = lib.vmscan_conv1d_silu_fwd(b, l, c, k, x.data_ptr(), S, w.data_ptr(), bias.data_ptr(),
-                                            out.data_ptr(), S, dref, sp)
+                                            out.data_ptr(), S, None, None, dref, sp)
             assert rc == 0, rc
 
         def bwd():
@@ -842,7 +858,7 @@ def time_dt(dev, iters=20):
 
     def bwd():
         assert lib.vmscan_dt_softplus_bwd(ntok, r, dn, xw.data_ptr(), wide, w.data_ptr(), bias.data_ptr(),
-                                          gin.data_ptr(), dn, out.data_ptr(), dn, part.data_ptr(), sp) == 0
+                                          gin.data_ptr(), dn, out.data_ptr(), dn, None, part.data_ptr(), sp) == 0
 
     res = {"shape": f"{ntok} tokens, dt_rank {r}, d_inner {dn}", "api": "vmscan_dt_softplus_fwd / _bwd"}
     for name, fn, byt in (("fwd", fwd, 4 * ntok * dn), ("bwd", bwd, 8 * ntok * dn)):
@@ -983,10 +999,12 @@ def run_sweep(iters, warmup, bf16=False):
               f"{100 * r['fwd_frac']:.1f} | {r['bwd_ms']:.4f} | {r['bwd_gbs']:.0f} | {100 * r['bwd_frac']:.1f} |")
 
 
-def profile_model(warmup):
+def profile_model(warmup, batch=None):
     """Device time per kernel of one VisionMamba-2D training step (1 GPU,
     torch.profiler over 2 steps after `warmup` steps), grouped as in the
-    committed model-step summary; prints a table, not a bench line."""
+    committed model-step summary; prints a table, not a bench line.  `batch`
+    (default: the global batch of 64) sets the images per step, e.g. 8 for
+    one GPU's share of the 8-GPU run."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
@@ -998,7 +1016,7 @@ def profile_model(warmup):
     cfg = train.VISION_MAMBA_2D
     model = train.build_encoder(cfg, dev, seed=0)
     opt = train.make_optimizer(model)
-    x, tgt = train.synthetic_batch(cfg, cfg.global_batch, dev, seed=100)
+    x, tgt = train.synthetic_batch(cfg, batch or cfg.global_batch, dev, seed=100)
     for _ in range(max(warmup, 1)):
         train.train_step(model, opt, x, tgt)
     torch.cuda.synchronize()
@@ -1053,6 +1071,9 @@ def run_encoder(dev, rank, world, which, mode, steps, warmup, barrier):
     side = torch.cuda.Stream(dev)
     if mode == "dp":
         a, b = train.shard(cfg.global_batch, rank, world)
+    if batch is not None:
+        assert world == 1 or single, "batch overrides apply to single-GPU runs"
+        a, b = 0, int(batch)
         with torch.cuda.stream(side):
             model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
         batch, seed = b - a, 100 + rank

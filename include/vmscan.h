@@ -268,11 +268,15 @@ int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d
  * weight uses MLX's Conv1d layout (channels, K, 1).  Replaces
  * `silu(conv1d(x)[:, :L])`, mamba_block.py:129-132,170-171, on the permuted
  * sequence of mamba_block.py:443-534.  K in 1..8; channels % 4 == 0.
+ * out_hi / out_lo (both or neither; 16-byte aligned, laid out like out)
+ * also receive the TF32 hi / lo parts of out that vmscan_gemm_tf32x3 reads
+ * (the x_proj GEMM's operand), so no separate vmscan_tf32_split pass is needed.
  */
 int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize,
                            const float* x, vmscan_strides sx,
                            const float* weight, const float* bias,
                            float* out, vmscan_strides sout,
+                           float* out_hi, float* out_lo,
                            const vmscan_direction* dir,
                            vmscan_stream_t stream);
 
@@ -308,16 +312,19 @@ int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
  * Softplus part of the VJP of vmscan_dt_softplus_fwd: dpre = ddelta *
  * sigmoid(pre) with pre recomputed from x, weight, bias (the gradient the
  * reference's autograd forms through log(1 + exp(.))).  dx = dpre weight and
- * dweight = dpre^T x are left to the caller (plain GEMMs).  When dbias_part
- * is not NULL it receives, as vmscan_dt_softplus_bias_rows(ntok) x d_inner
- * contiguous floats, the column sums of dpre over consecutive groups of
- * tokens; dbias is the sum of its rows (a small reduction for the caller).
+ * dweight = dpre^T x are left to the caller (GEMMs).  When dpre_lo is not
+ * NULL, dpre receives the TF32 hi part of dpre and dpre_lo (same row stride)
+ * the lo part, the operand form of vmscan_gemm_tf32x3, instead of dpre
+ * itself.  When dbias_part is not NULL it receives, as
+ * vmscan_dt_softplus_bias_rows(ntok) x d_inner contiguous floats, the column
+ * sums of dpre (fp32) over consecutive groups of tokens; dbias is the sum of
+ * its rows (a small reduction for the caller).
  */
 int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
                            const float* x, int64_t ldx,
                            const float* weight, const float* bias,
                            const float* ddelta, int64_t ld_ddelta,
-                           float* dpre, int64_t ld_dpre,
+                           float* dpre, int64_t ld_dpre, float* dpre_lo,
                            float* dbias_part,
                            vmscan_stream_t stream);
 

@@ -102,14 +102,14 @@ SIGNATURES = {
             _D, _p,
         ],
     ),
-    "vmscan_conv1d_silu_fwd": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _D, _p]),
+    "vmscan_conv1d_silu_fwd": (ctypes.c_int, [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _p, _p, _D, _p]),
     "vmscan_conv1d_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vmscan_conv1d_silu_bwd": (
         ctypes.c_int,
         [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _p, _S, _p, _p, _D, _p, _sz, _p],
     ),
     "vmscan_dt_softplus_fwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p]),
-    "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p]),
+    "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p]),
     "vmscan_dt_softplus_bias_rows": (_i64, [_i64]),
     "vmscan_tf32_split": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
     "vmscan_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),

@@ -34,6 +34,7 @@ import torch
 
 from . import _native
 from .direction import ScanDirection
+from .linear import gemm_tf32x3, tf32_split
 from .scan import _dir_ptr, _empty_seq, _prepare, _ptr, _strides, _tma_compatible
 
 D_STATE = 16
@@ -60,6 +61,13 @@ def _mm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return a.t() @ b
 
 
+def _tc_rows(dt_rank: int, d_inner: int) -> bool:
+    """x_proj / dt_proj GEMMs run on the tensor cores when every row they read
+    or write (dt_rank, dt_rank + 32, d_inner floats) is a whole number of
+    16-byte units, as the GEMM's tensor maps need."""
+    return dt_rank % 4 == 0 and d_inner % 4 == 0
+
+
 def _stream_ptr(s: torch.cuda.Stream) -> ctypes.c_void_p:
     return ctypes.c_void_p(s.cuda_stream)
 
@@ -79,6 +87,7 @@ class _BranchesFn(torch.autograd.Function):
         b, l, _ = xz.shape
         dev = xz.device
         wide = r + 2 * n
+        tc = _tc_rows(r, dn)
         cur = torch.cuda.current_stream(dev)
         y_all = _empty_seq(b, l, kb * dn, dev)
         need_grad = any(ctx.needs_input_grad)
@@ -97,9 +106,16 @@ class _BranchesFn(torch.autograd.Function):
                 cw = conv_w.detach().contiguous()
                 cb = conv_b.detach().contiguous()
                 xc = _empty_seq(b, l, dn, dev)
+                # with the tensor-core x_proj the conv also writes xc's TF32 parts (its GEMM operand)
+                xc_s = (_empty_seq(b, l, dn, dev), _empty_seq(b, l, dn, dev)) if tc else (None, None)
                 _native.check(lib.vmscan_conv1d_silu_fwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
-                                                         _ptr(xc), _strides(xc), dptr, sp), "vmscan_conv1d_silu_fwd")
-                xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
+                                                         _ptr(xc), _strides(xc), _ptr(xc_s[0]), _ptr(xc_s[1]), dptr,
+                                                         sp), "vmscan_conv1d_silu_fwd")
+                if tc:
+                    xc_s = (xc_s[0].view(b * l, dn), xc_s[1].view(b * l, dn))
+                    xdbc = gemm_tf32x3(xc_s, False, tf32_split(xproj_w.detach().contiguous()), False, b * l, wide, dn)
+                else:
+                    xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
                 dw_ = dt_w.detach().contiguous()
                 db_ = dt_b.detach().contiguous()
                 delta = _empty_seq(b, l, dn, dev)
@@ -124,7 +140,7 @@ class _BranchesFn(torch.autograd.Function):
                                              _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
                                              _ptr(dsk), _ptr(z), _strides(z), _ptr(y), _strides(y), _ptr(ckpt), dptr,
                                              _ptr(fws), int(fws_n), sp), "vmscan_fwd")
-                saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt))
+                saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s))
         for s in streams[:kb]:
             cur.wait_stream(s)
         if need_grad:
@@ -144,11 +160,12 @@ class _BranchesFn(torch.autograd.Function):
         b, l, _ = ctx.xz_shape
         dev = dy_all.device
         wide = r + 2 * n
+        tc = _tc_rows(r, dn)
         cur = torch.cuda.current_stream(dev)
         dxz = _empty_seq(b, l, kb * 2 * dn, dev)
         grads: List[Optional[torch.Tensor]] = [None] * (PARAMS_PER_BLOCK * kb)
         for k in range(kb):
-            x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt = ctx.saved[k]
+            x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s = ctx.saved[k]
             xproj_w = ctx.xproj[k].detach()
             s = streams[k]
             s.wait_stream(cur)
@@ -174,20 +191,36 @@ class _BranchesFn(torch.autograd.Function):
                                              _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta), _ptr(dA),
                                              _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD), _ptr(dz),
                                              _strides(dz), dptr, _ptr(ws), ws.numel(), sp), "vmscan_bwd")
-                # dt_proj + softplus: dpre, then its GEMMs; dbias from the kernel's partial sums
+                # dt_proj + softplus: dpre (for the tensor cores: its TF32 parts), then its
+                # GEMMs; dbias from the kernel's partial sums
+                t = b * l
                 dpre = _empty_seq(b, l, dn, dev)
-                part = torch.empty((lib.vmscan_dt_softplus_bias_rows(b * l), dn), dtype=torch.float32, device=dev)
-                _native.check(lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
+                dpre_lo = _empty_seq(b, l, dn, dev) if tc else None
+                part = torch.empty((lib.vmscan_dt_softplus_bias_rows(t), dn), dtype=torch.float32, device=dev)
+                _native.check(lib.vmscan_dt_softplus_bwd(t, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
                                                          _ptr(ddelta), ddelta.stride(1), _ptr(dpre), dpre.stride(1),
-                                                         _ptr(part), sp), "vmscan_dt_softplus_bwd")
-                dpre2 = dpre.reshape(b * l, dn)
-                dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
-                g_dt_w = _mm_tn(dpre2, xdbc[:, :r])
+                                                         _ptr(dpre_lo), _ptr(part), sp), "vmscan_dt_softplus_bwd")
                 g_dt_b = part.sum(0)
-                # x_proj: its input gradient lands on du in place (du += dx_dbc W)
-                du2 = du.view(b * l, dn)
-                du2.addmm_(dxdbc, xproj_w)
-                g_xproj = _mm_tn(dxdbc, xc.reshape(b * l, dn))
+                du2 = du.view(t, dn)
+                if tc:
+                    dpre_s = (dpre.view(t, dn), dpre_lo.view(t, dn))
+                    xdbc_s = tf32_split(xdbc)
+                    # dt_proj input gradient straight into its slice of dx_dbc: dpre W_dt
+                    gemm_tf32x3(dpre_s, False, tf32_split(dw_), True, t, r, dn, out=dxdbc[:, :r])
+                    # dt_proj weight gradient dpre^T x_dbc[:, :r] (both read MN-major)
+                    g_dt_w = gemm_tf32x3(dpre_s, True, (xdbc_s[0][:, :r], xdbc_s[1][:, :r]), True, dn, r, t)
+                    # x_proj: its input gradient lands on du in place (du += dx_dbc W_x)
+                    dxdbc_s = tf32_split(dxdbc)
+                    gemm_tf32x3(dxdbc_s, False, tf32_split(xproj_w.contiguous()), True, t, dn, wide, out=du2,
+                                accumulate=True)
+                    g_xproj = gemm_tf32x3(dxdbc_s, True, xc_s, True, wide, dn, t)
+                else:
+                    dpre2 = dpre.reshape(t, dn)
+                    dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
+                    g_dt_w = _mm_tn(dpre2, xdbc[:, :r])
+                    # x_proj: its input gradient lands on du in place (du += dx_dbc W)
+                    du2.addmm_(dxdbc, xproj_w)
+                    g_xproj = _mm_tn(dxdbc, xc.reshape(t, dn))
                 # conv1d + SiLU: dx straight into its slice of dxz
                 dx = dxz[:, :, 2 * dn * k:2 * dn * k + dn]
                 g_cw = torch.empty_like(cw)

@@ -568,7 +568,7 @@ namespace {
 template <bool BWD>
 int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
                        const float* weight, const float* bias, const float* gin, int64_t ldg, float* out,
-                       int64_t ldo, float* bpart, vmscan_stream_t stream) {
+                       int64_t ldo, float* out_lo, float* bpart, vmscan_stream_t stream) {
   if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr || (BWD && gin == nullptr))
     return VMSCAN_ERR_NULL;
   if (ntok <= 0 || d_inner <= 0 || d_inner > INT32_MAX || dt_rank < 1 || dt_rank > DTP_RMAX)
@@ -585,7 +585,7 @@ int launch_dt_softplus(int64_t ntok, int64_t dt_rank, int64_t d_inner, const flo
 #define VM_DTP(RP)                                                                                           \
   dt_softplus_kernel<RP, BWD>                                                                                \
       <<<dim3(unsigned((d_inner + DTP_THREADS * dtp_channels(RP) - 1) / (DTP_THREADS * dtp_channels(RP))), ty), \
-         DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, bpart, ntok, D)
+         DTP_THREADS, 0, s>>>(x, ldx, R, weight, bias, gin, ldg, out, ldo, out_lo, bpart, ntok, D)
   if (R <= 8)
     VM_DTP(8);
   else if (R <= 16)
@@ -636,7 +636,8 @@ int encode_gemm_map(CUtensorMap* m, const char* what, const float* p, int64_t co
 }
 
 // K splits of a GEMM: 1 while the output tiles fill the SMs, otherwise enough
-// splits to fill them with at least 8 k-blocks each (at most 8 splits).
+// splits to fill them with at least 4 k-blocks each (at most 32 splits; the
+// skinny weight gradients have a handful of tiles and K of 10^4).
 struct GemmPlan {
   int bn, tiles_n, tiles_m, splits, kb_per_split;
   size_t ws_bytes;
@@ -651,7 +652,7 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   const int64_t tiles = int64_t(p.tiles_n) * p.tiles_m;
   const int sms = sm_count();
   int s = 1;
-  if (tiles < sms) s = int(std::min<int64_t>({int64_t(sms) / tiles, int64_t(nkb / 8), 8}));
+  if (tiles < sms) s = int(std::min<int64_t>({int64_t(sms) / tiles, int64_t(nkb / 4), 32}));
   s = std::max(s, 1);
   p.kb_per_split = (nkb + s - 1) / s;
   p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // no empty split
@@ -805,7 +806,7 @@ int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const
                            const float* weight, const float* bias, float* delta, int64_t ld_delta,
                            vmscan_stream_t stream) {
   return launch_dt_softplus<false>(ntok, dt_rank, d_inner, x, ldx, weight, bias, nullptr, 0, delta, ld_delta,
-                                   nullptr, stream);
+                                   nullptr, nullptr, stream);
 }
 
 int64_t vmscan_dt_softplus_bias_rows(int64_t ntok) {
@@ -815,15 +816,18 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok) {
 
 int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
                            const float* weight, const float* bias, const float* ddelta, int64_t ld_ddelta,
-                           float* dpre, int64_t ld_dpre, float* dbias_part, vmscan_stream_t stream) {
+                           float* dpre, int64_t ld_dpre, float* dpre_lo, float* dbias_part, vmscan_stream_t stream) {
   return launch_dt_softplus<true>(ntok, dt_rank, d_inner, x, ldx, weight, bias, ddelta, ld_ddelta, dpre, ld_dpre,
-                                  dbias_part, stream);
+                                  dpre_lo, dbias_part, stream);
 }
 
 int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,
                            vmscan_strides sx, const float* weight, const float* bias, float* out,
-                           vmscan_strides sout, const vmscan_direction* dir, vmscan_stream_t stream) {
+                           vmscan_strides sout, float* out_hi, float* out_lo, const vmscan_direction* dir,
+                           vmscan_stream_t stream) {
   if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr) return VMSCAN_ERR_NULL;
+  if ((out_hi == nullptr) != (out_lo == nullptr)) return VMSCAN_ERR_NULL;
+  if (out_hi != nullptr && (!aligned16(out_hi) || !aligned16(out_lo))) return VMSCAN_ERR_ALIGN;
   if (ksize < 1 || ksize > CONV_KMAX || channels % 4 != 0) return VMSCAN_ERR_CONV;
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, channels, dir, g));
@@ -836,10 +840,10 @@ int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (ksize <= 4)
     conv_silu_fwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
-                                                         sout.seq, int(channels), int(ksize), g);
+                                                         sout.seq, out_hi, out_lo, int(channels), int(ksize), g);
   else
     conv_silu_fwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
-                                                         sout.seq, int(channels), int(ksize), g);
+                                                         sout.seq, out_hi, out_lo, int(channels), int(ksize), g);
   return check_launch();
 }
 

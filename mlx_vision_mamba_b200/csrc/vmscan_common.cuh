@@ -321,6 +321,25 @@ __device__ __forceinline__ void two_sum1(float& acc, float& x) {
   x = err;
 }
 
+// TF32 hi / lo parts of an fp32 value for the tensor-core GEMM: hi = x
+// rounded to 11 significant bits (to nearest, ties away from zero: add half a
+// TF32 unit to the magnitude bits, clear the 13 low bits), lo = (x - hi)
+// rounded the same way (x - hi is exact).  Integer ALU only, so producers can
+// emit the parts beside their fp32 output without loading the exp unit.
+__device__ __forceinline__ float tf32_round(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = tf32_round(x);
+  lo = tf32_round(x - hi);
+}
+__device__ __forceinline__ void split_tf32_4(const float4& x, float4& hi, float4& lo) {
+  split_tf32(x.x, hi.x, lo.x);
+  split_tf32(x.y, hi.y, lo.y);
+  split_tf32(x.z, hi.z, lo.z);
+  split_tf32(x.w, hi.w, lo.w);
+}
+
 __device__ __forceinline__ float2 shfl_xor2(float2 v, int m) {
   return make_float2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }

@@ -50,8 +50,8 @@ __device__ __forceinline__ float dsilu_f(float pre) {
 template <int KW>
 __global__ void __launch_bounds__(CONV_THREADS)
     conv_silu_fwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
-                         const float* __restrict__ bias, float* __restrict__ out, int64_t sob, int64_t sos, int C,
-                         int K, const ScanGeom g) {
+                         const float* __restrict__ bias, float* __restrict__ out, int64_t sob, int64_t sos,
+                         float* __restrict__ out_hi, float* __restrict__ out_lo, int C, int K, const ScanGeom g) {
   __shared__ int64_t tok[CONV_CHUNK + CONV_KMAX];
   const int p0 = blockIdx.y * CONV_CHUNK;
   const int b = blockIdx.z;
@@ -107,6 +107,14 @@ __global__ void __launch_bounds__(CONV_THREADS)
           o.z = silu_f(acc.z);
           o.w = silu_f(acc.w);
           *reinterpret_cast<float4*>(ob + tk * sos) = o;
+          if (out_hi != nullptr) {
+            // TF32 parts for the x_proj GEMM, same layout as out
+            float4 hi, lo;
+            split_tf32_4(o, hi, lo);
+            const int64_t off = b * sob + c4 * 4 + tk * sos;
+            *reinterpret_cast<float4*>(out_hi + off) = hi;
+            *reinterpret_cast<float4*>(out_lo + off) = lo;
+          }
         }
       }
     }

@@ -44,7 +44,8 @@ __device__ __forceinline__ float softplus_ref(float v) { return __logf(1.0f + __
 constexpr int DTP_XROW = DTP_TOKENS + 4;
 
 // RP: dt_rank rounded up to a multiple of 4 (<= DTP_RMAX).  BWD: write
-// dpre = gin * sigmoid(pre) instead of softplus(pre), and when bpart is given
+// dpre = gin * sigmoid(pre) instead of softplus(pre) (as its TF32 hi part in
+// out and lo part in out_lo when out_lo is given), and when bpart is given
 // the sum of dpre over the CTA's tokens per channel into row blockIdx.y of
 // bpart (the dbias partials; summed over rows by the caller).  A CTA covers
 // DTP_THREADS * dtp_channels(RP) channels x DTP_TOKENS tokens.
@@ -52,7 +53,8 @@ template <int RP, bool BWD>
 __global__ void __launch_bounds__(DTP_THREADS)
     dt_softplus_kernel(const float* __restrict__ x, int64_t ldx, int R, const float* __restrict__ W,
                        const float* __restrict__ bias, const float* __restrict__ gin, int64_t ldg,
-                       float* __restrict__ out, int64_t ldo, float* __restrict__ bpart, int64_t ntok, int Dn) {
+                       float* __restrict__ out, int64_t ldo, float* __restrict__ out_lo, float* __restrict__ bpart,
+                       int64_t ntok, int Dn) {
   constexpr int CH = dtp_channels(RP);
   // xs[r][t]: x of token t0 + t at rank index r (transposed, so one 128-bit
   // load gives 4 tokens' values of one r for the packed FMAs below)
@@ -127,7 +129,15 @@ __global__ void __launch_bounds__(DTP_THREADS)
           if (BWD) {
             const float sig = __fdividef(1.0f, 1.0f + __expf(-pre[u]));
             const float dp = g[c][u] * sig;
-            out[tt * ldo + dch[c]] = dp;
+            if (out_lo != nullptr) {
+              // the TF32 parts of dpre for its two GEMMs instead of dpre itself
+              float hi, lo;
+              split_tf32(dp, hi, lo);
+              out[tt * ldo + dch[c]] = hi;
+              out_lo[tt * ldo + dch[c]] = lo;
+            } else {
+              out[tt * ldo + dch[c]] = dp;
+            }
             bsum[c] += dp;
           } else {
             out[tt * ldo + dch[c]] = softplus_ref(pre[u]);

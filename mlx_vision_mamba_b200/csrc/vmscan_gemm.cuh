@@ -3,14 +3,16 @@
 // (mlx_vision_mamba/mamba_block.py:165,191 and the direction sum :562-566).
 //
 // Precision.  TF32 keeps 11 significant bits.  Each fp32 operand x is split
-// into hi = rna_tf32(x) and lo = rna_tf32(x - hi) (x - hi is exact), so x =
+// into hi = tf32(x) and lo = tf32(x - hi) (split_tf32: round to nearest,
+// ties away; x - hi is exact), so x =
 // hi + lo to about 2^-22 |x|, and
 //     C = A_hi B_hi + (A_hi B_lo + A_lo B_hi)
 // drops only A_lo B_lo (~2^-22 of a product).  The large products and the
 // two correction products accumulate in separate TMEM accumulators, summed
 // once in fp32 by the epilogue, so the rounding of the running sum acts on
 // the large products alone, as it does in an fp32 FFMA loop.  The split is a
-// separate elementwise pass (tf32_split_kernel) whose outputs the GEMM reads.
+// separate elementwise pass (tf32_split_kernel), or written by the kernel
+// that produces the operand, and the GEMM reads the two parts.
 //
 // Design.  A persistent CTA per SM walks the 128 x BN output tiles (and K
 // splits), 320 threads: warp 0 lane 0 issues the TMA loads of the hi / lo
@@ -35,6 +37,20 @@ constexpr int GM_THREADS = 320;
 constexpr int GM_EPI_WARP0 = 2;  // warps 2..9: two epilogue warps per TMEM lane quarter
 constexpr int GM_EPI_WARPS = 8;
 
+// Large-product TMEM buffers for narrower tiles (128-column tiles use two,
+// which with the two correction buffers fill TMEM), and k-blocks per
+// promotion chain.  Measured on B200 inside CUDA graphs at the VisionMamba-2D
+// shapes: chains of 2 k-blocks run the 128-column GEMMs 9-14 % faster than
+// chains of 1 (half the MMA / epilogue hand-overs) at a rounding bias of
+// about -1.4e-7 of the output RMS, still below PyTorch's fp32 GEMM's
+// random error; 4 narrow buffers instead of 2 change little.
+#ifndef VMSCAN_GEMM_NB_NARROW
+#define VMSCAN_GEMM_NB_NARROW 4
+#endif
+#ifndef VMSCAN_GEMM_PK
+#define VMSCAN_GEMM_PK 2
+#endif
+
 template <int BN>
 struct GemmCfg {
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN: 32, 64 or 128");
@@ -44,10 +60,15 @@ struct GemmCfg {
   static constexpr int STAGE_B = 2 * A_TILE_B + 2 * B_TILE_B;
   static constexpr int NST = (196 * 1024) / STAGE_B < 6 ? (196 * 1024) / STAGE_B : 6;
   static_assert(NST >= 2, "at least two stages");
-  // accumulators: two large-product buffers (columns 0, BN), two correction buffers (2 BN, 3 BN)
-  static constexpr uint32_t TMEM_COLS = 4 * BN <= 128 ? 128u : (4 * BN <= 256 ? 256u : 512u);
+  // accumulators: NB large-product buffers (columns 0 .. NB BN), two
+  // correction buffers after them
+  static constexpr int NB = BN == 128 ? 2 : VMSCAN_GEMM_NB_NARROW;
+  static constexpr int PK = VMSCAN_GEMM_PK;  // k-blocks whose large products share one buffer
+  static_assert((NB + 2) * BN <= 512, "accumulators fit in TMEM");
+  static constexpr uint32_t TMEM_COLS =
+      (NB + 2) * BN <= 128 ? 128u : ((NB + 2) * BN <= 256 ? 256u : 512u);
   static constexpr int OFF_BAR = NST * STAGE_B;
-  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 6) * 8 + 16 + 1024;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 2 * NB + 2) * 8 + 16 + 1024;
 };
 
 // ---- tcgen05 helpers ----
@@ -107,28 +128,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// fp32 -> tf32, round to nearest (ties away from zero), kept in an fp32 container.
-__device__ __forceinline__ float to_tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-// hi / lo split of n fp32 values (see the file comment).  n % 4 == 0 and
-// 16-byte aligned pointers take the vector path; the host guarantees both.
+// hi / lo split of n fp32 values (split_tf32, the same rounding the
+// producer kernels use when they emit the parts themselves).  The host
+// guarantees n % 4 == 0 and 16-byte aligned pointers.
 __global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
                                   int64_t n4) {
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
-    const float4 v = x[i];
     float4 h, l;
-    h.x = to_tf32_rna(v.x);
-    h.y = to_tf32_rna(v.y);
-    h.z = to_tf32_rna(v.z);
-    h.w = to_tf32_rna(v.w);
-    l.x = to_tf32_rna(v.x - h.x);
-    l.y = to_tf32_rna(v.y - h.y);
-    l.z = to_tf32_rna(v.z - h.z);
-    l.w = to_tf32_rna(v.w - h.w);
+    split_tf32_4(x[i], h, l);
     hi[i] = h;
     lo[i] = l;
   }
@@ -234,16 +241,17 @@ __device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int w, int bn, 
 }
 
 // Persistent GEMM: each CTA walks the work items blockIdx.x, + gridDim.x, ...
-// and every role keeps one running k-block count g over them, which drives
-// the stage ring (g % NST) and the large-product buffers (g & 1).
+// and every role keeps running counts over them: k-blocks g drive the stage
+// ring (g % NST), promotion chains cg (PK k-blocks of one item) the
+// large-product buffers (cg % NB).
 //
 // Accumulation.  The tensor core's fp32 accumulation rounds toward zero
 // (measured on B200: with exactly representable TF32 inputs the error of a
 // chain of n MMAs has a mean of about -1.3e-8 n of the output's RMS, growing
-// with n).  So the large products of each k-block go into a fresh TMEM
-// accumulator (two buffers, alternating) and the epilogue warps add every
-// k-block's result into fp32 registers (round to nearest) while the next
-// k-block runs; the correction products (2^-11 of the size) accumulate in one
+// with n).  So the large products of each chain of PK k-blocks go into a
+// fresh TMEM accumulator (NB buffers in turn) and the epilogue warps add
+// every chain's result into fp32 registers (round to nearest) while the next
+// chains run; the correction products (2^-11 of the size) accumulate in one
 // TMEM accumulator per work item (two, alternating between items, so that an
 // item's store overlaps the next item's MMAs).
 //
@@ -262,9 +270,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
   uint64_t* full = reinterpret_cast<uint64_t*>(smb + Cfg::OFF_BAR);
   uint64_t* empty = full + NST;
-  uint64_t* accf = empty + NST;  // [2]: k-block result ready in large-product buffer b
-  uint64_t* acce = accf + 2;     // [2]: large-product buffer b drained by the 8 epilogue warps
-  uint64_t* sme = acce + 2;      // [2]: correction buffer c drained by the 8 epilogue warps
+  constexpr int NB = Cfg::NB, PK = Cfg::PK;
+  uint64_t* accf = empty + NST;  // [NB]: a chain's large products ready in buffer b
+  uint64_t* acce = accf + NB;    // [NB]: large-product buffer b drained by the 8 epilogue warps
+  uint64_t* sme = acce + NB;     // [2]: correction buffer c drained by the 8 epilogue warps
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sme + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sme + 2) + 1;
 
@@ -278,11 +287,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], GM_EPI_WARPS);
-      mbar_init(&sme[b], GM_EPI_WARPS);
     }
+    for (int c = 0; c < 2; ++c) mbar_init(&sme[c], GM_EPI_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -329,18 +338,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN);
-    int g = 0, j = 0;
+    int g = 0, cg = 0, j = 0;  // k-blocks, promotion chains, items so far
     bool ok = true;
     for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
       const GemmItem it = gemm_item(args, w, BN, tiles_n);
       const int c = j & 1;
       // correction buffer c last held item j - 2: wait until the epilogue read it
       if (j >= 2 && !mbar_wait(&sme[c], uint32_t((j >> 1) - 1) & 1u, abort_flag, status)) break;
-      const uint32_t d_small = tmem_base + uint32_t((2 + c) * BN);
+      const uint32_t d_small = tmem_base + uint32_t((NB + c) * BN);
       for (int i = 0; i < it.nkb; ++i, ++g) {
-        const int s = g % NST, b = g & 1;
-        // buffer b last held k-block g - 2: wait until the epilogue has read it
-        if (g >= 2 && !mbar_wait(&acce[b], uint32_t((g >> 1) - 1) & 1u, abort_flag, status)) {
+        const int s = g % NST, b = cg % NB, ci = i % PK;
+        // a chain's first k-block: buffer b last held chain cg - NB; wait until the epilogue read it
+        if (ci == 0 && cg >= NB && !mbar_wait(&acce[b], uint32_t((cg / NB) - 1) & 1u, abort_flag, status)) {
           ok = false;
           break;
         }
@@ -355,12 +364,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int kk = 0; kk < GM_BK / 8; ++kk) {
           const uint64_t ahi = gemm_desc<A_MN>(st, kk), alo = gemm_desc<A_MN>(st + Cfg::OFF_ALO, kk);
           const uint64_t bhi = gemm_desc<B_MN>(st + Cfg::OFF_BHI, kk), blo = gemm_desc<B_MN>(st + Cfg::OFF_BLO, kk);
-          umma_tf32(d_big, ahi, bhi, idesc, kk > 0 ? 1u : 0u);
+          umma_tf32(d_big, ahi, bhi, idesc, (ci > 0 || kk > 0) ? 1u : 0u);
           umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
           umma_tf32(d_small, alo, bhi, idesc, 1u);
         }
         umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
-        umma_commit(&accf[b]);   // and buffer b holds this k-block's large products
+        if (ci == PK - 1 || i == it.nkb - 1) {
+          umma_commit(&accf[b]);  // buffer b holds this chain's large products
+          ++cg;
+        }
       }
     }
   } else if (warp >= GM_EPI_WARP0) {
@@ -370,16 +382,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const uint32_t lane_addr = tmem_base + (uint32_t(32 * q) << 16) + uint32_t(h * HC);
     const bool vec = (args.ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(args.C) & 15u) == 0) &&
                      (args.split_stride % 4 == 0);
-    int g = 0, j = 0;
+    int cg = 0, j = 0;  // promotion chains, items so far
     bool ok = true;
     for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
       const GemmItem it = gemm_item(args, w, BN, tiles_n);
       float acc[HC];
 #pragma unroll
       for (int x = 0; x < HC; ++x) acc[x] = 0.f;
-      for (int i = 0; i < it.nkb; ++i, ++g) {
-        const int b = g & 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], uint32_t(g >> 1) & 1u, abort_flag, status));
+      const int nch = (it.nkb + PK - 1) / PK;
+      for (int ch = 0; ch < nch; ++ch, ++cg) {
+        const int b = cg % NB;
+        ok = __all_sync(0xffffffffu, mbar_wait(&accf[b], uint32_t(cg / NB) & 1u, abort_flag, status));
         if (!ok) break;
         tmem_fence_after_sync();
         uint32_t r[HC];
@@ -391,10 +404,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         if (lane == 0) mbar_arrive(&acce[b]);
       }
       if (!ok || it.nkb == 0) break;
-      // the item's last k-block commit also covered all of its correction-product MMAs
+      // the item's last chain commit also covered all of its correction-product MMAs
       const int c = j & 1;
       uint32_t r[HC];
-      tmem_load_cols<HC>(lane_addr + uint32_t((2 + c) * BN), r);
+      tmem_load_cols<HC>(lane_addr + uint32_t((NB + c) * BN), r);
       tmem_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sme[c]);

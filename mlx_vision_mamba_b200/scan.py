@@ -281,7 +281,7 @@ class _ConvSiluFn(torch.autograd.Function):
         b_ = bias.detach().float().contiguous()
         out = _empty_seq(bt, l, c, x.device)
         st = lib.vmscan_conv1d_silu_fwd(
-            bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(out), _strides(out),
+            bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(out), _strides(out), None, None,
             _dir_ptr(direction), _stream(x),
         )
         _native.check(st, "vmscan_conv1d_silu_fwd")
@@ -367,7 +367,7 @@ class _DtSoftplusFn(torch.autograd.Function):
         # the rows of those partials are added here (a small reduction)
         part = torch.empty((lib.vmscan_dt_softplus_bias_rows(b * l), dn), dtype=torch.float32, device=x_.device)
         st = lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(x_), x_.stride(1), _ptr(w_), _ptr(b_), _ptr(g_in),
-                                        g_in.stride(1), _ptr(dpre), dpre.stride(1), _ptr(part), _stream(x_))
+                                        g_in.stride(1), _ptr(dpre), dpre.stride(1), None, _ptr(part), _stream(x_))
         _native.check(st, "vmscan_dt_softplus_bwd")
         g2 = dpre.reshape(b * l, dn)
         dx = (g2 @ w_).reshape(b, l, r)

@@ -189,8 +189,16 @@ def test_fused_branch_node_matches_per_node_autograd(K, grid):
     torch.testing.assert_close(y1, y2, rtol=1e-6, atol=1e-6)  # the same kernels; GEMM algorithms may differ
     torch.testing.assert_close(dh1, dh2, rtol=1e-5, atol=1e-6)
     assert g1.keys() == g2.keys()
+    # The two compositions run the same scan and conv kernels but different
+    # GEMMs for x_proj / dt_proj (the fused node: the tensor-core GEMM; the
+    # per-node path: cuBLAS), so near-zero elements of cancelling sums (conv
+    # bias) agree to rounding of the tensor's scale, not of themselves; a
+    # plumbing error would be of the tensor's scale.  Parity with the oracle is
+    # asserted by the block tests above.
     for k in g1:
-        torch.testing.assert_close(g1[k], g2[k], rtol=1e-5, atol=1e-6, msg=k)
+        scale = float(g2[k].abs().max())
+        torch.testing.assert_close(g1[k], g2[k], rtol=1e-5, atol=max(1e-6, 1e-5 * scale),
+                                   msg=lambda m, k=k: f"{k}: {m}")
 
 
 REAL_GRIDS = [(4, (14, 14)), (6, (8, 8, 8)), (8, (8, 4, 4, 4))]

@@ -137,3 +137,48 @@ def test_gemm_skinny_slices_and_accumulate():
     # x_proj weight gradient (M 56 < one tile)
     gx = gemm_tf32x3(xdbc_s, True, xc_s, True, wide, dn, t)
     assert_parity("skinny x_proj dW", gx, xdbc.double().t() @ xc.double(), xdbc.t() @ xc)
+
+
+def test_fused_split_outputs_match_split_pass():
+    """The conv forward's xc hi / lo outputs and the dt_proj VJP's dpre hi / lo
+    outputs equal vmscan_tf32_split of the fp32 results bit for bit, and the
+    dbias partials do not change."""
+    import ctypes
+
+    from mlx_vision_mamba_b200 import _native, directions_for
+    from mlx_vision_mamba_b200.linear import tf32_split
+
+    lib = _native.load()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(23)
+    b, l, c, k = 3, 196, 128, 4
+    x = torch.randn(b, l, c, generator=gen).to(dev)
+    w = torch.randn(c, k, 1, generator=gen).to(dev)
+    bias = torch.randn(c, generator=gen).to(dev)
+    S = _native.Strides(l * c, c)
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    direction = directions_for(4, (14, 14))[2]
+    dref = ctypes.byref(direction.to_native())
+    out, hi, lo = (torch.empty_like(x) for _ in range(3))
+    assert lib.vmscan_conv1d_silu_fwd(b, l, c, k, P(x), S, P(w), P(bias), P(out), S, P(hi), P(lo), dref, sp) == 0
+    out2 = torch.empty_like(x)
+    assert lib.vmscan_conv1d_silu_fwd(b, l, c, k, P(x), S, P(w), P(bias), P(out2), S, None, None, dref, sp) == 0
+    h_ref, l_ref = tf32_split(out2)
+    assert torch.equal(out, out2) and torch.equal(hi, h_ref) and torch.equal(lo, l_ref)
+
+    ntok, r, dn, wide = 300, 24, 256, 56
+    xw = torch.randn(ntok, wide, generator=gen).to(dev)
+    wdt = (torch.randn(dn, r, generator=gen) / r ** 0.5).to(dev)
+    bdt = torch.randn(dn, generator=gen).to(dev)
+    gin = torch.randn(ntok, dn, generator=gen).to(dev)
+    rows = lib.vmscan_dt_softplus_bias_rows(ntok)
+    dpre, part = torch.empty(ntok, dn, device=dev), torch.empty(rows, dn, device=dev)
+    dhi, dlo, part2 = torch.empty(ntok, dn, device=dev), torch.empty(ntok, dn, device=dev), torch.empty(rows, dn,
+                                                                                                        device=dev)
+    assert lib.vmscan_dt_softplus_bwd(ntok, r, dn, P(xw), wide, P(wdt), P(bdt), P(gin), dn, P(dpre), dn, None,
+                                      P(part), sp) == 0
+    assert lib.vmscan_dt_softplus_bwd(ntok, r, dn, P(xw), wide, P(wdt), P(bdt), P(gin), dn, P(dhi), dn, P(dlo),
+                                      P(part2), sp) == 0
+    h_ref, l_ref = tf32_split(dpre)
+    assert torch.equal(dhi, h_ref) and torch.equal(dlo, l_ref) and torch.equal(part, part2)
