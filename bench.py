@@ -194,8 +194,9 @@ class AbiScan:
         self.lib = lib = _native.load()
         if bf16:
             t = {k: (v.to(torch.bfloat16) if k not in ("A", "D") else v) for k, v in t.items()}
-        self.fwd_fn = lib.vmscan_fwd_bf16 if bf16 else lib.vmscan_fwd
-        self.bwd_fn = lib.vmscan_bwd_bf16 if bf16 else lib.vmscan_bwd
+        # the fp32 entry points take one more pointer (y_lo / dz_lo: NULL = plain fp32 outputs)
+        self.fwd_fn = lib.vmscan_fwd_bf16 if bf16 else (lambda *a: lib.vmscan_fwd(*a[:18], None, *a[18:]))
+        self.bwd_fn = lib.vmscan_bwd_bf16 if bf16 else (lambda *a: lib.vmscan_bwd(*a[:31], None, *a[31:]))
         self.t = t
         b, l, d = t["u"].shape
         self.shape = (b, l, d)
@@ -801,7 +802,7 @@ def time_conv(dev, iters=20):
 
         def bwd():
             rc = lib.vmscan_conv1d_silu_bwd(b, l, c, k, x.data_ptr(), S, w.data_ptr(), bias.data_ptr(),
-                                            dy.data_ptr(), S, dx.data_ptr(), S, dw.data_ptr(), db.data_ptr(), dref,
+                                            dy.data_ptr(), S, dx.data_ptr(), S, None, dw.data_ptr(), db.data_ptr(), dref,
                                             ws.data_ptr(), ws_n, sp)
             assert rc == 0, rc
 

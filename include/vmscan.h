@@ -110,6 +110,9 @@ int64_t vmscan_fwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inne
 /*
  * Fused forward: y = (selective_scan(u, delta, A, B, C, D)) * silu(z).
  * z == NULL drops the gate (plain reference `selective_scan` output).
+ * y_lo != NULL (same strides as y) writes the output as its TF32 hi part into
+ * y and lo part into y_lo, the operand form vmscan_gemm_tf32x3 reads (the
+ * block's out_proj GEMM), instead of y itself.
  * ckpt == NULL skips the checkpoints (inference); otherwise ckpt must hold
  * vmscan_ckpt_elems(...) floats.  workspace (16-byte aligned) of at least
  * vmscan_fwd_workspace_bytes(...) enables the chunked scan over L; NULL (or
@@ -125,6 +128,7 @@ int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
                const float* D,
                const float* z, vmscan_strides sz,
                float* y, vmscan_strides sy,
+               float* y_lo,
                float* ckpt,
                const vmscan_direction* dir,
                void* workspace, size_t workspace_bytes,
@@ -143,7 +147,9 @@ int64_t vmscan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inne
 /*
  * Fused VJP.  dy is the cotangent of the forward output (gated if z != NULL).
  * Writes du, ddelta, dA, dB, dC, dD and (when z != NULL) dz; all outputs are
- * overwritten, not accumulated.  Replaces mamba_metal_fused.py:182-250,
+ * overwritten, not accumulated.  dz_lo != NULL (same strides as dz) writes dz
+ * as its TF32 hi part into dz and lo part into dz_lo (the operand form of
+ * vmscan_gemm_tf32x3 for the in_proj gradient GEMMs).  Replaces mamba_metal_fused.py:182-250,
  * including the host-side reductions at :213-224, which run on the device in
  * a fixed order (deterministic).
  */
@@ -164,6 +170,7 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
                float* dC, vmscan_strides sdC,
                float* dD,
                float* dz, vmscan_strides sdz,
+               float* dz_lo,
                const vmscan_direction* dir,
                void* workspace, size_t workspace_bytes,
                vmscan_stream_t stream);
@@ -283,12 +290,17 @@ int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int6
 int64_t vmscan_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t channels,
                                           int64_t ksize);
 
-/* VJP of vmscan_conv1d_silu_fwd.  dweight / dbias are overwritten. */
+/*
+ * VJP of vmscan_conv1d_silu_fwd.  dweight / dbias are overwritten.  dx_lo !=
+ * NULL (16-byte aligned, laid out like dx) writes dx as its TF32 hi part into
+ * dx and lo part into dx_lo (the in_proj gradient GEMMs' operand form).
+ */
 int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize,
                            const float* x, vmscan_strides sx,
                            const float* weight, const float* bias,
                            const float* dout, vmscan_strides sdout,
                            float* dx, vmscan_strides sdx,
+                           float* dx_lo,
                            float* dweight, float* dbias,
                            const vmscan_direction* dir,
                            void* workspace, size_t workspace_bytes,

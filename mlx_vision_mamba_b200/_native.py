@@ -50,7 +50,7 @@ SIGNATURES = {
     "vmscan_fwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64, _D]),
     "vmscan_fwd": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _D, _p, _sz, _p],
+        [_i64, _i64, _i64, _i64, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _S, _p, _S, _p, _p, _D, _p, _sz, _p],
     ),
     "vmscan_fwd_bf16": (
         ctypes.c_int,
@@ -68,7 +68,7 @@ SIGNATURES = {
             _p,  # dA
             _p, _S, _p, _S,  # dB dC
             _p,  # dD
-            _p, _S,  # dz
+            _p, _S, _p,  # dz dz_lo
             _D, _p, _sz, _p,
         ],
     ),
@@ -106,7 +106,7 @@ SIGNATURES = {
     "vmscan_conv1d_bwd_workspace_bytes": (_i64, [_i64, _i64, _i64, _i64]),
     "vmscan_conv1d_silu_bwd": (
         ctypes.c_int,
-        [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _p, _S, _p, _p, _D, _p, _sz, _p],
+        [_i64, _i64, _i64, _i64, _p, _S, _p, _p, _p, _S, _p, _S, _p, _p, _p, _D, _p, _sz, _p],
     ),
     "vmscan_dt_softplus_fwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p]),
     "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p]),

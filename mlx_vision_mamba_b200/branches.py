@@ -77,170 +77,273 @@ def _seq_view(t: torch.Tensor, b: int, l: int) -> torch.Tensor:
     return t.view(b, l, t.shape[-1]) if t.is_contiguous() else t.unflatten(0, (b, l))
 
 
+def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad):
+    """The K branches' forward on their streams: direction k reads its x / z
+    column slices of xz and writes its scan output into its slice of y_all
+    (with y_lo_all: the output's TF32 hi part into y_all and lo part into
+    y_lo_all).  Returns what the backward needs per branch."""
+    lib = _native.load()
+    dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
+    kb = len(dirs)
+    n = D_STATE
+    b, l, _ = xz.shape
+    dev = xz.device
+    wide = r + 2 * n
+    tc = _tc_rows(r, dn)
+    cur = torch.cuda.current_stream(dev)
+    saved = []
+    for k in range(kb):
+        conv_w, conv_b, xproj_w, dt_w, dt_b, a_log, d_skip = params[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)]
+        s = streams[k]
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            sp = _stream_ptr(s)
+            dptr = _dir_ptr(dirs[k])
+            x = xz[:, :, 2 * dn * k:2 * dn * k + dn]
+            z = xz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
+            if not (_tma_compatible(x) and _tma_compatible(z)):
+                x, z = _prepare(x), _prepare(z)
+            cw = conv_w.detach().contiguous()
+            cb = conv_b.detach().contiguous()
+            xc = _empty_seq(b, l, dn, dev)
+            # with the tensor-core x_proj the conv also writes xc's TF32 parts (its GEMM operand)
+            xc_s = (_empty_seq(b, l, dn, dev), _empty_seq(b, l, dn, dev)) if tc else (None, None)
+            _native.check(lib.vmscan_conv1d_silu_fwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
+                                                     _ptr(xc), _strides(xc), _ptr(xc_s[0]), _ptr(xc_s[1]), dptr,
+                                                     sp), "vmscan_conv1d_silu_fwd")
+            if tc:
+                xc_s = (xc_s[0].view(b * l, dn), xc_s[1].view(b * l, dn))
+                xdbc = gemm_tf32x3(xc_s, False, tf32_split(xproj_w.detach().contiguous()), False, b * l, wide, dn)
+            else:
+                xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
+            dw_ = dt_w.detach().contiguous()
+            db_ = dt_b.detach().contiguous()
+            delta = _empty_seq(b, l, dn, dev)
+            _native.check(lib.vmscan_dt_softplus_fwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
+                                                     _ptr(delta), delta.stride(1), sp), "vmscan_dt_softplus_fwd")
+            a = -torch.exp(a_log.detach())
+            bmat = _prepare(_seq_view(xdbc[:, r:r + n], b, l))
+            cmat = _prepare(_seq_view(xdbc[:, r + n:], b, l))
+            dsk = d_skip.detach().contiguous()
+            y = y_all[:, :, dn * k:dn * (k + 1)]
+            y_lo = y_lo_all[:, :, dn * k:dn * (k + 1)] if y_lo_all is not None else None
+            ckpt = None
+            if need_grad:
+                n_ck = lib.vmscan_ckpt_elems(b, l, dn, D_STATE, dptr)
+                if n_ck < 0:
+                    _native.check(-n_ck, "vmscan_ckpt_elems")
+                ckpt = torch.empty(n_ck, dtype=torch.float32, device=dev)
+            fws_n = lib.vmscan_fwd_workspace_bytes(b, l, dn, D_STATE, dptr)
+            if fws_n < 0:
+                _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
+            fws = torch.empty(int(fws_n), dtype=torch.uint8, device=dev) if fws_n > 0 else None
+            _native.check(lib.vmscan_fwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
+                                         _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
+                                         _ptr(dsk), _ptr(z), _strides(z), _ptr(y), _strides(y), _ptr(y_lo),
+                                         _ptr(ckpt), dptr, _ptr(fws), int(fws_n), sp), "vmscan_fwd")
+            saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s))
+    for s in streams[:kb]:
+        cur.wait_stream(s)
+    return saved
+
+
+def _run_branches_bwd(saved, xproj, meta, dy_all, dxz, dxz_lo):
+    """The K branches' VJP on their streams: direction k reads its slice of
+    dy_all and writes dx / dz into its slices of dxz (with dxz_lo: their TF32
+    hi parts into dxz and lo parts into dxz_lo).  Returns the parameter
+    gradients in block_params order, branch after branch."""
+    lib = _native.load()
+    dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
+    kb = len(dirs)
+    n = D_STATE
+    b, l, _ = dy_all.shape
+    dev = dy_all.device
+    wide = r + 2 * n
+    tc = _tc_rows(r, dn)
+    cur = torch.cuda.current_stream(dev)
+    grads: List[Optional[torch.Tensor]] = [None] * (PARAMS_PER_BLOCK * kb)
+    for k in range(kb):
+        x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s = saved[k]
+        xproj_w = xproj[k].detach()
+        s = streams[k]
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            sp = _stream_ptr(s)
+            dptr = _dir_ptr(dirs[k])
+            dy = _prepare(dy_all[:, :, dn * k:dn * (k + 1)])
+            du = _empty_seq(b, l, dn, dev)
+            ddelta = _empty_seq(b, l, dn, dev)
+            dA = torch.empty((dn, n), dtype=torch.float32, device=dev)
+            dD = torch.empty((dn,), dtype=torch.float32, device=dev)
+            dxdbc = torch.empty((b * l, wide), dtype=torch.float32, device=dev)
+            dB = _seq_view(dxdbc[:, r:r + n], b, l)
+            dC = _seq_view(dxdbc[:, r + n:], b, l)
+            dz = dxz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
+            dz_lo = dxz_lo[:, :, 2 * dn * k + dn:2 * dn * (k + 1)] if dxz_lo is not None else None
+            ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, D_STATE, dptr, 0)
+            if ws_n < 0:
+                _native.check(-ws_n, "vmscan_bwd_workspace_bytes")
+            ws = torch.empty(max(int(ws_n), 256), dtype=torch.uint8, device=dev)
+            _native.check(lib.vmscan_bwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
+                                         _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
+                                         _ptr(dsk), _ptr(z), _strides(z), _ptr(ckpt), _ptr(dy), _strides(dy),
+                                         _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta), _ptr(dA),
+                                         _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD), _ptr(dz),
+                                         _strides(dz), _ptr(dz_lo), dptr, _ptr(ws), ws.numel(), sp),
+                          "vmscan_bwd")
+            # dt_proj + softplus: dpre (for the tensor cores: its TF32 parts), then its
+            # GEMMs; dbias from the kernel's partial sums
+            t = b * l
+            dpre = _empty_seq(b, l, dn, dev)
+            dpre_lo = _empty_seq(b, l, dn, dev) if tc else None
+            part = torch.empty((lib.vmscan_dt_softplus_bias_rows(t), dn), dtype=torch.float32, device=dev)
+            _native.check(lib.vmscan_dt_softplus_bwd(t, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
+                                                     _ptr(ddelta), ddelta.stride(1), _ptr(dpre), dpre.stride(1),
+                                                     _ptr(dpre_lo), _ptr(part), sp), "vmscan_dt_softplus_bwd")
+            g_dt_b = part.sum(0)
+            du2 = du.view(t, dn)
+            if tc:
+                dpre_s = (dpre.view(t, dn), dpre_lo.view(t, dn))
+                xdbc_s = tf32_split(xdbc)
+                # dt_proj input gradient straight into its slice of dx_dbc: dpre W_dt
+                gemm_tf32x3(dpre_s, False, tf32_split(dw_), True, t, r, dn, out=dxdbc[:, :r])
+                # dt_proj weight gradient dpre^T x_dbc[:, :r] (both read MN-major)
+                g_dt_w = gemm_tf32x3(dpre_s, True, (xdbc_s[0][:, :r], xdbc_s[1][:, :r]), True, dn, r, t)
+                # x_proj: its input gradient lands on du in place (du += dx_dbc W_x)
+                dxdbc_s = tf32_split(dxdbc)
+                gemm_tf32x3(dxdbc_s, False, tf32_split(xproj_w.contiguous()), True, t, dn, wide, out=du2,
+                            accumulate=True)
+                g_xproj = gemm_tf32x3(dxdbc_s, True, xc_s, True, wide, dn, t)
+            else:
+                dpre2 = dpre.reshape(t, dn)
+                dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
+                g_dt_w = _mm_tn(dpre2, xdbc[:, :r])
+                # x_proj: its input gradient lands on du in place (du += dx_dbc W)
+                du2.addmm_(dxdbc, xproj_w)
+                g_xproj = _mm_tn(dxdbc, xc.reshape(t, dn))
+            # conv1d + SiLU: dx straight into its slice of dxz
+            dx = dxz[:, :, 2 * dn * k:2 * dn * k + dn]
+            dx_lo = dxz_lo[:, :, 2 * dn * k:2 * dn * k + dn] if dxz_lo is not None else None
+            g_cw = torch.empty_like(cw)
+            g_cb = torch.empty_like(cb)
+            cws_n = lib.vmscan_conv1d_bwd_workspace_bytes(b, l, dn, ksize)
+            if cws_n < 0:
+                _native.check(-cws_n, "vmscan_conv1d_bwd_workspace_bytes")
+            cws = torch.empty(int(cws_n), dtype=torch.uint8, device=dev)
+            _native.check(lib.vmscan_conv1d_silu_bwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
+                                                     _ptr(du), _strides(du), _ptr(dx), _strides(dx), _ptr(dx_lo),
+                                                     _ptr(g_cw), _ptr(g_cb), dptr, _ptr(cws), cws.numel(), sp),
+                          "vmscan_conv1d_silu_bwd")
+            # A = -exp(A_log): dA_log = dA * A
+            g_alog = dA * a
+            grads[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)] = [g_cw, g_cb, g_xproj, g_dt_w, g_dt_b, g_alog,
+                                                                      dD]
+    for s in streams[:kb]:
+        cur.wait_stream(s)
+    return grads
+
+
 class _BranchesFn(torch.autograd.Function):
+    """xz (in_proj output, B x L x K 2 d_inner) -> y_all (B x L x K d_inner)."""
+
     @staticmethod
     def forward(ctx, xz, meta, *params):
-        lib = _native.load()
-        dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
-        kb = len(dirs)
-        n = D_STATE
         b, l, _ = xz.shape
-        dev = xz.device
-        wide = r + 2 * n
-        tc = _tc_rows(r, dn)
-        cur = torch.cuda.current_stream(dev)
-        y_all = _empty_seq(b, l, kb * dn, dev)
+        kb = len(meta["dirs"])
+        y_all = _empty_seq(b, l, kb * meta["d_inner"], xz.device)
         need_grad = any(ctx.needs_input_grad)
-        saved = []
-        for k in range(kb):
-            conv_w, conv_b, xproj_w, dt_w, dt_b, a_log, d_skip = params[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)]
-            s = streams[k]
-            s.wait_stream(cur)
-            with torch.cuda.stream(s):
-                sp = _stream_ptr(s)
-                dptr = _dir_ptr(dirs[k])
-                x = xz[:, :, 2 * dn * k:2 * dn * k + dn]
-                z = xz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
-                if not (_tma_compatible(x) and _tma_compatible(z)):
-                    x, z = _prepare(x), _prepare(z)
-                cw = conv_w.detach().contiguous()
-                cb = conv_b.detach().contiguous()
-                xc = _empty_seq(b, l, dn, dev)
-                # with the tensor-core x_proj the conv also writes xc's TF32 parts (its GEMM operand)
-                xc_s = (_empty_seq(b, l, dn, dev), _empty_seq(b, l, dn, dev)) if tc else (None, None)
-                _native.check(lib.vmscan_conv1d_silu_fwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
-                                                         _ptr(xc), _strides(xc), _ptr(xc_s[0]), _ptr(xc_s[1]), dptr,
-                                                         sp), "vmscan_conv1d_silu_fwd")
-                if tc:
-                    xc_s = (xc_s[0].view(b * l, dn), xc_s[1].view(b * l, dn))
-                    xdbc = gemm_tf32x3(xc_s, False, tf32_split(xproj_w.detach().contiguous()), False, b * l, wide, dn)
-                else:
-                    xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
-                dw_ = dt_w.detach().contiguous()
-                db_ = dt_b.detach().contiguous()
-                delta = _empty_seq(b, l, dn, dev)
-                _native.check(lib.vmscan_dt_softplus_fwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
-                                                         _ptr(delta), delta.stride(1), sp), "vmscan_dt_softplus_fwd")
-                a = -torch.exp(a_log.detach())
-                bmat = _prepare(_seq_view(xdbc[:, r:r + n], b, l))
-                cmat = _prepare(_seq_view(xdbc[:, r + n:], b, l))
-                dsk = d_skip.detach().contiguous()
-                y = y_all[:, :, dn * k:dn * (k + 1)]
-                ckpt = None
-                if need_grad:
-                    n_ck = lib.vmscan_ckpt_elems(b, l, dn, D_STATE, dptr)
-                    if n_ck < 0:
-                        _native.check(-n_ck, "vmscan_ckpt_elems")
-                    ckpt = torch.empty(n_ck, dtype=torch.float32, device=dev)
-                fws_n = lib.vmscan_fwd_workspace_bytes(b, l, dn, D_STATE, dptr)
-                if fws_n < 0:
-                    _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
-                fws = torch.empty(int(fws_n), dtype=torch.uint8, device=dev) if fws_n > 0 else None
-                _native.check(lib.vmscan_fwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
-                                             _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
-                                             _ptr(dsk), _ptr(z), _strides(z), _ptr(y), _strides(y), _ptr(ckpt), dptr,
-                                             _ptr(fws), int(fws_n), sp), "vmscan_fwd")
-                saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s))
-        for s in streams[:kb]:
-            cur.wait_stream(s)
+        saved = _run_branches_fwd(xz, meta, params, y_all, None, need_grad)
         if need_grad:
             ctx.saved = saved
             ctx.xproj = [params[PARAMS_PER_BLOCK * k + 2] for k in range(kb)]
             ctx.meta = meta
-            ctx.xz_shape = xz.shape
         return y_all
 
     @staticmethod
     def backward(ctx, dy_all):
-        lib = _native.load()
         meta = ctx.meta
-        dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
-        kb = len(dirs)
-        n = D_STATE
-        b, l, _ = ctx.xz_shape
-        dev = dy_all.device
-        wide = r + 2 * n
-        tc = _tc_rows(r, dn)
-        cur = torch.cuda.current_stream(dev)
-        dxz = _empty_seq(b, l, kb * 2 * dn, dev)
-        grads: List[Optional[torch.Tensor]] = [None] * (PARAMS_PER_BLOCK * kb)
-        for k in range(kb):
-            x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s = ctx.saved[k]
-            xproj_w = ctx.xproj[k].detach()
-            s = streams[k]
-            s.wait_stream(cur)
-            with torch.cuda.stream(s):
-                sp = _stream_ptr(s)
-                dptr = _dir_ptr(dirs[k])
-                dy = _prepare(dy_all[:, :, dn * k:dn * (k + 1)])
-                du = _empty_seq(b, l, dn, dev)
-                ddelta = _empty_seq(b, l, dn, dev)
-                dA = torch.empty((dn, n), dtype=torch.float32, device=dev)
-                dD = torch.empty((dn,), dtype=torch.float32, device=dev)
-                dxdbc = torch.empty((b * l, wide), dtype=torch.float32, device=dev)
-                dB = _seq_view(dxdbc[:, r:r + n], b, l)
-                dC = _seq_view(dxdbc[:, r + n:], b, l)
-                dz = dxz[:, :, 2 * dn * k + dn:2 * dn * (k + 1)]
-                ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, D_STATE, dptr, 0)
-                if ws_n < 0:
-                    _native.check(-ws_n, "vmscan_bwd_workspace_bytes")
-                ws = torch.empty(max(int(ws_n), 256), dtype=torch.uint8, device=dev)
-                _native.check(lib.vmscan_bwd(b, l, dn, D_STATE, _ptr(xc), _strides(xc), _ptr(delta), _strides(delta),
-                                             _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
-                                             _ptr(dsk), _ptr(z), _strides(z), _ptr(ckpt), _ptr(dy), _strides(dy),
-                                             _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta), _ptr(dA),
-                                             _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD), _ptr(dz),
-                                             _strides(dz), dptr, _ptr(ws), ws.numel(), sp), "vmscan_bwd")
-                # dt_proj + softplus: dpre (for the tensor cores: its TF32 parts), then its
-                # GEMMs; dbias from the kernel's partial sums
-                t = b * l
-                dpre = _empty_seq(b, l, dn, dev)
-                dpre_lo = _empty_seq(b, l, dn, dev) if tc else None
-                part = torch.empty((lib.vmscan_dt_softplus_bias_rows(t), dn), dtype=torch.float32, device=dev)
-                _native.check(lib.vmscan_dt_softplus_bwd(t, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
-                                                         _ptr(ddelta), ddelta.stride(1), _ptr(dpre), dpre.stride(1),
-                                                         _ptr(dpre_lo), _ptr(part), sp), "vmscan_dt_softplus_bwd")
-                g_dt_b = part.sum(0)
-                du2 = du.view(t, dn)
-                if tc:
-                    dpre_s = (dpre.view(t, dn), dpre_lo.view(t, dn))
-                    xdbc_s = tf32_split(xdbc)
-                    # dt_proj input gradient straight into its slice of dx_dbc: dpre W_dt
-                    gemm_tf32x3(dpre_s, False, tf32_split(dw_), True, t, r, dn, out=dxdbc[:, :r])
-                    # dt_proj weight gradient dpre^T x_dbc[:, :r] (both read MN-major)
-                    g_dt_w = gemm_tf32x3(dpre_s, True, (xdbc_s[0][:, :r], xdbc_s[1][:, :r]), True, dn, r, t)
-                    # x_proj: its input gradient lands on du in place (du += dx_dbc W_x)
-                    dxdbc_s = tf32_split(dxdbc)
-                    gemm_tf32x3(dxdbc_s, False, tf32_split(xproj_w.contiguous()), True, t, dn, wide, out=du2,
-                                accumulate=True)
-                    g_xproj = gemm_tf32x3(dxdbc_s, True, xc_s, True, wide, dn, t)
-                else:
-                    dpre2 = dpre.reshape(t, dn)
-                    dxdbc[:, :r].copy_(torch.mm(dpre2, dw_))
-                    g_dt_w = _mm_tn(dpre2, xdbc[:, :r])
-                    # x_proj: its input gradient lands on du in place (du += dx_dbc W)
-                    du2.addmm_(dxdbc, xproj_w)
-                    g_xproj = _mm_tn(dxdbc, xc.reshape(t, dn))
-                # conv1d + SiLU: dx straight into its slice of dxz
-                dx = dxz[:, :, 2 * dn * k:2 * dn * k + dn]
-                g_cw = torch.empty_like(cw)
-                g_cb = torch.empty_like(cb)
-                cws_n = lib.vmscan_conv1d_bwd_workspace_bytes(b, l, dn, ksize)
-                if cws_n < 0:
-                    _native.check(-cws_n, "vmscan_conv1d_bwd_workspace_bytes")
-                cws = torch.empty(int(cws_n), dtype=torch.uint8, device=dev)
-                _native.check(lib.vmscan_conv1d_silu_bwd(b, l, dn, ksize, _ptr(x), _strides(x), _ptr(cw), _ptr(cb),
-                                                         _ptr(du), _strides(du), _ptr(dx), _strides(dx), _ptr(g_cw),
-                                                         _ptr(g_cb), dptr, _ptr(cws), cws.numel(), sp),
-                              "vmscan_conv1d_silu_bwd")
-                # A = -exp(A_log): dA_log = dA * A
-                g_alog = dA * a
-                grads[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)] = [g_cw, g_cb, g_xproj, g_dt_w, g_dt_b, g_alog,
-                                                                          dD]
-        for s in streams[:kb]:
-            cur.wait_stream(s)
+        b, l, _ = dy_all.shape
+        dxz = _empty_seq(b, l, len(meta["dirs"]) * 2 * meta["d_inner"], dy_all.device)
+        grads = _run_branches_bwd(ctx.saved, ctx.xproj, meta, dy_all, dxz, None)
         ctx.saved = None
         return (dxz, None, *grads)
+
+
+class _BlockCoreFn(torch.autograd.Function):
+    """h (B x L x E) -> out_proj(concat_k branch_k(in_proj(h))) as one node.
+
+    in_proj and out_proj run on the tensor-core GEMM with the block's
+    concatenated weights (w_in: K 2 d_inner x E, w_out: E x K d_inner), and
+    the tensors between them never exist as fp32 where only a GEMM reads
+    them: the scans write y_all as its TF32 parts (the out_proj operand, kept
+    for out_proj's weight gradient), and the scan and conv VJPs write dxz, the
+    in_proj output gradient, as its TF32 parts (the operand of in_proj's input
+    and weight gradients).  Only h, the block output's gradient and the
+    weights go through separate split passes."""
+
+    @staticmethod
+    def forward(ctx, h, w_in, w_out, meta, *params):
+        b, l, e = h.shape
+        kb, dn = len(meta["dirs"]), meta["d_inner"]
+        t = b * l
+        h_s = tf32_split(h.reshape(t, e).contiguous())
+        win_s = tf32_split(w_in.detach().contiguous())
+        xz = gemm_tf32x3(h_s, False, win_s, False, t, kb * 2 * dn, e).view(b, l, kb * 2 * dn)
+        y_hi = _empty_seq(b, l, kb * dn, h.device)
+        y_lo = _empty_seq(b, l, kb * dn, h.device)
+        need_grad = any(ctx.needs_input_grad)
+        saved = _run_branches_fwd(xz, meta, params, y_hi, y_lo, need_grad)
+        y_s = (y_hi.view(t, kb * dn), y_lo.view(t, kb * dn))
+        wout_s = tf32_split(w_out.detach().contiguous())
+        out = gemm_tf32x3(y_s, False, wout_s, False, t, e, kb * dn).view(b, l, e)
+        if need_grad:
+            ctx.saved = saved
+            ctx.xproj = [params[PARAMS_PER_BLOCK * k + 2] for k in range(kb)]
+            ctx.meta = meta
+            ctx.parts = (h_s, win_s, y_s, wout_s)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        meta = ctx.meta
+        h_s, win_s, y_s, wout_s = ctx.parts
+        b, l, e = dout.shape
+        kb, dn = len(meta["dirs"]), meta["d_inner"]
+        t = b * l
+        dev = dout.device
+        d_s = tf32_split(dout.reshape(t, e).contiguous())
+        # out_proj: weight gradient dout^T y, input gradient dout W_out (W_out read MN-major)
+        g_wout = gemm_tf32x3(d_s, True, y_s, True, e, kb * dn, t)
+        dy_all = gemm_tf32x3(d_s, False, wout_s, True, t, kb * dn, e).view(b, l, kb * dn)
+        dxz_hi = _empty_seq(b, l, kb * 2 * dn, dev)
+        dxz_lo = _empty_seq(b, l, kb * 2 * dn, dev)
+        grads = _run_branches_bwd(ctx.saved, ctx.xproj, meta, dy_all, dxz_hi, dxz_lo)
+        dxz_s = (dxz_hi.view(t, kb * 2 * dn), dxz_lo.view(t, kb * 2 * dn))
+        # in_proj: input gradient dxz W_in (W_in read MN-major), weight gradient dxz^T h
+        dh = gemm_tf32x3(dxz_s, False, win_s, True, t, e, kb * 2 * dn).view(b, l, e)
+        g_win = gemm_tf32x3(dxz_s, True, h_s, True, kb * 2 * dn, e, t)
+        ctx.saved = ctx.parts = None
+        return (dh, g_win, g_wout, None, *grads)
+
+
+def block_core_ok(blocks: Sequence, h: torch.Tensor) -> bool:
+    """_BlockCoreFn applies when every row its GEMMs read or write (E, K 2
+    d_inner, K d_inner floats) is a whole number of 16-byte units."""
+    b0 = blocks[0]
+    return (h.is_cuda and h.dtype == torch.float32 and h.shape[-1] % 4 == 0 and b0.d_inner % 4 == 0
+            and _tc_rows(b0.dt_rank, b0.d_inner) and h.numel() > 0)
+
+
+def block_core_forward(blocks: Sequence, directions: Sequence[Optional[ScanDirection]], h: torch.Tensor,
+                       w_in: torch.Tensor, w_out: torch.Tensor, streams: Sequence[torch.cuda.Stream]) -> torch.Tensor:
+    """sum_k block_k(h, direction_k) for K MambaBlocks as one autograd node
+    (_BlockCoreFn); w_in / w_out are the blocks' in_proj / out_proj weights
+    concatenated (torch.cat, so their gradients reach every block)."""
+    b0 = blocks[0]
+    meta = {"d_inner": b0.d_inner, "dt_rank": b0.dt_rank, "d_conv": b0.d_conv, "dirs": list(directions),
+            "streams": list(streams)}
+    params = [p for blk in blocks for p in block_params(blk)]
+    return _BlockCoreFn.apply(h, w_in, w_out, meta, *params)
 
 
 def branches_forward(blocks: Sequence, directions: Sequence[Optional[ScanDirection]], xz: torch.Tensor,

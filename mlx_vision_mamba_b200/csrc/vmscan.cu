@@ -335,8 +335,8 @@ size_t fwd_chunk_bytes(const ScanGeom& g) { return fwd_chunk_plan(g).bytes; }
 
 template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY>
 int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-                 const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
-                 const ChunkArgs& ch, int nz, const ScanGeom& g, cudaStream_t stream) {
+                 const CUtensorMap& mC, T* y, vmscan_strides sy, float* y_lo, const float* A, const float* D,
+                 float* ckpt, const ChunkArgs& ch, int nz, const ScanGeom& g, cudaStream_t stream) {
   using Cfg = FwdCfg<kFwdNCW, T>;
   auto kern = scan_fwd_kernel<kFwdNCW, T, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
@@ -346,7 +346,8 @@ int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
   int sys = 0;
   if (STORE_Y) VM_TRY(seq_stride32("y", sy, g.seqlen, sys));
   const dim3 grid(unsigned((g.d_inner + Cfg::DT - 1) / Cfg::DT), unsigned(g.batch), unsigned(nz));
-  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sys, A, D, ckpt, ch, g, st);
+  kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mB, mC, y, sy.batch, sys, y_lo, A, D, ckpt, ch, g,
+                                                   st);
   return check_launch();
 }
 
@@ -355,13 +356,13 @@ int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
 // 0 .. nc-2, the carry chain, then the main pass over all chunks.
 template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV>
 int run_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-              const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
-              void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
+              const CUtensorMap& mC, T* y, vmscan_strides sy, float* y_lo, const float* A, const float* D,
+              float* ckpt, void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
   const ChunkPlan plan = fwd_chunk_plan(g);
   if (plan.nc == 1 || ws == nullptr || ws_bytes < plan.bytes) {
     const ChunkArgs one{g.nboxes, 1, nullptr, nullptr, nullptr};
-    return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, one, 1, g,
-                                                                stream);
+    return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, one,
+                                                                1, g, stream);
   }
   const size_t per = size_t(g.batch) * plan.nc * g.d_inner;
   char* w = static_cast<char*>(ws);
@@ -369,25 +370,25 @@ int run_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& 
   float* h_start = reinterpret_cast<float*>(w + align256(per * NS * 4));
   float* carry_s = reinterpret_cast<float*>(w + 2 * align256(per * NS * 4));
   const ChunkArgs ch{plan.bpc, plan.nc, h_start, carry_h, carry_s};
-  VM_TRY((launch_fwd_t<T, false, false, false, REV, true>(mu, mdt, mz, mB, mC, nullptr, vmscan_strides{0, 0}, A,
-                                                         D, nullptr, ch, plan.nc - 1, g, stream)));
+  VM_TRY((launch_fwd_t<T, false, false, false, REV, true>(mu, mdt, mz, mB, mC, nullptr, vmscan_strides{0, 0},
+                                                         nullptr, A, D, nullptr, ch, plan.nc - 1, g, stream)));
   const int64_t n = int64_t(g.batch) * g.d_inner * NS;
   carry_fwd_kernel<<<unsigned((n + 255) / 256), 256, 0, stream>>>(A, carry_h, carry_s, h_start, g.batch, plan.nc,
                                                                   g.d_inner);
   VM_TRY(check_launch());
-  return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ch, plan.nc,
-                                                              g, stream);
+  return launch_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, REV, false>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ch,
+                                                              plan.nc, g, stream);
 }
 
 template <typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y>
 int launch_fwd(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMap& mz, const CUtensorMap& mB,
-               const CUtensorMap& mC, T* y, vmscan_strides sy, const float* A, const float* D, float* ckpt,
-               void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
+               const CUtensorMap& mC, T* y, vmscan_strides sy, float* y_lo, const float* A, const float* D,
+               float* ckpt, void* ws, size_t ws_bytes, const ScanGeom& g, cudaStream_t stream) {
   if (g.reverse)
-    return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g,
-                                                       stream);
-  return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, ws_bytes, g,
-                                                      stream);
+    return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, true>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, ws_bytes,
+                                                       g, stream);
+  return run_fwd_t<T, HAS_Z, SAVE_CK, STORE_Y, false>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, ws_bytes,
+                                                      g, stream);
 }
 
 template <typename T>
@@ -398,6 +399,7 @@ struct BwdOut {
   vmscan_strides sddt;
   T* dz;
   vmscan_strides sdz;
+  float* dz_lo;  // fp32 only: dz as TF32 parts (hi into dz) when not NULL
 };
 
 template <typename T, bool HAS_Z, bool REV>
@@ -437,8 +439,8 @@ int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
   const BwdChunkArgs chunk{wl.bpc, wl.nc, p_in};
   const dim3 grid(ndt, unsigned(g.batch), unsigned(wl.nc));
   kern<<<grid, Cfg::NT, Cfg::SMEM_BYTES, stream>>>(mu, mdt, mz, mdy, mB, mC, o.du, o.sdu.batch, sdus, o.ddt,
-                                                   o.sddt.batch, sdts, o.dz, o.sdz.batch, sdzs, A, D, ckpt, wpart,
-                                                   wA, wD, chunk, g, st);
+                                                   o.sddt.batch, sdts, o.dz, o.sdz.batch, sdzs, o.dz_lo, A, D, ckpt,
+                                                   wpart, wA, wD, chunk, g, st);
   return check_launch();
 }
 
@@ -463,12 +465,13 @@ template <typename T>
 int fwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const T* u, vmscan_strides su,
              const T* delta, vmscan_strides sdelta, const float* A, const T* B, vmscan_strides sB, const T* C,
              vmscan_strides sC, const float* D, const T* z, vmscan_strides sz, T* y, vmscan_strides sy,
-             float* ckpt, const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
+             float* y_lo, float* ckpt, const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
              vmscan_stream_t stream) {
   constexpr int ES = int(sizeof(T));
   VM_TRY(check_common(d_state, A, D));
   if (u == nullptr || delta == nullptr || B == nullptr || C == nullptr || y == nullptr) return VMSCAN_ERR_NULL;
   if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
+  if (y_lo != nullptr && ES != 4) return fail(VMSCAN_ERR_SHAPE, "y_lo (TF32 parts) needs fp32 outputs");
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
   VM_TRY(ensure_context(u));
@@ -488,10 +491,10 @@ int fwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, co
   void* ws = workspace;
   const size_t wb = workspace_bytes;
   if (ws != nullptr && !aligned16(ws)) return fail(VMSCAN_ERR_ALIGN, "workspace is not 16-byte aligned");
-  if (hz && ck) return launch_fwd<T, true, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  if (hz) return launch_fwd<T, true, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  if (ck) return launch_fwd<T, false, true, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
-  return launch_fwd<T, false, false, true>(mu, mdt, mz, mB, mC, y, sy, A, D, ckpt, ws, wb, g, s);
+  if (hz && ck) return launch_fwd<T, true, true, true>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, wb, g, s);
+  if (hz) return launch_fwd<T, true, false, true>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, wb, g, s);
+  if (ck) return launch_fwd<T, false, true, true>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, wb, g, s);
+  return launch_fwd<T, false, false, true>(mu, mdt, mz, mB, mC, y, sy, y_lo, A, D, ckpt, ws, wb, g, s);
 }
 
 // VJP entry (fp32 or bf16 sequence tensors and their gradients; A, D, dA,
@@ -501,7 +504,7 @@ int bwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, co
              const T* delta, vmscan_strides sdelta, const float* A, const T* B, vmscan_strides sB, const T* C,
              vmscan_strides sC, const float* D, const T* z, vmscan_strides sz, const float* ckpt, const T* dy,
              vmscan_strides sdy, T* du, vmscan_strides sdu, T* ddelta, vmscan_strides sddelta, float* dA, T* dB,
-             vmscan_strides sdB, T* dC, vmscan_strides sdC, float* dD, T* dz, vmscan_strides sdz,
+             vmscan_strides sdB, T* dC, vmscan_strides sdC, float* dD, T* dz, vmscan_strides sdz, float* dz_lo,
              const vmscan_direction* dir, void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
   constexpr int ES = int(sizeof(T));
   VM_TRY(check_common(d_state, A, D));
@@ -509,6 +512,7 @@ int bwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, co
       ddelta == nullptr || dA == nullptr || dB == nullptr || dC == nullptr || dD == nullptr)
     return VMSCAN_ERR_NULL;
   if (z != nullptr && dz == nullptr) return VMSCAN_ERR_NULL;
+  if (dz_lo != nullptr && ES != 4) return fail(VMSCAN_ERR_SHAPE, "dz_lo (TF32 parts) needs fp32 outputs");
   if (ckpt != nullptr && !aligned16(ckpt)) return fail(VMSCAN_ERR_ALIGN, "ckpt is not 16-byte aligned");
   ScanGeom g;
   VM_TRY(make_geom(batch, seqlen, d_inner, dir, g));
@@ -543,11 +547,11 @@ int bwd_impl(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, co
     VM_TRY(encode_map(&fdt, "delta", delta, d_inner, FC::DT, sdelta, g, ES));
     VM_TRY(encode_map(&fB, "B", B, NS, NS, sB, g, ES));
     float* ckw = reinterpret_cast<float*>(ws + wl.ck);
-    VM_TRY((launch_fwd<T, false, true, false>(fu, fdt, fu, fB, fB, static_cast<T*>(nullptr), vmscan_strides{0, 0}, A, D, ckw,
-                                           ws + wl.fws, wl.total - wl.fws, g, s)));
+    VM_TRY((launch_fwd<T, false, true, false>(fu, fdt, fu, fB, fB, static_cast<T*>(nullptr), vmscan_strides{0, 0},
+                                              nullptr, A, D, ckw, ws + wl.fws, wl.total - wl.fws, g, s)));
     ck = ckw;
   }
-  const BwdOut<T> o{du, sdu, ddelta, sddelta, dz, sdz};
+  const BwdOut<T> o{du, sdu, ddelta, sddelta, dz, sdz, z != nullptr ? dz_lo : nullptr};
   if (z != nullptr) {
     VM_TRY((launch_bwd<T, true>(mu, mdt, mz, mdy, mB, mC, o, A, D, ck, wpart, wA, wD, wl, ws, g, s)));
   } else {
@@ -738,10 +742,10 @@ int64_t vmscan_ckpt_elems(int64_t batch, int64_t seqlen, int64_t d_inner, int64_
 int vmscan_fwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const float* u, vmscan_strides su,
                const float* delta, vmscan_strides sdelta, const float* A, const float* B, vmscan_strides sB,
                const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz, float* y,
-               vmscan_strides sy, float* ckpt, const vmscan_direction* dir, void* workspace,
+               vmscan_strides sy, float* y_lo, float* ckpt, const vmscan_direction* dir, void* workspace,
                size_t workspace_bytes, vmscan_stream_t stream) {
   return fwd_impl<float>(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, y, sy,
-                         ckpt, dir, workspace, workspace_bytes, stream);
+                         y_lo, ckpt, dir, workspace, workspace_bytes, stream);
 }
 
 int vmscan_fwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, const void* u,
@@ -752,8 +756,8 @@ int vmscan_fwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_st
   using T = __nv_bfloat16;
   return fwd_impl<T>(batch, seqlen, d_inner, d_state, static_cast<const T*>(u), su, static_cast<const T*>(delta),
                      sdelta, A, static_cast<const T*>(B), sB, static_cast<const T*>(C), sC, D,
-                     static_cast<const T*>(z), sz, static_cast<T*>(y), sy, ckpt, dir, workspace, workspace_bytes,
-                     stream);
+                     static_cast<const T*>(z), sz, static_cast<T*>(y), sy, nullptr, ckpt, dir, workspace,
+                     workspace_bytes, stream);
 }
 
 int64_t vmscan_fwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
@@ -780,10 +784,10 @@ int vmscan_bwd(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, 
                const float* C, vmscan_strides sC, const float* D, const float* z, vmscan_strides sz,
                const float* ckpt, const float* dy, vmscan_strides sdy, float* du, vmscan_strides sdu,
                float* ddelta, vmscan_strides sddelta, float* dA, float* dB, vmscan_strides sdB, float* dC,
-               vmscan_strides sdC, float* dD, float* dz, vmscan_strides sdz, const vmscan_direction* dir,
-               void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
+               vmscan_strides sdC, float* dD, float* dz, vmscan_strides sdz, float* dz_lo,
+               const vmscan_direction* dir, void* workspace, size_t workspace_bytes, vmscan_stream_t stream) {
   return bwd_impl<float>(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy,
-                         sdy, du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, workspace,
+                         sdy, du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dz_lo, dir, workspace,
                          workspace_bytes, stream);
 }
 
@@ -799,7 +803,7 @@ int vmscan_bwd_bf16(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_st
                      sdelta, A, static_cast<const T*>(B), sB, static_cast<const T*>(C), sC, D,
                      static_cast<const T*>(z), sz, ckpt, static_cast<const T*>(dy), sdy, static_cast<T*>(du), sdu,
                      static_cast<T*>(ddelta), sddelta, dA, static_cast<T*>(dB), sdB, static_cast<T*>(dC), sdC, dD,
-                     static_cast<T*>(dz), sdz, dir, workspace, workspace_bytes, stream);
+                     static_cast<T*>(dz), sdz, nullptr, dir, workspace, workspace_bytes, stream);
 }
 
 int vmscan_dt_softplus_fwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
@@ -857,8 +861,8 @@ int64_t vmscan_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t
 
 int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int64_t ksize, const float* x,
                            vmscan_strides sx, const float* weight, const float* bias, const float* dout,
-                           vmscan_strides sdout, float* dx, vmscan_strides sdx, float* dweight, float* dbias,
-                           const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
+                           vmscan_strides sdout, float* dx, vmscan_strides sdx, float* dx_lo, float* dweight,
+                           float* dbias, const vmscan_direction* dir, void* workspace, size_t workspace_bytes,
                            vmscan_stream_t stream) {
   if (x == nullptr || weight == nullptr || bias == nullptr || dout == nullptr || dx == nullptr ||
       dweight == nullptr || dbias == nullptr)
@@ -868,7 +872,7 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   VM_TRY(make_geom(batch, seqlen, channels, dir, g));
   VM_TRY(ensure_context(x));
   if (!aligned16(x) || !aligned16(dout) || !aligned16(dx) || !aligned16(bias) || sx.seq % 4 || sx.batch % 4 ||
-      sdout.seq % 4 || sdout.batch % 4 || sdx.seq % 4 || sdx.batch % 4)
+      sdout.seq % 4 || sdout.batch % 4 || sdx.seq % 4 || sdx.batch % 4 || (dx_lo != nullptr && !aligned16(dx_lo)))
     return VMSCAN_ERR_ALIGN;
   const int64_t need = vmscan_conv1d_bwd_workspace_bytes(batch, seqlen, channels, ksize);
   if (workspace == nullptr || int64_t(workspace_bytes) < need) return VMSCAN_ERR_WORKSPACE;
@@ -878,12 +882,12 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   float* wpart = static_cast<float*>(workspace);
   if (ksize <= 4)
     conv_silu_bwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
-                                                         sdout.seq, dx, sdx.batch, sdx.seq, wpart, int(channels),
-                                                         int(ksize), g);
+                                                         sdout.seq, dx, sdx.batch, sdx.seq, dx_lo, wpart,
+                                                         int(channels), int(ksize), g);
   else
     conv_silu_bwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
-                                                         sdout.seq, dx, sdx.batch, sdx.seq, wpart, int(channels),
-                                                         int(ksize), g);
+                                                         sdout.seq, dx, sdx.batch, sdx.seq, dx_lo, wpart,
+                                                         int(channels), int(ksize), g);
   VM_TRY(check_launch());
   const int n = int(channels * (ksize + 1));
   const int nrows = int(batch) * nchunk;
@@ -966,7 +970,7 @@ int vmscan_bwd_noalloc(int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d
   void* scratch = nullptr;
   VM_TRY(noalloc_scratch_addr(u, &scratch));
   return vmscan_bwd(batch, seqlen, d_inner, d_state, u, su, delta, sdelta, A, B, sB, C, sC, D, z, sz, ckpt, dy, sdy,
-                    du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, dir, scratch,
+                    du, sdu, ddelta, sddelta, dA, dB, sdB, dC, sdC, dD, dz, sdz, nullptr, dir, scratch,
                     size_t(VMSCAN_NOALLOC_SCRATCH_BYTES), stream);
 }
 

@@ -245,8 +245,8 @@ struct FwdCarry {
 template <typename T, bool HAS_Z, bool REV>
 __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float* __restrict__ part, uint32_t taddr,
                                         int nv, int warp, int lane, int c0l, const PairLane& pl, bool has_ck,
-                                        bool v0, bool v1, float Down, T* du_b, T* dt_b, T* dz_b, int sdus, int sdts,
-                                        int sdzs, bool ev) {
+                                        bool v0, bool v1, float Down, T* du_b, T* dt_b, T* dz_b, float* dzlo_b,
+                                        int sdus, int sdts, int sdzs, bool ev) {
   constexpr int DT = BwdCfg<T>::DT;
   const int* tok = S.tok;
   const int own = c0l + pl.hb;
@@ -310,7 +310,17 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
     const float dyv = ld_one(S.dy + k.r * DT + own);
     const float ypre = fmaf(k.uo, Down, ys);
     const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * zz));
-    stg_if_t(dz_b + int64_t(tok[k.r]) * sdzs, dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f), ev);
+    const float dzv = dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f);
+    const int64_t off = int64_t(tok[k.r]) * sdzs;
+    if (dzlo_b != nullptr) {
+      // dz as TF32 parts (hi into dz, lo into dz_lo) for the in_proj gradient GEMMs
+      float hi, lo;
+      split_tf32(dzv, hi, lo);
+      stg_if_t(dz_b + off, hi, ev);
+      stg_if(dzlo_b + off, lo, ev);
+    } else {
+      stg_if_t(dz_b + off, dzv, ev);
+    }
     S.dyp[k.r * DT + own] = dyv * (zz * sig);
   };
   {
@@ -398,7 +408,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_dy,
                     const __grid_constant__ CUtensorMap tm_B, const __grid_constant__ CUtensorMap tm_C,
                     T* __restrict__ du_out, int64_t sdub, int sdus, T* __restrict__ ddt_out,
-                    int64_t sdtb, int sdts, T* __restrict__ dz_out, int64_t sdzb, int sdzs,
+                    int64_t sdtb, int sdts, T* __restrict__ dz_out, int64_t sdzb, int sdzs, float* __restrict__ dz_lo,
                     const float* __restrict__ A, const float* __restrict__ Dskip, const float* __restrict__ ckpt,
                     float* __restrict__ wpart, float* __restrict__ wA, float* __restrict__ wD,
                     const BwdChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
@@ -521,6 +531,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
   T* du_b = du_out + b * sdub + own;
   T* dt_b = ddt_out + b * sdtb + own;
   T* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
+  float* dzlo_b = (HAS_Z && Cfg::F32 && dz_lo != nullptr) ? dz_lo + b * sdzb + own : nullptr;
   bool alive = true;
 
   for (int i = 0; i < nbx; ++i) {
@@ -538,7 +549,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     const int nv = S.tok[TMAX];
     if (alive)
       bwd_box<T, HAS_Z, REV>(L, S, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
-                          sdus, sdts, sdzs, ev);
+                          dzlo_b, sdus, sdts, sdzs, ev);
     // dy' was written into the stage: order those generic-proxy writes before
     // the TMA load that will refill the stage
     fence_proxy_async_smem();

@@ -131,8 +131,8 @@ template <int KW>
 __global__ void __launch_bounds__(CONV_THREADS)
     conv_silu_bwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
                          const float* __restrict__ bias, const float* __restrict__ dout, int64_t sdb, int64_t sds,
-                         float* __restrict__ dx, int64_t sxgb, int64_t sxgs, float* __restrict__ wpart, int C,
-                         int K, const ScanGeom g) {
+                         float* __restrict__ dx, int64_t sxgb, int64_t sxgs, float* __restrict__ dx_lo,
+                         float* __restrict__ wpart, int C, int K, const ScanGeom g) {
   __shared__ int64_t tok[CONV_CHUNK + 2 * CONV_KMAX];
   const int p0 = blockIdx.y * CONV_CHUNK;
   const int nchunk = gridDim.y;
@@ -236,7 +236,15 @@ __global__ void __launch_bounds__(CONV_THREADS)
             acc.w = fmaf(wr[j][3], dpw[j].w, acc.w);
           }
           const int64_t tkp = tok[t - (K - 1)];
-          *reinterpret_cast<float4*>(dxb + tkp * sxgs) = acc;
+          if (dx_lo != nullptr) {
+            // the TF32 parts of dx (for the in_proj gradient GEMMs) instead of dx
+            float4 hi, lo;
+            split_tf32_4(acc, hi, lo);
+            *reinterpret_cast<float4*>(dxb + tkp * sxgs) = hi;
+            *reinterpret_cast<float4*>(dx_lo + b * sxgb + c4 * 4 + tkp * sxgs) = lo;
+          } else {
+            *reinterpret_cast<float4*>(dxb + tkp * sxgs) = acc;
+          }
         }
       }
     }

@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
                     const __grid_constant__ CUtensorMap tm_C, T* __restrict__ y, int64_t syb, int sys,
-                    const float* __restrict__ A, const float* __restrict__ Dskip, float* __restrict__ ckpt,
+                    float* __restrict__ y_lo, const float* __restrict__ A, const float* __restrict__ Dskip,
+                    float* __restrict__ ckpt,
                     const ChunkArgs chunk, const ScanGeom g, int* __restrict__ status) {
   using Cfg = FwdCfg<NCW, T>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST;
@@ -167,6 +168,8 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
   const int own = c0l + pl.hb;
   const float Down = ev ? Dskip[d0 + own] : 0.f;
   T* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
+  // fp32 output as TF32 parts (hi into y, lo into y_lo) for the out_proj GEMM
+  float* ylo_base = (STORE_Y && Cfg::ES == 4 && y_lo != nullptr) ? y_lo + b * syb + d0 + own : nullptr;
   bool alive = true;
 
   struct Carry {
@@ -224,7 +227,15 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
         const float ys = pair_scatter(k.yp[0], k.yp[1], pl.hb);
         float yy = fmaf(k.uo, Down, ys);
         if (HAS_Z) yy *= silu_f(ld_one(sz + k.r * DT + own));
-        stg_if_t(ybase + int64_t(tok[k.r]) * sys, yy, ev);
+        const int64_t off = int64_t(tok[k.r]) * sys;
+        if (ylo_base != nullptr) {
+          float hi, lo;
+          split_tf32(yy, hi, lo);
+          stg_if_t(ybase + off, hi, ev);
+          stg_if(ylo_base + off, lo, ev);
+        } else {
+          stg_if_t(ybase + off, yy, ev);
+        }
       };
       Carry ka, kb;
       math(0, ka);

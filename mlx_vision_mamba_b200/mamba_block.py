@@ -26,7 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .direction import BACKWARD, ScanDirection, directions_for
-from .branches import branches_forward
+from .branches import block_core_forward, block_core_ok, branches_forward
 from .linear import linear_tc, supported as _tc_supported
 from .scan import conv1d_silu_cuda, dt_softplus_cuda, selective_scan_cuda
 
@@ -116,6 +116,9 @@ class MambaBlock(nn.Module):
         self.out_proj = Linear(self.d_inner, d_model, bias=False)
 
     def forward(self, x: torch.Tensor, direction: Optional[ScanDirection] = None) -> torch.Tensor:
+        if _fused_branches_ok([self], x) and block_core_ok([self], x):
+            return block_core_forward([self], [direction], x, self.in_proj.weight, self.out_proj.weight,
+                                      _branch_streams(x.device, 1))
         if _fused_branches_ok([self], x):
             xz = project(x, self.in_proj.weight)
             y = branches_forward([self], [direction], xz, _branch_streams(x.device, 1))
@@ -157,6 +160,11 @@ def directions_sum(blocks: Sequence[MambaBlock], directions: Sequence[Optional[S
     if len(blocks) == 1:
         return blocks[0](h, directions[0])
     two_dn = 2 * blocks[0].d_inner
+    if _fused_branches_ok(blocks, h) and block_core_ok(blocks, h):
+        # in_proj, the K branches and out_proj as one autograd node (branches.py)
+        return block_core_forward(blocks, directions, h, torch.cat([b.in_proj.weight for b in blocks], 0),
+                                  torch.cat([b.out_proj.weight for b in blocks], 1),
+                                  _branch_streams(h.device, len(blocks)))
     xz = project(h, torch.cat([b.in_proj.weight for b in blocks], 0))
     if _fused_branches_ok(blocks, h):
         # one autograd node for the K branches: outputs and input gradients

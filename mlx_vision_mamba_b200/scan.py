@@ -161,14 +161,13 @@ class _SelectiveScanFn(torch.autograd.Function):
         if fws_n < 0:
             _native.check(-fws_n, "vmscan_fwd_workspace_bytes")
         fws = torch.empty(int(fws_n), dtype=torch.uint8, device=x.device) if fws_n > 0 else None
-        fwd = lib.vmscan_fwd_bf16 if sd == torch.bfloat16 else lib.vmscan_fwd
-        st = fwd(
-            bt, l, dn, D_STATE,
-            _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
-            _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
-            _ptr(z_), _strides(z_), _ptr(y), _strides(y), _ptr(ckpt), dptr,
-            _ptr(fws), int(fws_n), _stream(x),
-        )
+        head = (bt, l, dn, D_STATE, _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_), _ptr(B_),
+                _strides(B_), _ptr(C_), _strides(C_), _ptr(D_), _ptr(z_), _strides(z_), _ptr(y), _strides(y))
+        tail = (_ptr(ckpt), dptr, _ptr(fws), int(fws_n), _stream(x))
+        if sd == torch.bfloat16:
+            st = lib.vmscan_fwd_bf16(*head, *tail)
+        else:
+            st = lib.vmscan_fwd(*head, None, *tail)  # y_lo: the fp32 output itself
         _native.check(st, "vmscan_fwd_bf16" if sd == torch.bfloat16 else "vmscan_fwd")
         if need_grad:
             ctx.save_for_backward(u_, dt_, A_, B_, C_, D_, z_, ckpt)
@@ -204,18 +203,15 @@ class _SelectiveScanFn(torch.autograd.Function):
         if ws_bytes < 0:
             _native.check(-ws_bytes, "vmscan_bwd_workspace_bytes")
         ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=dev)
-        bwd = lib.vmscan_bwd_bf16 if sd == torch.bfloat16 else lib.vmscan_bwd
-        st = bwd(
-            bt, l, dn, D_STATE,
-            _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_),
-            _ptr(B_), _strides(B_), _ptr(C_), _strides(C_), _ptr(D_),
-            _ptr(z_), _strides(z_), _ptr(ckpt),
-            _ptr(dy_), _strides(dy_),
-            _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta),
-            _ptr(dA), _ptr(dB), _strides(dB), _ptr(dC), _strides(dC), _ptr(dD),
-            _ptr(dz), _strides(dz),
-            dptr, _ptr(ws), ws.numel(), _stream(u_),
-        )
+        head = (bt, l, dn, D_STATE, _ptr(u_), _strides(u_), _ptr(dt_), _strides(dt_), _ptr(A_), _ptr(B_),
+                _strides(B_), _ptr(C_), _strides(C_), _ptr(D_), _ptr(z_), _strides(z_), _ptr(ckpt), _ptr(dy_),
+                _strides(dy_), _ptr(du), _strides(du), _ptr(ddelta), _strides(ddelta), _ptr(dA), _ptr(dB),
+                _strides(dB), _ptr(dC), _strides(dC), _ptr(dD), _ptr(dz), _strides(dz))
+        tail = (dptr, _ptr(ws), ws.numel(), _stream(u_))
+        if sd == torch.bfloat16:
+            st = lib.vmscan_bwd_bf16(*head, *tail)
+        else:
+            st = lib.vmscan_bwd(*head, None, *tail)  # dz_lo: dz itself
         _native.check(st, "vmscan_bwd_bf16" if sd == torch.bfloat16 else "vmscan_bwd")
         a_dt, d_dt = ctx.param_dtypes
         return du, ddelta, dA.to(a_dt), dB, dC, dD.to(d_dt), dz, None
@@ -305,7 +301,7 @@ class _ConvSiluFn(torch.autograd.Function):
         ws = torch.empty(int(ws_bytes), dtype=torch.uint8, device=x_.device)
         st = lib.vmscan_conv1d_silu_bwd(
             bt, l, c, k, _ptr(x_), _strides(x_), _ptr(w_), _ptr(b_), _ptr(dout_), _strides(dout_),
-            _ptr(dx), _strides(dx), _ptr(dw), _ptr(db), _dir_ptr(ctx.direction), _ptr(ws), ws.numel(),
+            _ptr(dx), _strides(dx), None, _ptr(dw), _ptr(db), _dir_ptr(ctx.direction), _ptr(ws), ws.numel(),
             _stream(x_),
         )
         _native.check(st, "vmscan_conv1d_silu_bwd")

@@ -50,7 +50,7 @@ def _null_call(lib, **over):
     return lib.vmscan_fwd(
         args["batch"], args["seqlen"], args["d_inner"], args["d_state"],
         args["u"], S, args["delta"], S, args["A"], args["B"], S, args["C"], S, args["D"],
-        None, S, args["y"], S, None, None, None, 0, None,
+        None, S, args["y"], S, None, None, None, None, 0, None,
     )
 
 

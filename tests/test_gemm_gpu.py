@@ -182,3 +182,83 @@ def test_fused_split_outputs_match_split_pass():
                                       P(part2), sp) == 0
     h_ref, l_ref = tf32_split(dpre)
     assert torch.equal(dhi, h_ref) and torch.equal(dlo, l_ref) and torch.equal(part, part2)
+
+
+def test_scan_and_conv_vjp_split_outputs_match_split_pass():
+    """y_lo of vmscan_fwd, dz_lo of vmscan_bwd and dx_lo of
+    vmscan_conv1d_silu_bwd: hi written over the fp32 output and lo beside it
+    equal vmscan_tf32_split of the plain outputs bit for bit, with every other
+    output unchanged (a direction with chunking over L and a permuted order)."""
+    import ctypes
+
+    from mlx_vision_mamba_b200 import _native, directions_for
+    from mlx_vision_mamba_b200.linear import tf32_split
+
+    lib = _native.load()
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(29)
+    b, l, dn = 2, 196, 256
+    sp = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    S = lambda t: _native.Strides(t.stride(0), t.stride(1))  # noqa: E731
+    t = {"u": torch.randn(b, l, dn, generator=gen), "z": torch.randn(b, l, dn, generator=gen),
+         "delta": torch.nn.functional.softplus(torch.randn(b, l, dn, generator=gen) * 0.5 - 3),
+         "A": -torch.rand(dn, 16, generator=gen) * 4, "B": torch.randn(b, l, 16, generator=gen),
+         "C": torch.randn(b, l, 16, generator=gen), "D": torch.randn(dn, generator=gen),
+         "dy": torch.randn(b, l, dn, generator=gen)}
+    t = {k: v.to(dev).contiguous() for k, v in t.items()}
+    dref = ctypes.byref(directions_for(4, (14, 14))[3].to_native())
+    n_ck = lib.vmscan_ckpt_elems(b, l, dn, 16, dref)
+    fws_n = lib.vmscan_fwd_workspace_bytes(b, l, dn, 16, dref)
+    fws = torch.empty(max(fws_n, 16), dtype=torch.uint8, device=dev)
+
+    def fwd(split):
+        y, ylo, ck = torch.empty_like(t["u"]), (torch.empty_like(t["u"]) if split else None), torch.empty(n_ck, device=dev)
+        assert lib.vmscan_fwd(b, l, dn, 16, P(t["u"]), S(t["u"]), P(t["delta"]), S(t["delta"]), P(t["A"]), P(t["B"]),
+                              S(t["B"]), P(t["C"]), S(t["C"]), P(t["D"]), P(t["z"]), S(t["z"]), P(y), S(y), P(ylo),
+                              P(ck), dref, P(fws), fws_n, sp) == 0
+        return y, ylo, ck
+
+    y, _, ck = fwd(False)
+    yhi, ylo, ck2 = fwd(True)
+    h_ref, l_ref = tf32_split(y)
+    assert torch.equal(yhi, h_ref) and torch.equal(ylo, l_ref) and torch.equal(ck, ck2)
+
+    ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, 16, dref, 0)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+
+    def bwd(split):
+        o = {k: torch.empty_like(t["u"]) for k in ("du", "ddelta", "dz")}
+        o["dzlo"] = torch.empty_like(t["u"]) if split else None
+        o["dA"], o["dD"] = torch.empty(dn, 16, device=dev), torch.empty(dn, device=dev)
+        o["dB"], o["dC"] = torch.empty(b, l, 16, device=dev), torch.empty(b, l, 16, device=dev)
+        assert lib.vmscan_bwd(b, l, dn, 16, P(t["u"]), S(t["u"]), P(t["delta"]), S(t["delta"]), P(t["A"]), P(t["B"]),
+                              S(t["B"]), P(t["C"]), S(t["C"]), P(t["D"]), P(t["z"]), S(t["z"]), P(ck), P(t["dy"]),
+                              S(t["dy"]), P(o["du"]), S(o["du"]), P(o["ddelta"]), S(o["ddelta"]), P(o["dA"]),
+                              P(o["dB"]), S(o["dB"]), P(o["dC"]), S(o["dC"]), P(o["dD"]), P(o["dz"]), S(o["dz"]),
+                              P(o["dzlo"]), dref, P(ws), ws_n, sp) == 0
+        return o
+
+    a, s_ = bwd(False), bwd(True)
+    h_ref, l_ref = tf32_split(a["dz"])
+    assert torch.equal(s_["dz"], h_ref) and torch.equal(s_["dzlo"], l_ref)
+    for k in ("du", "ddelta", "dA", "dB", "dC", "dD"):
+        assert torch.equal(a[k], s_[k]), k
+
+    k = 4
+    w = torch.randn(dn, k, 1, generator=gen).to(dev)
+    bias = torch.randn(dn, generator=gen).to(dev)
+    cws_n = lib.vmscan_conv1d_bwd_workspace_bytes(b, l, dn, k)
+    cws = torch.empty(cws_n, dtype=torch.uint8, device=dev)
+
+    def cbwd(split):
+        dx, dxlo = torch.empty_like(t["u"]), (torch.empty_like(t["u"]) if split else None)
+        dw, db = torch.empty_like(w), torch.empty_like(bias)
+        assert lib.vmscan_conv1d_silu_bwd(b, l, dn, k, P(t["u"]), S(t["u"]), P(w), P(bias), P(t["dy"]), S(t["dy"]),
+                                          P(dx), S(dx), P(dxlo), P(dw), P(db), dref, P(cws), cws_n, sp) == 0
+        return dx, dxlo, dw, db
+
+    dx, _, dw, db = cbwd(False)
+    dxhi, dxlo, dw2, db2 = cbwd(True)
+    h_ref, l_ref = tf32_split(dx)
+    assert torch.equal(dxhi, h_ref) and torch.equal(dxlo, l_ref) and torch.equal(dw, dw2) and torch.equal(db, db2)

@@ -148,7 +148,7 @@ def test_bwd_without_checkpoints_recomputes_them():
             S(t["z"]), None if ckpt is None else ckpt.data_ptr(), t["dy"].data_ptr(), S(t["dy"]),
             outs["du"].data_ptr(), S(outs["du"]), outs["ddelta"].data_ptr(), S(outs["ddelta"]),
             outs["dA"].data_ptr(), outs["dB"].data_ptr(), S(outs["dB"]), outs["dC"].data_ptr(), S(outs["dC"]),
-            outs["dD"].data_ptr(), outs["dz"].data_ptr(), S(outs["dz"]), None, ws.data_ptr(), ws_n, stream)
+            outs["dD"].data_ptr(), outs["dz"].data_ptr(), S(outs["dz"]), None, None, ws.data_ptr(), ws_n, stream)
         assert st == 0, lib.vmscan_strerror(st)
         torch.cuda.synchronize()
         return outs
@@ -158,8 +158,8 @@ def test_bwd_without_checkpoints_recomputes_them():
     y = torch.empty_like(t["u"])
     st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
                         t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
-                        t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), ck.data_ptr(), None,
-                        None, 0, stream)
+                        t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), None, ck.data_ptr(),
+                        None, None, 0, stream)
     assert st == 0
     a = bwd(ck)
     r = bwd(None)
@@ -245,7 +245,7 @@ def test_chunked_scan_matches_oracle_and_unchunked(b, l, dn, gated, dirname):
     st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
                         t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
                         t["D"].data_ptr(), t["z"].data_ptr() if gated else None,
-                        S(t["z"]) if gated else _native.Strides(0, 0), y1.data_ptr(), S(y1), None, dptr,
+                        S(t["z"]) if gated else _native.Strides(0, 0), y1.data_ptr(), S(y1), None, None, dptr,
                         None, 0, torch.cuda.current_stream().cuda_stream)
     assert st == 0, lib.vmscan_last_error()
     y2, _ = cuda_vjp(inp, gated, direction)
@@ -286,7 +286,7 @@ def test_abi_rejects_views_that_break_the_tma_rules():
     def fwd(u, su, dt=good, sdt=(l * dn, dn)):
         return lib.vmscan_fwd(b, l, dn, 16, u, S(su), dt.data_ptr(), S(sdt), A.data_ptr(), bc.data_ptr(),
                               S((l * 16, 16)), bc.data_ptr(), S((l * 16, 16)), D.data_ptr(), None, S((0, 0)),
-                              y.data_ptr(), S((l * dn, dn)), None, None, None, 0, stream)
+                              y.data_ptr(), S((l * dn, dn)), None, None, None, None, 0, stream)
 
     assert fwd(good.data_ptr(), (l * dn, dn)) == 0
     wide = torch.randn(b, l, dn + 2, device=dev)  # seq stride 66: not a multiple of 4

@@ -57,8 +57,8 @@ def _fwd_ckpt(lib, t, dptr):
     y = torch.empty_like(t["u"])
     st = lib.vmscan_fwd(b, l, dn, 16, t["u"].data_ptr(), S(t["u"]), t["delta"].data_ptr(), S(t["delta"]),
                         t["A"].data_ptr(), t["B"].data_ptr(), S(t["B"]), t["C"].data_ptr(), S(t["C"]),
-                        t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), ck.data_ptr(), dptr,
-                        None, 0, _stream())
+                        t["D"].data_ptr(), t["z"].data_ptr(), S(t["z"]), y.data_ptr(), S(y), None, ck.data_ptr(),
+                        dptr, None, 0, _stream())
     assert st == 0, lib.vmscan_last_error()
     return ck
 
@@ -69,7 +69,9 @@ def _with_workspace(lib, t, ck, dptr):
     o = _outs(b, l, dn)
     ws_n = lib.vmscan_bwd_workspace_bytes(b, l, dn, 16, dptr, 1 if ck is None else 0)
     ws = torch.empty(ws_n, dtype=torch.uint8, device="cuda")
-    st = lib.vmscan_bwd(*_args(t, o, ck, dptr), ws.data_ptr(), ws_n, _stream())
+    args = _args(t, o, ck, dptr)
+    args.insert(-1, None)  # vmscan_bwd's dz_lo (NULL: dz itself), which the no-alloc entry point does not take
+    st = lib.vmscan_bwd(*args, ws.data_ptr(), ws_n, _stream())
     assert st == 0, lib.vmscan_last_error()
     torch.cuda.synchronize()
     return o
