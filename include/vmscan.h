@@ -365,6 +365,10 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
  * vmscan_gemm_workspace_bytes(M, N, K) bytes of workspace (0: none).
  */
 int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_stream_t stream);
+/* The same split for up to 16 tensors in one launch (x[k], hi[k], lo[k] of
+ * n[k] floats each): a block's weights before its GEMMs. */
+int vmscan_tf32_split_multi(int count, const float* const* x, float* const* hi, float* const* lo,
+                            const int64_t* n, vmscan_stream_t stream);
 int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K,
                        const float* a_hi, const float* a_lo, int64_t lda, int a_mn_major,

@@ -112,6 +112,7 @@ SIGNATURES = {
     "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p]),
     "vmscan_dt_softplus_bias_rows": (_i64, [_i64]),
     "vmscan_tf32_split": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
+    "vmscan_tf32_split_multi": (ctypes.c_int, [ctypes.c_int, _p, _p, _p, _p, _p]),
     "vmscan_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
     "vmscan_gemm_tf32x3": (
         ctypes.c_int,
@@ -150,7 +151,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 # its name so profiler timelines (nsys, ncu --nvtx) group the launches.
 TRACED = (
     "vmscan_fwd", "vmscan_bwd", "vmscan_fwd_bf16", "vmscan_bwd_bf16", "vmscan_bwd_noalloc", "vmscan_conv1d_silu_fwd", "vmscan_conv1d_silu_bwd",
-    "vmscan_dt_softplus_fwd", "vmscan_dt_softplus_bwd", "vmscan_tf32_split", "vmscan_gemm_tf32x3",
+    "vmscan_dt_softplus_fwd", "vmscan_dt_softplus_bwd", "vmscan_tf32_split", "vmscan_tf32_split_multi",
+    "vmscan_gemm_tf32x3",
 )
 
 

@@ -34,7 +34,7 @@ import torch
 
 from . import _native
 from .direction import ScanDirection
-from .linear import gemm_tf32x3, tf32_split
+from .linear import gemm_tf32x3, tf32_split, tf32_split_many
 from .scan import _dir_ptr, _empty_seq, _prepare, _ptr, _strides, _tma_compatible
 
 D_STATE = 16
@@ -77,11 +77,13 @@ def _seq_view(t: torch.Tensor, b: int, l: int) -> torch.Tensor:
     return t.view(b, l, t.shape[-1]) if t.is_contiguous() else t.unflatten(0, (b, l))
 
 
-def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad):
+def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad, wsplits=None):
     """The K branches' forward on their streams: direction k reads its x / z
     column slices of xz and writes its scan output into its slice of y_all
     (with y_lo_all: the output's TF32 hi part into y_all and lo part into
-    y_lo_all).  Returns what the backward needs per branch."""
+    y_lo_all).  wsplits[k]: the TF32 parts of branch k's x_proj and dt_proj
+    weights when the caller split them already.  Returns what the backward
+    needs per branch."""
     lib = _native.load()
     dn, r, ksize, dirs, streams = meta["d_inner"], meta["dt_rank"], meta["d_conv"], meta["dirs"], meta["streams"]
     kb = len(dirs)
@@ -113,7 +115,8 @@ def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad):
                                                      sp), "vmscan_conv1d_silu_fwd")
             if tc:
                 xc_s = (xc_s[0].view(b * l, dn), xc_s[1].view(b * l, dn))
-                xdbc = gemm_tf32x3(xc_s, False, tf32_split(xproj_w.detach().contiguous()), False, b * l, wide, dn)
+                wx_s = wsplits[k][0] if wsplits is not None else tf32_split(xproj_w.detach().contiguous())
+                xdbc = gemm_tf32x3(xc_s, False, wx_s, False, b * l, wide, dn)
             else:
                 xdbc = torch.mm(xc.reshape(b * l, dn), xproj_w.detach().t())  # (B L, r + 2n)
             dw_ = dt_w.detach().contiguous()
@@ -141,7 +144,8 @@ def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad):
                                          _ptr(a), _ptr(bmat), _strides(bmat), _ptr(cmat), _strides(cmat),
                                          _ptr(dsk), _ptr(z), _strides(z), _ptr(y), _strides(y), _ptr(y_lo),
                                          _ptr(ckpt), dptr, _ptr(fws), int(fws_n), sp), "vmscan_fwd")
-            saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s))
+            saved.append((x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s,
+                          wsplits[k] if wsplits is not None else None))
     for s in streams[:kb]:
         cur.wait_stream(s)
     return saved
@@ -163,7 +167,7 @@ def _run_branches_bwd(saved, xproj, meta, dy_all, dxz, dxz_lo):
     cur = torch.cuda.current_stream(dev)
     grads: List[Optional[torch.Tensor]] = [None] * (PARAMS_PER_BLOCK * kb)
     for k in range(kb):
-        x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s = saved[k]
+        x, z, cw, cb, xc, xdbc, dw_, db_, delta, a, bmat, cmat, dsk, ckpt, xc_s, wsp = saved[k]
         xproj_w = xproj[k].detach()
         s = streams[k]
         s.wait_stream(cur)
@@ -206,13 +210,14 @@ def _run_branches_bwd(saved, xproj, meta, dy_all, dxz, dxz_lo):
                 dpre_s = (dpre.view(t, dn), dpre_lo.view(t, dn))
                 xdbc_s = tf32_split(xdbc)
                 # dt_proj input gradient straight into its slice of dx_dbc: dpre W_dt
-                gemm_tf32x3(dpre_s, False, tf32_split(dw_), True, t, r, dn, out=dxdbc[:, :r])
+                wdt_s = wsp[1] if wsp is not None else tf32_split(dw_)
+                gemm_tf32x3(dpre_s, False, wdt_s, True, t, r, dn, out=dxdbc[:, :r])
                 # dt_proj weight gradient dpre^T x_dbc[:, :r] (both read MN-major)
                 g_dt_w = gemm_tf32x3(dpre_s, True, (xdbc_s[0][:, :r], xdbc_s[1][:, :r]), True, dn, r, t)
                 # x_proj: its input gradient lands on du in place (du += dx_dbc W_x)
                 dxdbc_s = tf32_split(dxdbc)
-                gemm_tf32x3(dxdbc_s, False, tf32_split(xproj_w.contiguous()), True, t, dn, wide, out=du2,
-                            accumulate=True)
+                wx_s = wsp[0] if wsp is not None else tf32_split(xproj_w.contiguous())
+                gemm_tf32x3(dxdbc_s, False, wx_s, True, t, dn, wide, out=du2, accumulate=True)
                 g_xproj = gemm_tf32x3(dxdbc_s, True, xc_s, True, wide, dn, t)
             else:
                 dpre2 = dpre.reshape(t, dn)
@@ -287,14 +292,22 @@ class _BlockCoreFn(torch.autograd.Function):
         kb, dn = len(meta["dirs"]), meta["d_inner"]
         t = b * l
         h_s = tf32_split(h.reshape(t, e).contiguous())
-        win_s = tf32_split(w_in.detach().contiguous())
+        # every weight of the block split in one launch: in_proj, out_proj, then
+        # each branch's x_proj and dt_proj
+        ws = [w_in.detach().contiguous(), w_out.detach().contiguous()]
+        if _tc_rows(meta["dt_rank"], dn):
+            for k in range(kb):
+                ws += [params[PARAMS_PER_BLOCK * k + 2].detach().contiguous(),
+                       params[PARAMS_PER_BLOCK * k + 3].detach().contiguous()]
+        splits = tf32_split_many(ws)
+        win_s, wout_s = splits[0], splits[1]
+        wsplits = [(splits[2 + 2 * k], splits[3 + 2 * k]) for k in range(kb)] if len(splits) > 2 else None
         xz = gemm_tf32x3(h_s, False, win_s, False, t, kb * 2 * dn, e).view(b, l, kb * 2 * dn)
         y_hi = _empty_seq(b, l, kb * dn, h.device)
         y_lo = _empty_seq(b, l, kb * dn, h.device)
         need_grad = any(ctx.needs_input_grad)
-        saved = _run_branches_fwd(xz, meta, params, y_hi, y_lo, need_grad)
+        saved = _run_branches_fwd(xz, meta, params, y_hi, y_lo, need_grad, wsplits)
         y_s = (y_hi.view(t, kb * dn), y_lo.view(t, kb * dn))
-        wout_s = tf32_split(w_out.detach().contiguous())
         out = gemm_tf32x3(y_s, False, wout_s, False, t, e, kb * dn).view(b, l, e)
         if need_grad:
             ctx.saved = saved

@@ -988,6 +988,34 @@ int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_st
   return check_launch();
 }
 
+int vmscan_tf32_split_multi(int count, const float* const* x, float* const* hi, float* const* lo, const int64_t* n,
+                            vmscan_stream_t stream) {
+  if (count == 0) return VMSCAN_OK;
+  if (count < 0 || count > kSplitMaxTensors)
+    return fail(VMSCAN_ERR_SHAPE, "tf32_split_multi: %d tensors (1..%d)", count, kSplitMaxTensors);
+  if (x == nullptr || hi == nullptr || lo == nullptr || n == nullptr) return VMSCAN_ERR_NULL;
+  SplitTable t{};
+  int64_t most = 0;
+  for (int k = 0; k < count; ++k) {
+    if (x[k] == nullptr || hi[k] == nullptr || lo[k] == nullptr) return VMSCAN_ERR_NULL;
+    if (n[k] < 0 || n[k] % 4 != 0)
+      return fail(VMSCAN_ERR_SHAPE, "tf32_split_multi: tensor %d has %lld floats (a multiple of 4)", k,
+                  (long long)n[k]);
+    if (!aligned16(x[k]) || !aligned16(hi[k]) || !aligned16(lo[k]))
+      return fail(VMSCAN_ERR_ALIGN, "tf32_split_multi: tensor %d is not 16-byte aligned", k);
+    t.x[k] = reinterpret_cast<const float4*>(x[k]);
+    t.hi[k] = reinterpret_cast<float4*>(hi[k]);
+    t.lo[k] = reinterpret_cast<float4*>(lo[k]);
+    t.n4[k] = n[k] / 4;
+    most = std::max(most, n[k] / 4);
+  }
+  if (most == 0) return VMSCAN_OK;
+  VM_TRY(ensure_context(x[0]));
+  const unsigned bx = unsigned(std::min<int64_t>((most + 255) / 256, int64_t(sm_count()) * 2));
+  tf32_split_multi_kernel<<<dim3(bx, unsigned(count)), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(t);
+  return check_launch();
+}
+
 int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return -VMSCAN_ERR_SHAPE;
   return int64_t(gemm_plan(M, N, K).ws_bytes);

@@ -141,6 +141,30 @@ __global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restri
   }
 }
 
+// Several tensors' hi / lo splits in one launch (the weights of a block):
+// the table travels in the kernel parameters, so the launch can be captured
+// in a CUDA graph.  blockIdx.y picks the tensor.
+constexpr int kSplitMaxTensors = 16;
+struct SplitTable {
+  const float4* x[kSplitMaxTensors];
+  float4* hi[kSplitMaxTensors];
+  float4* lo[kSplitMaxTensors];
+  int64_t n4[kSplitMaxTensors];
+};
+
+__global__ void tf32_split_multi_kernel(const __grid_constant__ SplitTable t) {
+  const int k = blockIdx.y;
+  const float4* __restrict__ x = t.x[k];
+  float4* __restrict__ hi = t.hi[k];
+  float4* __restrict__ lo = t.lo[k];
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < t.n4[k]; i += int64_t(gridDim.x) * blockDim.x) {
+    float4 h, l;
+    split_tf32_4(x[i], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
 // Loads the hi and lo tiles of one operand for k-block kb.  K-major: one box
 // {32 k, rows} at (k0, r0).  MN-major: nbox <= rows/32 boxes {32 mn, 32 k} at
 // (r0 + 32 j, k0), 4 KB apart; boxes that would lie wholly past the operand's

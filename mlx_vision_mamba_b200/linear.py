@@ -41,6 +41,25 @@ def tf32_split(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     return hi, lo
 
 
+def tf32_split_many(xs) -> list:
+    """[(hi, lo)] of several contiguous fp32 CUDA tensors (numel % 4 == 0),
+    split in one launch (up to 16 per launch)."""
+    lib = _native.load()
+    out = [(torch.empty_like(x), torch.empty_like(x)) for x in xs]
+    for a in range(0, len(xs), 16):
+        chunk = list(range(a, min(a + 16, len(xs))))
+        m = len(chunk)
+        P = ctypes.c_void_p * m
+        xp = P(*[xs[i].data_ptr() for i in chunk])
+        hp = P(*[out[i][0].data_ptr() for i in chunk])
+        lp = P(*[out[i][1].data_ptr() for i in chunk])
+        nn = (ctypes.c_int64 * m)(*[xs[i].numel() for i in chunk])
+        _native.check(lib.vmscan_tf32_split_multi(m, ctypes.cast(xp, ctypes.c_void_p), ctypes.cast(hp, ctypes.c_void_p),
+                                                  ctypes.cast(lp, ctypes.c_void_p), ctypes.cast(nn, ctypes.c_void_p),
+                                                  _stream(xs[0].device)), "vmscan_tf32_split_multi")
+    return out
+
+
 def gemm_tf32x3(a: Tuple[torch.Tensor, torch.Tensor], a_mn: bool, b: Tuple[torch.Tensor, torch.Tensor], b_mn: bool,
                 m: int, n: int, k: int, out: Optional[torch.Tensor] = None, accumulate: bool = False) -> torch.Tensor:
     """C (m x n, row-major) = A B^T from split operands: A(i, j) is a[i, j]

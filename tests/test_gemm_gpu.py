@@ -262,3 +262,19 @@ def test_scan_and_conv_vjp_split_outputs_match_split_pass():
     dxhi, dxlo, dw2, db2 = cbwd(True)
     h_ref, l_ref = tf32_split(dx)
     assert torch.equal(dxhi, h_ref) and torch.equal(dxlo, l_ref) and torch.equal(dw, dw2) and torch.equal(db, db2)
+
+
+def test_tf32_split_many_matches_split():
+    """vmscan_tf32_split_multi (one launch, several tensors) equals
+    vmscan_tf32_split per tensor bit for bit."""
+    from mlx_vision_mamba_b200.linear import tf32_split, tf32_split_many
+
+    gen = torch.Generator().manual_seed(31)
+    xs = [torch.randn(n, generator=gen).cuda() for n in (4, 56 * 768, 384 * 6144, 768 * 24, 1000)]
+    many = tf32_split_many(xs)
+    for x, (h, l) in zip(xs, many):
+        h_ref, l_ref = tf32_split(x)
+        assert torch.equal(h, h_ref) and torch.equal(l, l_ref)
+    xs20 = [torch.randn(8 * (i + 1), generator=gen).cuda() for i in range(20)]  # more than one launch's 16
+    for x, (h, l) in zip(xs20, tf32_split_many(xs20)):
+        assert torch.equal(h, tf32_split(x)[0]) and torch.equal(l, tf32_split(x)[1])
