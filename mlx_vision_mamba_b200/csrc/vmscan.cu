@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/vmscan.h"
 #include "vmscan_bwd.cuh"
@@ -339,6 +340,10 @@ int launch_fwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
                  float* ckpt, const ChunkArgs& ch, int nz, const ScanGeom& g, cudaStream_t stream) {
   using Cfg = FwdCfg<kFwdNCW, T>;
   auto kern = scan_fwd_kernel<kFwdNCW, T, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY>;
+  // y as TF32 parts: its own instantiation (fp32 outputs of a main pass only)
+  if constexpr (std::is_same<T, float>::value && STORE_Y && !CARRY) {
+    if (y_lo != nullptr) kern = scan_fwd_kernel<kFwdNCW, T, HAS_Z, SAVE_CK, STORE_Y, REV, CARRY, true>;
+  }
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_fwd_kernel) failed");
   int* st = status_ptr();
@@ -430,6 +435,10 @@ int launch_bwd_t(const CUtensorMap& mu, const CUtensorMap& mdt, const CUtensorMa
     VM_TRY(check_launch());
   }
   auto kern = scan_bwd_kernel<T, HAS_Z, REV>;
+  // dz as TF32 parts: its own instantiation (gated fp32 VJP only)
+  if constexpr (std::is_same<T, float>::value && HAS_Z) {
+    if (o.dz_lo != nullptr) kern = scan_bwd_kernel<T, HAS_Z, REV, true>;
+  }
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(scan_bwd_kernel) failed");
   int sdus = 0, sdts = 0, sdzs = 0;
@@ -842,12 +851,11 @@ int vmscan_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   const dim3 grid(unsigned((channels / 4 + CONV_THREADS - 1) / CONV_THREADS),
                   unsigned((seqlen + CONV_CHUNK - 1) / CONV_CHUNK), unsigned(batch));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (ksize <= 4)
-    conv_silu_fwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
-                                                         sout.seq, out_hi, out_lo, int(channels), int(ksize), g);
-  else
-    conv_silu_fwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch,
-                                                         sout.seq, out_hi, out_lo, int(channels), int(ksize), g);
+  const bool split = out_hi != nullptr;
+  auto kern = ksize <= 4 ? (split ? conv_silu_fwd_kernel<4, true> : conv_silu_fwd_kernel<4, false>)
+                         : (split ? conv_silu_fwd_kernel<8, true> : conv_silu_fwd_kernel<8, false>);
+  kern<<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, out, sout.batch, sout.seq, out_hi, out_lo,
+                                     int(channels), int(ksize), g);
   return check_launch();
 }
 
@@ -880,14 +888,11 @@ int vmscan_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t channels, int6
   const dim3 grid(unsigned((channels / 4 + CONV_THREADS - 1) / CONV_THREADS), unsigned(nchunk), unsigned(batch));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   float* wpart = static_cast<float*>(workspace);
-  if (ksize <= 4)
-    conv_silu_bwd_kernel<4><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
-                                                         sdout.seq, dx, sdx.batch, sdx.seq, dx_lo, wpart,
-                                                         int(channels), int(ksize), g);
-  else
-    conv_silu_bwd_kernel<8><<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch,
-                                                         sdout.seq, dx, sdx.batch, sdx.seq, dx_lo, wpart,
-                                                         int(channels), int(ksize), g);
+  const bool split = dx_lo != nullptr;
+  auto kern = ksize <= 4 ? (split ? conv_silu_bwd_kernel<4, true> : conv_silu_bwd_kernel<4, false>)
+                         : (split ? conv_silu_bwd_kernel<8, true> : conv_silu_bwd_kernel<8, false>);
+  kern<<<grid, CONV_THREADS, 0, s>>>(x, sx.batch, sx.seq, weight, bias, dout, sdout.batch, sdout.seq, dx, sdx.batch,
+                                     sdx.seq, dx_lo, wpart, int(channels), int(ksize), g);
   VM_TRY(check_launch());
   const int n = int(channels * (ksize + 1));
   const int nrows = int(batch) * nchunk;

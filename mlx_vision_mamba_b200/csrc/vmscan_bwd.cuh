@@ -242,7 +242,7 @@ struct FwdCarry {
 
 // One box of the VJP (nv rows).  The loops are kept rolled (pairs of steps):
 // a fully unrolled box overflows the instruction cache and runs slower.
-template <typename T, bool HAS_Z, bool REV>
+template <typename T, bool HAS_Z, bool REV, bool SPLIT>
 __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float* __restrict__ part, uint32_t taddr,
                                         int nv, int warp, int lane, int c0l, const PairLane& pl, bool has_ck,
                                         bool v0, bool v1, float Down, T* du_b, T* dt_b, T* dz_b, float* dzlo_b,
@@ -312,7 +312,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
     const float sig = __fdividef(1.0f, 1.0f + ex2_approx(-kLog2e * zz));
     const float dzv = dyv * ypre * sig * fmaf(zz, 1.0f - sig, 1.0f);
     const int64_t off = int64_t(tok[k.r]) * sdzs;
-    if (dzlo_b != nullptr) {
+    if constexpr (SPLIT) {
       // dz as TF32 parts (hi into dz, lo into dz_lo) for the in_proj gradient GEMMs
       float hi, lo;
       split_tf32(dzv, hi, lo);
@@ -402,7 +402,10 @@ struct BwdChunkArgs {
   const float* p_in;  // (batch, nchunks, d_inner, 16); row nchunks-1 unused
 };
 
-template <typename T, bool HAS_Z, bool REV>
+// SPLIT: write dz as TF32 parts (hi into dz, lo into dz_lo) for the in_proj
+// gradient GEMMs; a separate instantiation, so the plain output path carries no
+// per-step test for it.
+template <typename T, bool HAS_Z, bool REV, bool SPLIT = false>
 __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     scan_bwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_dy,
@@ -531,7 +534,8 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
   T* du_b = du_out + b * sdub + own;
   T* dt_b = ddt_out + b * sdtb + own;
   T* dz_b = HAS_Z ? dz_out + b * sdzb + own : nullptr;
-  float* dzlo_b = (HAS_Z && Cfg::F32 && dz_lo != nullptr) ? dz_lo + b * sdzb + own : nullptr;
+  static_assert(!SPLIT || (HAS_Z && Cfg::F32), "TF32 parts of an fp32 dz");
+  float* dzlo_b = SPLIT ? dz_lo + b * sdzb + own : nullptr;
   bool alive = true;
 
   for (int i = 0; i < nbx; ++i) {
@@ -548,7 +552,7 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     const BwdStage<T> S(smb + st * Cfg::STAGE_B);
     const int nv = S.tok[TMAX];
     if (alive)
-      bwd_box<T, HAS_Z, REV>(L, S, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
+      bwd_box<T, HAS_Z, REV, SPLIT>(L, S, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,
                           dzlo_b, sdus, sdts, sdzs, ev);
     // dy' was written into the stage: order those generic-proxy writes before
     // the TMA load that will refill the stage

@@ -47,7 +47,7 @@ __device__ __forceinline__ float dsilu_f(float pre) {
 }
 
 // Window KW (4 or 8) >= K; the K real taps sit at the newest end of the window.
-template <int KW>
+template <int KW, bool SPLIT>
 __global__ void __launch_bounds__(CONV_THREADS)
     conv_silu_fwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
                          const float* __restrict__ bias, float* __restrict__ out, int64_t sob, int64_t sos,
@@ -107,8 +107,9 @@ __global__ void __launch_bounds__(CONV_THREADS)
           o.z = silu_f(acc.z);
           o.w = silu_f(acc.w);
           *reinterpret_cast<float4*>(ob + tk * sos) = o;
-          if (out_hi != nullptr) {
-            // TF32 parts for the x_proj GEMM, same layout as out
+          if constexpr (SPLIT) {
+            // TF32 parts for the x_proj GEMM, same layout as out (a separate
+            // instantiation: the plain path carries no per-position test)
             float4 hi, lo;
             split_tf32_4(o, hi, lo);
             const int64_t off = b * sob + c4 * 4 + tk * sos;
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(CONV_THREADS)
 // and per-thread partial sums of dw[k] = sum_p dpre[p] x[p-K+1+k] and
 // dbias = sum_p dpre[p] over the chunk, written slot-major to
 // wpart[b][chunk][slot][c] (slot k < K: dw[k], slot KMAX: dbias) as float4.
-template <int KW>
+template <int KW, bool SPLIT>
 __global__ void __launch_bounds__(CONV_THREADS)
     conv_silu_bwd_kernel(const float* __restrict__ x, int64_t sxb, int64_t sxs, const float* __restrict__ w,
                          const float* __restrict__ bias, const float* __restrict__ dout, int64_t sdb, int64_t sds,
@@ -236,8 +237,9 @@ __global__ void __launch_bounds__(CONV_THREADS)
             acc.w = fmaf(wr[j][3], dpw[j].w, acc.w);
           }
           const int64_t tkp = tok[t - (K - 1)];
-          if (dx_lo != nullptr) {
+          if constexpr (SPLIT) {
             // the TF32 parts of dx (for the in_proj gradient GEMMs) instead of dx
+            // (a separate instantiation: the plain path carries no per-position test)
             float4 hi, lo;
             split_tf32_4(acc, hi, lo);
             *reinterpret_cast<float4*>(dxb + tkp * sxgs) = hi;

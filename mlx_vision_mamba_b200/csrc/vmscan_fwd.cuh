@@ -61,7 +61,10 @@ struct ChunkArgs {
   float* carry_s;           // (batch, nchunks, d_inner)
 };
 
-template <int NCW, typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY = false>
+// SPLIT: write y as TF32 parts (hi into y, lo into y_lo) for the out_proj
+// GEMM; a separate instantiation, so the plain output path carries no per-step
+// test for it.
+template <int NCW, typename T, bool HAS_Z, bool SAVE_CK, bool STORE_Y, bool REV, bool CARRY = false, bool SPLIT = false>
 __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
     scan_fwd_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_dt,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_B,
@@ -72,6 +75,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
   using Cfg = FwdCfg<NCW, T>;
   constexpr int DT = Cfg::DT, NST = Cfg::NST;
   static_assert(!CARRY || (!HAS_Z && !SAVE_CK && !STORE_Y), "a carry pass stores nothing but the carries");
+  static_assert(!SPLIT || (STORE_Y && sizeof(T) == 4), "TF32 parts of an fp32 output");
   constexpr bool LOAD_Z = HAS_Z && STORE_Y;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smb = reinterpret_cast<unsigned char*>(smem_align1024(smem_raw));
@@ -168,8 +172,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
   const int own = c0l + pl.hb;
   const float Down = ev ? Dskip[d0 + own] : 0.f;
   T* ybase = STORE_Y ? y + b * syb + d0 + own : nullptr;
-  // fp32 output as TF32 parts (hi into y, lo into y_lo) for the out_proj GEMM
-  float* ylo_base = (STORE_Y && Cfg::ES == 4 && y_lo != nullptr) ? y_lo + b * syb + d0 + own : nullptr;
+  float* ylo_base = SPLIT ? y_lo + b * syb + d0 + own : nullptr;
   bool alive = true;
 
   struct Carry {
@@ -228,7 +231,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
         float yy = fmaf(k.uo, Down, ys);
         if (HAS_Z) yy *= silu_f(ld_one(sz + k.r * DT + own));
         const int64_t off = int64_t(tok[k.r]) * sys;
-        if (ylo_base != nullptr) {
+        if constexpr (SPLIT) {
           float hi, lo;
           split_tf32(yy, hi, lo);
           stg_if_t(ybase + off, hi, ev);
