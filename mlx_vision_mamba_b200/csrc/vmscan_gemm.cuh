@@ -41,14 +41,17 @@ constexpr int GM_EPI_WARPS = 8;
 // which with the two correction buffers fill TMEM), and k-blocks per
 // promotion chain.  Measured on B200 inside CUDA graphs at the VisionMamba-2D
 // shapes: chains of 2 k-blocks run the 128-column GEMMs 9-14 % faster than
-// chains of 1 (half the MMA / epilogue hand-overs) at a rounding bias of
-// about -1.4e-7 of the output RMS, still below PyTorch's fp32 GEMM's
-// random error; 4 narrow buffers instead of 2 change little.
+// chains of 1 (half the MMA / epilogue hand-overs), chains of 3 another 2-7 %
+// (training step 21.66 -> 21.07 ms; 4 gain nothing more).  RMS error of the
+// output RMS on N(0,1) operands at K = 384 / 3072 / 12544: chains of 2
+// 2.0 / 2.3 / 2.7e-7, of 3 2.7 / 2.9 / 3.1e-7, of 4 3.4 / 3.5 / 3.6e-7,
+// against PyTorch's fp32 GEMM 3.5 / 9.9 / 20e-7; 4 narrow buffers instead of
+// 2 change little.
 #ifndef VMSCAN_GEMM_NB_NARROW
 #define VMSCAN_GEMM_NB_NARROW 4
 #endif
 #ifndef VMSCAN_GEMM_PK
-#define VMSCAN_GEMM_PK 2
+#define VMSCAN_GEMM_PK 3
 #endif
 
 template <int BN>
