@@ -1072,9 +1072,6 @@ def run_encoder(dev, rank, world, which, mode, steps, warmup, barrier):
     side = torch.cuda.Stream(dev)
     if mode == "dp":
         a, b = train.shard(cfg.global_batch, rank, world)
-    if batch is not None:
-        assert world == 1 or single, "batch overrides apply to single-GPU runs"
-        a, b = 0, int(batch)
         with torch.cuda.stream(side):
             model = train.wrap_data_parallel(train.build_encoder(cfg, dev, seed=0), dev)
         batch, seed = b - a, 100 + rank
