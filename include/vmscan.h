@@ -344,6 +344,14 @@ int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner,
 int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
 
 /*
+ * Column sums of a row-major (rows x cols) fp32 array, added in a fixed
+ * order (deterministic): out[c] = sum_r part[r * cols + c].  Finishes dbias of
+ * vmscan_dt_softplus_bwd from its dbias_part rows (the reference's dt_proj
+ * bias gradient, mamba_block.py:180 through nn.Linear's autograd).
+ */
+int vmscan_sum_rows(int64_t rows, int64_t cols, const float* part, float* out, vmscan_stream_t stream);
+
+/*
  * Projection GEMMs of the block on the tensor cores with fp32 accuracy
  * (in_proj and out_proj, mamba_block.py:165,191, the out_proj over the
  * concatenated directions performing the sum of :562-566, and their input

@@ -93,9 +93,12 @@ def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad, wsplits=None
     wide = r + 2 * n
     tc = _tc_rows(r, dn)
     cur = torch.cuda.current_stream(dev)
+    # A = -exp(A_log) of every branch in two multi-tensor launches
+    a_all = torch._foreach_exp([params[PARAMS_PER_BLOCK * k + 5].detach() for k in range(kb)])
+    torch._foreach_neg_(a_all)
     saved = []
     for k in range(kb):
-        conv_w, conv_b, xproj_w, dt_w, dt_b, a_log, d_skip = params[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)]
+        conv_w, conv_b, xproj_w, dt_w, dt_b, _, d_skip = params[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)]
         s = streams[k]
         s.wait_stream(cur)
         with torch.cuda.stream(s):
@@ -124,7 +127,7 @@ def _run_branches_fwd(xz, meta, params, y_all, y_lo_all, need_grad, wsplits=None
             delta = _empty_seq(b, l, dn, dev)
             _native.check(lib.vmscan_dt_softplus_fwd(b * l, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
                                                      _ptr(delta), delta.stride(1), sp), "vmscan_dt_softplus_fwd")
-            a = -torch.exp(a_log.detach())
+            a = a_all[k]
             bmat = _prepare(_seq_view(xdbc[:, r:r + n], b, l))
             cmat = _prepare(_seq_view(xdbc[:, r + n:], b, l))
             dsk = d_skip.detach().contiguous()
@@ -204,7 +207,8 @@ def _run_branches_bwd(saved, xproj, meta, dy_all, dxz, dxz_lo):
             _native.check(lib.vmscan_dt_softplus_bwd(t, r, dn, _ptr(xdbc), wide, _ptr(dw_), _ptr(db_),
                                                      _ptr(ddelta), ddelta.stride(1), _ptr(dpre), dpre.stride(1),
                                                      _ptr(dpre_lo), _ptr(part), sp), "vmscan_dt_softplus_bwd")
-            g_dt_b = part.sum(0)
+            g_dt_b = torch.empty((dn,), dtype=torch.float32, device=dev)
+            _native.check(lib.vmscan_sum_rows(part.shape[0], dn, _ptr(part), _ptr(g_dt_b), sp), "vmscan_sum_rows")
             du2 = du.view(t, dn)
             if tc:
                 dpre_s = (dpre.view(t, dn), dpre_lo.view(t, dn))
@@ -239,12 +243,14 @@ def _run_branches_bwd(saved, xproj, meta, dy_all, dxz, dxz_lo):
                                                      _ptr(du), _strides(du), _ptr(dx), _strides(dx), _ptr(dx_lo),
                                                      _ptr(g_cw), _ptr(g_cb), dptr, _ptr(cws), cws.numel(), sp),
                           "vmscan_conv1d_silu_bwd")
-            # A = -exp(A_log): dA_log = dA * A
-            g_alog = dA * a
-            grads[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)] = [g_cw, g_cb, g_xproj, g_dt_w, g_dt_b, g_alog,
+            grads[PARAMS_PER_BLOCK * k:PARAMS_PER_BLOCK * (k + 1)] = [g_cw, g_cb, g_xproj, g_dt_w, g_dt_b, dA,
                                                                       dD]
     for s in streams[:kb]:
         cur.wait_stream(s)
+    # A = -exp(A_log): dA_log = dA * A, every branch in one multi-tensor launch
+    g_alogs = torch._foreach_mul([grads[PARAMS_PER_BLOCK * k + 5] for k in range(kb)], [sv[9] for sv in saved])
+    for k in range(kb):
+        grads[PARAMS_PER_BLOCK * k + 5] = g_alogs[k]
     return grads
 
 

@@ -827,6 +827,16 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok) {
   return (ntok + DTP_TOKENS - 1) / DTP_TOKENS;
 }
 
+int vmscan_sum_rows(int64_t rows, int64_t cols, const float* part, float* out, vmscan_stream_t stream) {
+  if (rows <= 0 || cols <= 0 || rows > INT32_MAX || cols > INT32_MAX) return VMSCAN_ERR_SHAPE;
+  if (part == nullptr || out == nullptr) return VMSCAN_ERR_NULL;
+  VM_TRY(ensure_context(part));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  sum_rows_kernel<<<unsigned((cols + kSumRowsCols - 1) / kSumRowsCols), kSumRowsCols * kSumRowsGroups, 0, s>>>(
+      part, out, int(rows), int(cols));
+  return check_launch();
+}
+
 int vmscan_dt_softplus_bwd(int64_t ntok, int64_t dt_rank, int64_t d_inner, const float* x, int64_t ldx,
                            const float* weight, const float* bias, const float* ddelta, int64_t ld_ddelta,
                            float* dpre, int64_t ld_dpre, float* dpre_lo, float* dbias_part, vmscan_stream_t stream) {

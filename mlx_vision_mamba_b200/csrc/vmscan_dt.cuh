@@ -159,4 +159,38 @@ __global__ void __launch_bounds__(DTP_THREADS)
   }
 }
 
+// Column sums of a row-major (rows x cols) array: out[c] = sum_r part[r *
+// cols + c] (the dt_proj VJP's dbias partials, one row per 64-token CTA).  A
+// CTA of 256 threads owns 32 columns; thread (g, c) sums rows g, g + 8, g +
+// 16, ... of column c with all its loads in flight at once, then the 8 group
+// sums of a column are added in group order: a fixed order, so the result is
+// deterministic.
+constexpr int kSumRowsCols = 32, kSumRowsGroups = 8;
+__global__ void __launch_bounds__(kSumRowsCols * kSumRowsGroups)
+    sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int rows, int cols) {
+  __shared__ float gs[kSumRowsGroups][kSumRowsCols];
+  const int cl = threadIdx.x % kSumRowsCols, grp = threadIdx.x / kSumRowsCols;
+  const int c = blockIdx.x * kSumRowsCols + cl;
+  float acc = 0.f;
+  if (c < cols) {
+    int r = grp;
+    for (; r + 7 * kSumRowsGroups < rows; r += 8 * kSumRowsGroups) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = part[int64_t(r + i * kSumRowsGroups) * cols + c];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += v[i];
+    }
+    for (; r < rows; r += kSumRowsGroups) acc += part[int64_t(r) * cols + c];
+  }
+  gs[grp][cl] = acc;
+  __syncthreads();
+  if (grp == 0 && c < cols) {
+    float t = gs[0][cl];
+#pragma unroll
+    for (int g = 1; g < kSumRowsGroups; ++g) t += gs[g][cl];
+    out[c] = t;
+  }
+}
+
 }  // namespace vmscan

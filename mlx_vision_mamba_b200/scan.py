@@ -360,7 +360,7 @@ class _DtSoftplusFn(torch.autograd.Function):
         g_in = _token_rows(ddelta)
         dpre = _empty_seq(b, l, dn, x_.device)
         # dbias: the kernel sums dpre over each group of tokens it handles;
-        # the rows of those partials are added here (a small reduction)
+        # vmscan_sum_rows adds the rows of those partials in a fixed order
         part = torch.empty((lib.vmscan_dt_softplus_bias_rows(b * l), dn), dtype=torch.float32, device=x_.device)
         st = lib.vmscan_dt_softplus_bwd(b * l, r, dn, _ptr(x_), x_.stride(1), _ptr(w_), _ptr(b_), _ptr(g_in),
                                         g_in.stride(1), _ptr(dpre), dpre.stride(1), None, _ptr(part), _stream(x_))
@@ -368,7 +368,8 @@ class _DtSoftplusFn(torch.autograd.Function):
         g2 = dpre.reshape(b * l, dn)
         dx = (g2 @ w_).reshape(b, l, r)
         dw = g2.t() @ x_.reshape(b * l, r)
-        db = part.sum(0)
+        db = torch.empty((dn,), dtype=torch.float32, device=x_.device)
+        _native.check(lib.vmscan_sum_rows(part.shape[0], dn, _ptr(part), _ptr(db), _stream(x_)), "vmscan_sum_rows")
         return dx, dw, db
 
 
