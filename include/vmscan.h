@@ -352,6 +352,26 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok);
 int vmscan_sum_rows(int64_t rows, int64_t cols, const float* part, float* out, vmscan_stream_t stream);
 
 /*
+ * LayerNorm over the last dimension of a (rows x dim) fp32 array (row strides
+ * ld*, multiples of 4; 16-byte aligned x, y, dy, dx, weight, bias), as MLX's
+ * nn.LayerNorm in the reference's blocks and encoder (mamba_block.py:201,222,
+ * 401, vision_mamba.py:192): y = (x - mean) rstd weight + bias, rstd = 1 /
+ * sqrt(var + eps) with the biased variance.  dim % 4 == 0 and dim <= 1024
+ * (VMSCAN_ERR_SHAPE otherwise).  The forward also writes each row's mean and
+ * rstd (rows floats each) for the VJP.  The VJP writes dx and the weight /
+ * bias gradients (summed over rows in a fixed order: deterministic), with
+ * vmscan_layernorm_bwd_workspace_bytes(rows, dim) bytes of workspace.
+ */
+int vmscan_layernorm_fwd(int64_t rows, int64_t dim, const float* x, int64_t ldx, const float* weight,
+                         const float* bias, float eps, float* y, int64_t ldy, float* mean, float* rstd,
+                         vmscan_stream_t stream);
+int64_t vmscan_layernorm_bwd_workspace_bytes(int64_t rows, int64_t dim);
+int vmscan_layernorm_bwd(int64_t rows, int64_t dim, const float* x, int64_t ldx, const float* weight,
+                         const float* mean, const float* rstd, const float* dy, int64_t lddy, float* dx,
+                         int64_t lddx, float* dweight, float* dbias, void* workspace, size_t workspace_bytes,
+                         vmscan_stream_t stream);
+
+/*
  * Projection GEMMs of the block on the tensor cores with fp32 accuracy
  * (in_proj and out_proj, mamba_block.py:165,191, the out_proj over the
  * concatenated directions performing the sum of :562-566, and their input

@@ -112,6 +112,10 @@ SIGNATURES = {
     "vmscan_dt_softplus_bwd": (ctypes.c_int, [_i64, _i64, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p]),
     "vmscan_dt_softplus_bias_rows": (_i64, [_i64]),
     "vmscan_sum_rows": (ctypes.c_int, [_i64, _i64, _p, _p, _p]),
+    "vmscan_layernorm_fwd": (ctypes.c_int, [_i64, _i64, _p, _i64, _p, _p, ctypes.c_float, _p, _i64, _p, _p, _p]),
+    "vmscan_layernorm_bwd_workspace_bytes": (_i64, [_i64, _i64]),
+    "vmscan_layernorm_bwd": (ctypes.c_int, [_i64, _i64, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p,
+                                            ctypes.c_size_t, _p]),
     "vmscan_tf32_split": (ctypes.c_int, [_i64, _p, _p, _p, _p]),
     "vmscan_tf32_split_multi": (ctypes.c_int, [ctypes.c_int, _p, _p, _p, _p, _p]),
     "vmscan_gemm_workspace_bytes": (_i64, [_i64, _i64, _i64]),
@@ -153,7 +157,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 TRACED = (
     "vmscan_fwd", "vmscan_bwd", "vmscan_fwd_bf16", "vmscan_bwd_bf16", "vmscan_bwd_noalloc", "vmscan_conv1d_silu_fwd", "vmscan_conv1d_silu_bwd",
     "vmscan_dt_softplus_fwd", "vmscan_dt_softplus_bwd", "vmscan_tf32_split", "vmscan_tf32_split_multi",
-    "vmscan_gemm_tf32x3", "vmscan_sum_rows",
+    "vmscan_gemm_tf32x3", "vmscan_sum_rows", "vmscan_layernorm_fwd", "vmscan_layernorm_bwd",
 )
 
 

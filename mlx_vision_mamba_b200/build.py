@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libvmscan.so")
 SOURCES = ["vmscan.cu"]
 DEPS = ["vmscan.cu", "vmscan_common.cuh", "vmscan_fwd.cuh", "vmscan_bwd.cuh", "vmscan_conv.cuh", "vmscan_dt.cuh",
-        "vmscan_gemm.cuh"]
+        "vmscan_gemm.cuh", "vmscan_norm.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

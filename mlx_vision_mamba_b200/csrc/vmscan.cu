@@ -21,6 +21,7 @@
 #include "vmscan_dt.cuh"
 #include "vmscan_fwd.cuh"
 #include "vmscan_gemm.cuh"
+#include "vmscan_norm.cuh"
 
 using namespace vmscan;
 
@@ -714,6 +715,38 @@ __global__ void wait_timeout_selftest_kernel(uint32_t tries, int* status) {
   if (threadIdx.x == 0) (void)mbar_wait(&bar, 0u, &abort_flag, status, tries);
 }
 
+namespace {
+
+int ln_chunks(int64_t dim) { return int((dim / 4 + 31) / 32); }
+
+bool ln_shape_ok(int64_t rows, int64_t dim) {
+  return rows > 0 && rows <= INT32_MAX && dim > 0 && dim % 4 == 0 && dim <= LN_MAX_DIM;
+}
+
+template <int NC>
+void launch_ln_fwd(int rows, int dim, const float* x, int64_t ldx, const float* w, const float* b, float eps,
+                   float* y, int64_t ldy, float* mean, float* rstd, cudaStream_t s) {
+  layernorm_fwd_kernel<NC><<<unsigned((rows + LN_WARPS - 1) / LN_WARPS), LN_WARPS * 32, 0, s>>>(
+      x, ldx, w, b, eps, y, ldy, mean, rstd, rows, dim);
+}
+
+template <int NC>
+int launch_ln_bwd(int rows, int dim, const float* x, int64_t ldx, const float* w, const float* mean,
+                  const float* rstd, const float* dy, int64_t lddy, float* dx, int64_t lddx, float* part,
+                  cudaStream_t s) {
+  const int per = LN_WARPS * LN_ROWS_PER_WARP;
+  const size_t smem = size_t(LN_WARPS) * 2 * size_t(dim) * 4;
+  auto kern = layernorm_bwd_kernel<NC>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(layernorm_bwd_kernel) failed");
+  kern<<<unsigned((rows + per - 1) / per), LN_WARPS * 32, smem, s>>>(x, ldx, w, mean, rstd, dy, lddy, dx, lddx,
+                                                                    part, rows, dim);
+  return VMSCAN_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int vmscan_version(void) { return 100; }
@@ -827,13 +860,74 @@ int64_t vmscan_dt_softplus_bias_rows(int64_t ntok) {
   return (ntok + DTP_TOKENS - 1) / DTP_TOKENS;
 }
 
+
+int vmscan_layernorm_fwd(int64_t rows, int64_t dim, const float* x, int64_t ldx, const float* weight,
+                         const float* bias, float eps, float* y, int64_t ldy, float* mean, float* rstd,
+                         vmscan_stream_t stream) {
+  if (!ln_shape_ok(rows, dim) || ldx < dim || ldy < dim) return VMSCAN_ERR_SHAPE;
+  if (x == nullptr || weight == nullptr || bias == nullptr || y == nullptr || mean == nullptr || rstd == nullptr)
+    return VMSCAN_ERR_NULL;
+  if (!aligned16(x) || !aligned16(y) || !aligned16(weight) || !aligned16(bias) || ldx % 4 || ldy % 4)
+    return VMSCAN_ERR_ALIGN;
+  VM_TRY(ensure_context(x));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int r = int(rows), d = int(dim);
+  switch (ln_chunks(dim)) {
+    case 1: launch_ln_fwd<1>(r, d, x, ldx, weight, bias, eps, y, ldy, mean, rstd, s); break;
+    case 2: launch_ln_fwd<2>(r, d, x, ldx, weight, bias, eps, y, ldy, mean, rstd, s); break;
+    case 3: launch_ln_fwd<3>(r, d, x, ldx, weight, bias, eps, y, ldy, mean, rstd, s); break;
+    case 4: launch_ln_fwd<4>(r, d, x, ldx, weight, bias, eps, y, ldy, mean, rstd, s); break;
+    default: launch_ln_fwd<8>(r, d, x, ldx, weight, bias, eps, y, ldy, mean, rstd, s); break;
+  }
+  return check_launch();
+}
+
+int64_t vmscan_layernorm_bwd_workspace_bytes(int64_t rows, int64_t dim) {
+  if (!ln_shape_ok(rows, dim)) return -VMSCAN_ERR_SHAPE;
+  const int64_t per = LN_WARPS * LN_ROWS_PER_WARP;
+  return int64_t(align256(size_t((rows + per - 1) / per) * 2 * size_t(dim) * 4));
+}
+
+int vmscan_layernorm_bwd(int64_t rows, int64_t dim, const float* x, int64_t ldx, const float* weight,
+                         const float* mean, const float* rstd, const float* dy, int64_t lddy, float* dx,
+                         int64_t lddx, float* dweight, float* dbias, void* workspace, size_t workspace_bytes,
+                         vmscan_stream_t stream) {
+  if (!ln_shape_ok(rows, dim) || ldx < dim || lddy < dim || lddx < dim) return VMSCAN_ERR_SHAPE;
+  if (x == nullptr || weight == nullptr || mean == nullptr || rstd == nullptr || dy == nullptr || dx == nullptr ||
+      dweight == nullptr || dbias == nullptr)
+    return VMSCAN_ERR_NULL;
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(weight) || ldx % 4 || lddy % 4 || lddx % 4)
+    return VMSCAN_ERR_ALIGN;
+  const int64_t need = vmscan_layernorm_bwd_workspace_bytes(rows, dim);
+  if (workspace == nullptr || int64_t(workspace_bytes) < need || !aligned16(workspace)) return VMSCAN_ERR_WORKSPACE;
+  VM_TRY(ensure_context(x));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int r = int(rows), d = int(dim);
+  float* part = static_cast<float*>(workspace);
+  switch (ln_chunks(dim)) {
+    case 1: VM_TRY(launch_ln_bwd<1>(r, d, x, ldx, weight, mean, rstd, dy, lddy, dx, lddx, part, s)); break;
+    case 2: VM_TRY(launch_ln_bwd<2>(r, d, x, ldx, weight, mean, rstd, dy, lddy, dx, lddx, part, s)); break;
+    case 3: VM_TRY(launch_ln_bwd<3>(r, d, x, ldx, weight, mean, rstd, dy, lddy, dx, lddx, part, s)); break;
+    case 4: VM_TRY(launch_ln_bwd<4>(r, d, x, ldx, weight, mean, rstd, dy, lddy, dx, lddx, part, s)); break;
+    default: VM_TRY(launch_ln_bwd<8>(r, d, x, ldx, weight, mean, rstd, dy, lddy, dx, lddx, part, s)); break;
+  }
+  VM_TRY(check_launch());
+  const int64_t per = LN_WARPS * LN_ROWS_PER_WARP;
+  const int prow = int((rows + per - 1) / per);
+  const dim3 g(unsigned((dim + kSumRowsCols - 1) / kSumRowsCols));
+  sum_rows_kernel<<<g, kSumRowsCols * kSumRowsGroups, 0, s>>>(part, dweight, prow, d, 2 * dim);
+  VM_TRY(check_launch());
+  sum_rows_kernel<<<g, kSumRowsCols * kSumRowsGroups, 0, s>>>(part + dim, dbias, prow, d, 2 * dim);
+  return check_launch();
+}
+
 int vmscan_sum_rows(int64_t rows, int64_t cols, const float* part, float* out, vmscan_stream_t stream) {
   if (rows <= 0 || cols <= 0 || rows > INT32_MAX || cols > INT32_MAX) return VMSCAN_ERR_SHAPE;
   if (part == nullptr || out == nullptr) return VMSCAN_ERR_NULL;
   VM_TRY(ensure_context(part));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   sum_rows_kernel<<<unsigned((cols + kSumRowsCols - 1) / kSumRowsCols), kSumRowsCols * kSumRowsGroups, 0, s>>>(
-      part, out, int(rows), int(cols));
+      part, out, int(rows), int(cols), cols);
   return check_launch();
 }
 

@@ -159,15 +159,16 @@ __global__ void __launch_bounds__(DTP_THREADS)
   }
 }
 
-// Column sums of a row-major (rows x cols) array: out[c] = sum_r part[r *
-// cols + c] (the dt_proj VJP's dbias partials, one row per 64-token CTA).  A
-// CTA of 256 threads owns 32 columns; thread (g, c) sums rows g, g + 8, g +
-// 16, ... of column c with all its loads in flight at once, then the 8 group
-// sums of a column are added in group order: a fixed order, so the result is
+// Column sums of a row-major (rows x cols, row stride ld) array: out[c] =
+// sum_r part[r * ld + c] (the dt_proj VJP's dbias partials, one row per
+// 64-token CTA; the LayerNorm VJP's dw / db partials).  A
+// CTA of 1024 threads owns 32 columns; thread (g, c) sums rows g, g + 32, g +
+// 64, ... of column c with 8 loads in flight at a time, then the 32 group sums
+// of a column are added in group order: a fixed order, so the result is
 // deterministic.
-constexpr int kSumRowsCols = 32, kSumRowsGroups = 8;
+constexpr int kSumRowsCols = 32, kSumRowsGroups = 32;
 __global__ void __launch_bounds__(kSumRowsCols * kSumRowsGroups)
-    sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int rows, int cols) {
+    sum_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int rows, int cols, int64_t ld) {
   __shared__ float gs[kSumRowsGroups][kSumRowsCols];
   const int cl = threadIdx.x % kSumRowsCols, grp = threadIdx.x / kSumRowsCols;
   const int c = blockIdx.x * kSumRowsCols + cl;
@@ -177,11 +178,11 @@ __global__ void __launch_bounds__(kSumRowsCols * kSumRowsGroups)
     for (; r + 7 * kSumRowsGroups < rows; r += 8 * kSumRowsGroups) {
       float v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = part[int64_t(r + i * kSumRowsGroups) * cols + c];
+      for (int i = 0; i < 8; ++i) v[i] = part[int64_t(r + i * kSumRowsGroups) * ld + c];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc += v[i];
     }
-    for (; r < rows; r += kSumRowsGroups) acc += part[int64_t(r) * cols + c];
+    for (; r < rows; r += kSumRowsGroups) acc += part[int64_t(r) * ld + c];
   }
   gs[grp][cl] = acc;
   __syncthreads();

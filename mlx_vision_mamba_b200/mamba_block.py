@@ -28,6 +28,7 @@ import torch.nn.functional as F
 from .direction import BACKWARD, ScanDirection, directions_for
 from .branches import block_core_forward, block_core_ok, branches_forward
 from .linear import linear_tc, supported as _tc_supported
+from .norm import layer_norm_cuda as _layer_norm_cuda, supported as _ln_supported
 from .scan import conv1d_silu_cuda, dt_softplus_cuda, selective_scan_cuda
 
 GPU_SCAN_MODES = ("cuda_fused", "metal_fused", "metal_train", "metal")
@@ -50,7 +51,16 @@ class Linear(nn.Linear):
 
 
 class LayerNorm(nn.LayerNorm):
-    """MLX nn.LayerNorm defaults: eps 1e-5, weight 1, bias 0."""
+    """MLX nn.LayerNorm defaults: eps 1e-5, weight 1, bias 0.
+
+    CUDA fp32 inputs whose last dimension is a multiple of 4 and at most 1024
+    (the encoders' 384) run forward and VJP in the library's LayerNorm kernels
+    (`norm.layer_norm_cuda`); other inputs use PyTorch's layer_norm."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if len(self.normalized_shape) == 1 and _ln_supported(x, self.weight, self.bias):
+            return _layer_norm_cuda(x, self.weight, self.bias, self.eps)
+        return super().forward(x)
 
 
 class DepthwiseConv1d(nn.Module):
