@@ -69,7 +69,10 @@ struct BwdCfg {
   static constexpr int PART_F = 2 * TMAX * NCW * 32;  // double-buffered per-warp dB/dC partials (fp32)
   static constexpr int OFF_PART_B = NST * STAGE_B;
   static constexpr int OFF_BAR_B = OFF_PART_B + PART_F * 4;
-  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR_B) + 2 * NST * 8 + 32 + 1024;
+  // 16-bit T: each warp's fp32 copy of the box's B and C tiles, after the barriers
+  static constexpr int OFF_BCF_B = OFF_BAR_B + 64;
+  static constexpr int BCF_B = F32 ? 0 : NCW * 2 * BCT * 4;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BCF_B) + BCF_B + 1024;
 };
 
 // Typed views of one VJP stage.
@@ -82,6 +85,8 @@ struct BwdStage {
   float* dyp;  // dy' = dy silu(z) (fp32), written by the recompute pass
   const T* B;
   const T* C;
+  const float* Bf;  // B and C as fp32: the stage tiles, or (16-bit T) the warp's widened copy
+  const float* Cf;
   const float* ck;
   const int* tok;
   __device__ __forceinline__ explicit BwdStage(unsigned char* base) {
@@ -95,6 +100,8 @@ struct BwdStage {
     C = reinterpret_cast<const T*>(base + Cfg::OFF_C_B);
     ck = reinterpret_cast<const float*>(base + Cfg::OFF_CK_B);
     tok = reinterpret_cast<const int*>(base + Cfg::OFF_TOK_B);
+    Bf = reinterpret_cast<const float*>(B);
+    Cf = reinterpret_cast<const float*>(C);
   }
 };
 
@@ -179,8 +186,8 @@ __device__ __forceinline__ void bwd_rev_math(BwdLane& L, float2 (&hs)[2][4], flo
   const float2 u2 = ld_pair(S.u + r * DT + c0l);
   const float2 t2 = ld_pair(S.dt + r * DT + c0l);
   float2 B2[4], C2[4];
-  load8t(S.B + r * NS, pl, B2);
-  load8t(S.C + r * NS, pl, C2);
+  load8(S.Bf + r * NS, pl, B2);
+  load8(S.Cf + r * NS, pl, C2);
   const float2 du2 = mul2(t2, u2);
   const float2 dl2 = mul2(t2, bcast2(kLog2e));
   const float dyc[2] = {dy2.x, dy2.y}, duc[2] = {du2.x, du2.y}, dtc[2] = {t2.x, t2.y}, dlc[2] = {dl2.x, dl2.y};
@@ -269,7 +276,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
     const float2 u2 = ld_pair(S.u + r * DT + c0l);
     const float2 t2 = ld_pair(S.dt + r * DT + c0l);
     float2 B2[4];
-    load8t(S.B + r * NS, pl, B2);
+    load8(S.Bf + r * NS, pl, B2);
     const float2 du2 = mul2(t2, u2);
     const float2 dl2 = mul2(t2, bcast2(kLog2e));
     const float duc[2] = {du2.x, du2.y}, dlc[2] = {dl2.x, dl2.y};
@@ -292,7 +299,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
     }
     if (HAS_Z) {
       float2 C2[4];
-      load8t(S.C + r * NS, pl, C2);
+      load8(S.Cf + r * NS, pl, C2);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const float2 acc = add2(fma2(C2[1], h[c][1], mul2(C2[0], h[c][0])), fma2(C2[3], h[c][3], mul2(C2[2], h[c][2])));
@@ -549,7 +556,17 @@ __global__ void __launch_bounds__(BwdCfg<T>::NT, 2)
     alive = alive && mbar_wait(&full[st], ph, abort_flag, status);
     alive = __all_sync(0xffffffffu, alive);  // shuffles and tcgen05 below need the whole warp
     float* part = reinterpret_cast<float*>(smb + Cfg::OFF_PART_B) + (i & 1) * (TMAX * NCW * 32);
-    const BwdStage<T> S(smb + st * Cfg::STAGE_B);
+    BwdStage<T> S(smb + st * Cfg::STAGE_B);
+    if constexpr (!Cfg::F32) {
+      if (alive) {
+        float* bcf = reinterpret_cast<float*>(smb + Cfg::OFF_BCF_B) + warp * 2 * Cfg::BCT;
+        widen_bc_tile(S.B, bcf, lane);
+        widen_bc_tile(S.C, bcf + Cfg::BCT, lane);
+        __syncwarp();
+        S.Bf = bcf;
+        S.Cf = bcf + Cfg::BCT;
+      }
+    }
     const int nv = S.tok[TMAX];
     if (alive)
       bwd_box<T, HAS_Z, REV, SPLIT>(L, S, part, taddr, nv, warp, lane, c0l, pl, ib > 0, v0, v1, Down, du_b, dt_b, dz_b,

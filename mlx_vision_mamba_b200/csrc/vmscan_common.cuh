@@ -422,6 +422,24 @@ __device__ __forceinline__ void load8t<__nv_bfloat16>(const __nv_bfloat16* p, co
   }
 }
 
+// Widens a box's B or C tile (TMAX x 16 values of T) into fp32 once per
+// box, one warp: lane l converts values 8 l .. 8 l + 7.  For the bf16 I/O
+// variant the scans then read the fp32 copy every step (plain 128-bit loads)
+// instead of unpacking bf16 pairs at every use.
+__device__ __forceinline__ void widen_bc_tile(const __nv_bfloat16* src, float* dst, int lane) {
+  const uint4 q = *reinterpret_cast<const uint4*>(src + 8 * lane);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  float f[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    f[2 * k] = v.x;
+    f[2 * k + 1] = v.y;
+  }
+  *reinterpret_cast<float4*>(dst + 8 * lane) = make_float4(f[0], f[1], f[2], f[3]);
+  *reinterpret_cast<float4*>(dst + 8 * lane + 4) = make_float4(f[4], f[5], f[6], f[7]);
+}
+
 template <typename T>
 __device__ __forceinline__ void stg_if_t(T* p, float v, bool pred);
 template <>

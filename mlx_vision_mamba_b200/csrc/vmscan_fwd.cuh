@@ -43,7 +43,11 @@ struct FwdCfg {
   static constexpr int OFF_DT_B = TILE * ES, OFF_Z_B = 2 * TILE * ES, OFF_B_B = 3 * TILE * ES,
                        OFF_C_B = 3 * TILE * ES + BCT * ES, OFF_TOK_B = 3 * TILE * ES + 2 * BCT * ES;
   static constexpr int STAGE_B = (OFF_TOK_B + TOKF * 4 + 127) / 128 * 128;
-  static constexpr size_t SMEM_BYTES = size_t(NST) * STAGE_B + 2 * NST * 8 + 16 + 1024;
+  // 16-bit T: each consumer warp's fp32 copy of the box's B and C tiles, after
+  // the barriers
+  static constexpr int OFF_BCF_B = NST * STAGE_B + 128;
+  static constexpr int BCF_B = ES == 4 ? 0 : NCW * 2 * BCT * 4;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_BCF_B) + BCF_B + 1024;
 };
 
 // Chunked scan over L.  Chunk c holds boxes [c * bpc, min((c + 1) * bpc,
@@ -193,6 +197,20 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
       const T* __restrict__ sz = reinterpret_cast<const T*>(sb + Cfg::OFF_Z_B);
       const T* __restrict__ sB = reinterpret_cast<const T*>(sb + Cfg::OFF_B_B);
       const T* __restrict__ sC = reinterpret_cast<const T*>(sb + Cfg::OFF_C_B);
+      // B and C as fp32: the stage itself, or (16-bit T) this warp's widened copy
+      const float* __restrict__ sBf;
+      const float* __restrict__ sCf;
+      if constexpr (Cfg::ES == 4) {
+        sBf = reinterpret_cast<const float*>(sB);
+        sCf = reinterpret_cast<const float*>(sC);
+      } else {
+        float* bcf = reinterpret_cast<float*>(smb + Cfg::OFF_BCF_B) + warp * 2 * Cfg::BCT;
+        widen_bc_tile(sB, bcf, lane);
+        if (STORE_Y) widen_bc_tile(sC, bcf + Cfg::BCT, lane);
+        __syncwarp();
+        sBf = bcf;
+        sCf = bcf + Cfg::BCT;
+      }
       const int* tok = reinterpret_cast<const int*>(sb + Cfg::OFF_TOK_B);
       const int nv = tok[TMAX];
       auto math = [&](int s, Carry& k) {
@@ -200,7 +218,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
         const float2 u2 = ld_pair(su + r * DT + c0l);
         const float2 t2 = ld_pair(sdt + r * DT + c0l);
         float2 B2[4];
-        load8t(sB + r * NS, pl, B2);
+        load8(sBf + r * NS, pl, B2);
         const float2 du2 = mul2(t2, u2);
         const float2 dl2 = mul2(t2, bcast2(kLog2e));
         if (CARRY) dsum = add2(dsum, t2);
@@ -215,7 +233,7 @@ __global__ void __launch_bounds__(FwdCfg<NCW, T>::NT, 4)
         }
         if (STORE_Y) {
           float2 C2[4];
-          load8t(sC + r * NS, pl, C2);
+          load8(sCf + r * NS, pl, C2);
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float2 acc =
