@@ -15,7 +15,17 @@ from typing import Optional
 import torch
 import torch.nn as nn
 
+from .linear import linear_tc, supported as _tc_supported
 from .mamba_block import LayerNorm, MultiDirectionalMambaBlock
+
+
+def _patch_proj(x2: torch.Tensor, proj) -> torch.Tensor:
+    """(N, patch features) @ W^T + b for a patch embedding: on the tensor-core
+    GEMM (fp32 accuracy) when its operands qualify, else PyTorch's addmm."""
+    wt = proj.weight.reshape(proj.weight.shape[0], -1)
+    if _tc_supported(x2, wt):
+        return linear_tc(x2, wt) + proj.bias
+    return torch.addmm(proj.bias, x2, wt.t())
 
 
 def _mlx_conv_init(weight: torch.Tensor, fan_in: int) -> None:
@@ -41,8 +51,7 @@ class PatchEmbed(nn.Module):
         hp, wp = h // p, w // p
         x = x[:, : hp * p, : wp * p, :].reshape(b, hp, p, wp, p, c).permute(0, 1, 3, 2, 4, 5)
         x = x.reshape(b, hp * wp, p * p * c)
-        wt = self.proj.weight.reshape(self.proj.weight.shape[0], -1)
-        return torch.addmm(self.proj.bias, x.reshape(-1, x.shape[-1]), wt.t()).reshape(b, hp * wp, -1)
+        return _patch_proj(x.reshape(-1, x.shape[-1]), self.proj).reshape(b, hp * wp, -1)
 
 
 class PatchEmbed3D(nn.Module):
@@ -62,8 +71,7 @@ class PatchEmbed3D(nn.Module):
         dp, hp, wp = d // p, h // p, w // p
         x = x[:, : dp * p, : hp * p, : wp * p, :].reshape(b, dp, p, hp, p, wp, p, c)
         x = x.permute(0, 1, 3, 5, 2, 4, 6, 7).reshape(b, dp * hp * wp, p * p * p * c)
-        wt = self.proj.weight.reshape(self.proj.weight.shape[0], -1)
-        return torch.addmm(self.proj.bias, x.reshape(-1, x.shape[-1]), wt.t()).reshape(b, dp * hp * wp, -1)
+        return _patch_proj(x.reshape(-1, x.shape[-1]), self.proj).reshape(b, dp * hp * wp, -1)
 
 
 class PatchEmbed4D(nn.Module):
@@ -92,9 +100,7 @@ class PatchEmbed4D(nn.Module):
         cc = x.shape[-1]
         x = x[:, : dp * p, : hp * p, : wp * p, :].reshape(b * t_out, dp, p, hp, p, wp, p, cc)
         x = x.permute(0, 1, 3, 5, 2, 4, 6, 7).reshape(b * t_out * dp * hp * wp, p * p * p * cc)
-        wt = self.proj.weight.reshape(self.proj.weight.shape[0], -1)
-        y = torch.addmm(self.proj.bias, x, wt.t())
-        return y.reshape(b, t_out * dp * hp * wp, -1)
+        return _patch_proj(x, self.proj).reshape(b, t_out * dp * hp * wp, -1)
 
 
 class VisionMamba(nn.Module):
