@@ -71,7 +71,14 @@ struct GemmCfg {
   static constexpr uint32_t TMEM_COLS =
       (NB + 2) * BN <= 128 ? 128u : ((NB + 2) * BN <= 256 ? 256u : 512u);
   static constexpr int OFF_BAR = NST * STAGE_B;
-  static constexpr size_t SMEM_BYTES = size_t(OFF_BAR) + (2 * NST + 2 * NB + 2) * 8 + 16 + 1024;
+  static_assert((2 * NST + 2 * NB + 2) * 8 + 8 <= 256, "barriers, abort flag and TMEM slot fit in 256 bytes");
+  // per epilogue warp a 32-row x EPI_SC-column fp32 staging tile: the warp
+  // writes its rows (one per lane) there and stores whole row pieces to global
+  static constexpr int EPI_SC = BN / 2 < 32 ? BN / 2 : 32;
+  static constexpr int OFF_EPI = OFF_BAR + 256;
+  static constexpr int EPI_B = GM_EPI_WARPS * 32 * EPI_SC * 4;
+  static constexpr size_t SMEM_BYTES = size_t(OFF_EPI) + EPI_B + 1024;
+  static_assert(SMEM_BYTES <= 232448, "fits the 227 KB opt-in shared memory");
 };
 
 // ---- tcgen05 helpers ----
@@ -447,28 +454,53 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sme[c]);
       const int row = it.m0 + 32 * q + lane;
-      if (row >= args.M) continue;
-      float* out = args.C + int64_t(it.split) * args.split_stride + int64_t(row) * args.ldc;
+      float* tile = args.C + int64_t(it.split) * args.split_stride;
       const int col0 = it.n0 + h * HC;
       if (vec && col0 + HC <= args.N) {
+        // Through the warp's staging tile, SC columns per pass: lane l writes
+        // row l, then each store instruction covers 32 / TPR whole row pieces
+        // of SC * 4 bytes (rows strided by ldc) instead of 32 rows x 16 bytes.
+        // 16-byte chunk k of row r sits at chunk k ^ ((r / RPL) % TPR), so both
+        // the row-wise writes and the piece-wise reads hit distinct banks in
+        // every 8-lane phase.
+        constexpr int SC = Cfg::EPI_SC, TPR = SC / 4, RPL = 8 / TPR;
+        float* st = reinterpret_cast<float*>(smb + Cfg::OFF_EPI) + (warp - GM_EPI_WARP0) * 32 * SC;
 #pragma unroll
-        for (int x = 0; x < HC; x += 4) {
-          float4 v;
-          v.x = acc[x] + __uint_as_float(r[x]);
-          v.y = acc[x + 1] + __uint_as_float(r[x + 1]);
-          v.z = acc[x + 2] + __uint_as_float(r[x + 2]);
-          v.w = acc[x + 3] + __uint_as_float(r[x + 3]);
-          float4* dst = reinterpret_cast<float4*>(out + col0 + x);
-          if (args.accumulate) {
-            const float4 o = *dst;
-            v.x += o.x;
-            v.y += o.y;
-            v.z += o.z;
-            v.w += o.w;
+        for (int p = 0; p < HC; p += SC) {
+#pragma unroll
+          for (int k = 0; k < TPR; ++k) {
+            const int x = p + 4 * k;
+            float4 v;
+            v.x = acc[x] + __uint_as_float(r[x]);
+            v.y = acc[x + 1] + __uint_as_float(r[x + 1]);
+            v.z = acc[x + 2] + __uint_as_float(r[x + 2]);
+            v.w = acc[x + 3] + __uint_as_float(r[x + 3]);
+            reinterpret_cast<float4*>(st + lane * SC)[k ^ ((lane / RPL) & (TPR - 1))] = v;
           }
-          *dst = v;
+          __syncwarp();
+          const int k = lane % TPR;
+#pragma unroll
+          for (int i = 0; i < TPR; ++i) {
+            const int rr = i * (32 / TPR) + lane / TPR;
+            float4 v = reinterpret_cast<const float4*>(st + rr * SC)[k ^ ((rr / RPL) & (TPR - 1))];
+            const int grow = it.m0 + 32 * q + rr;
+            if (grow < args.M) {
+              float4* dst = reinterpret_cast<float4*>(tile + int64_t(grow) * args.ldc + col0 + p + 4 * k);
+              if (args.accumulate) {
+                const float4 o = *dst;
+                v.x += o.x;
+                v.y += o.y;
+                v.z += o.z;
+                v.w += o.w;
+              }
+              *dst = v;
+            }
+          }
+          __syncwarp();
         }
       } else {
+        if (row >= args.M) continue;
+        float* out = tile + int64_t(row) * args.ldc;
 #pragma unroll
         for (int x = 0; x < HC; ++x)
           if (col0 + x < args.N) {
