@@ -652,19 +652,34 @@ int encode_gemm_map(CUtensorMap* m, const char* what, const float* p, int64_t co
 // K splits of a GEMM: 1 while the output tiles fill the SMs, otherwise enough
 // splits to fill them with at least 4 k-blocks each (at most 32 splits; the
 // skinny weight gradients have a handful of tiles and K of 10^4).
+//
+// CTA pairs (256-row work items, cta_group::2 MMAs, 4 ring stages instead of
+// 3) for 128-column tiles with an MN-major A (the weight gradients, A = dY^T,
+// whose k-blocks arrive as 4 + 4 TMA boxes) when M is a multiple of 256, so
+// no pair has an empty half; the pairs then play the role of the SMs in the
+// split count.  Measured on one B200 (A/B, bench.py --gemm): in_proj weight
+// gradient (M 6144, N 384, K 12544) 0.408 -> 0.324 ms; with a K-major A the
+// pairs were 2-6 % slower (in_proj / out_proj forward and input gradients:
+// the two SMs wait for each other at every chain and tile hand-over).
 struct GemmPlan {
   int bn, tiles_n, tiles_m, splits, kb_per_split;
+  bool pair;
   size_t ws_bytes;
 };
 
-GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
+#ifndef VMSCAN_GEMM_PAIR
+#define VMSCAN_GEMM_PAIR 1
+#endif
+
+GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K, bool a_mn) {
   GemmPlan p;
   p.bn = gemm_bn(N);
+  p.pair = VMSCAN_GEMM_PAIR && a_mn && p.bn == 128 && M % (2 * GM_BM) == 0;
   p.tiles_n = int((N + p.bn - 1) / p.bn);
-  p.tiles_m = int((M + GM_BM - 1) / GM_BM);
+  p.tiles_m = int((M + GM_BM - 1) / GM_BM) / (p.pair ? 2 : 1);
   const int nkb = int((K + GM_BK - 1) / GM_BK);
   const int64_t tiles = int64_t(p.tiles_n) * p.tiles_m;
-  const int sms = sm_count();
+  const int sms = sm_count() / (p.pair ? 2 : 1);
   int s = 1;
   if (tiles < sms) s = int(std::min<int64_t>({int64_t(sms) / tiles, int64_t(nkb / 4), 32}));
   s = std::max(s, 1);
@@ -674,18 +689,36 @@ GemmPlan gemm_plan(int64_t M, int64_t N, int64_t K) {
   return p;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool PAIR = false>
 int launch_gemm(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtensorMap& bhi, const CUtensorMap& blo,
                 const GemmPlan& p, const GemmArgs& a, cudaStream_t s) {
-  using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tf32x3_kernel<BN, A_MN, B_MN>;
+  using Cfg = GemmCfg<BN, PAIR>;
+  auto kern = gemm_tf32x3_kernel<BN, A_MN, B_MN, PAIR>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::SMEM_BYTES)) != cudaSuccess)
     return fail(VMSCAN_ERR_LAUNCH, "cudaFuncSetAttribute(gemm_tf32x3_kernel) failed");
   int* st = status_ptr();
   if (st == nullptr) return fail(VMSCAN_ERR_LAUNCH, "status symbol unavailable");
   const int64_t items = int64_t(p.tiles_n) * p.tiles_m * p.splits;
-  const unsigned grid = unsigned(std::min<int64_t>(items, sm_count()));
-  kern<<<grid, GM_THREADS, Cfg::SMEM_BYTES, s>>>(ahi, alo, bhi, blo, a, st);
+  if constexpr (PAIR) {
+    // clusters of 2 CTAs, one pair per work item up to one pair per 2 SMs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2u * unsigned(std::min<int64_t>(items, sm_count() / 2)));
+    cfg.blockDim = dim3(GM_THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ahi, alo, bhi, blo, a, st);
+    if (e != cudaSuccess) return fail(VMSCAN_ERR_LAUNCH, "gemm (CTA pairs) launch: %s", cudaGetErrorString(e));
+  } else {
+    const unsigned grid = unsigned(std::min<int64_t>(items, sm_count()));
+    kern<<<grid, GM_THREADS, Cfg::SMEM_BYTES, s>>>(ahi, alo, bhi, blo, a, st);
+  }
   return check_launch();
 }
 
@@ -694,6 +727,8 @@ int launch_gemm_bn(const CUtensorMap& ahi, const CUtensorMap& alo, const CUtenso
                    const GemmPlan& p, const GemmArgs& a, cudaStream_t s) {
   if (p.bn == 32) return launch_gemm<32, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
   if (p.bn == 64) return launch_gemm<64, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
+  if constexpr (A_MN)
+    if (p.pair) return launch_gemm<128, A_MN, B_MN, true>(ahi, alo, bhi, blo, p, a, s);
   return launch_gemm<128, A_MN, B_MN>(ahi, alo, bhi, blo, p, a, s);
 }
 
@@ -1127,7 +1162,8 @@ int vmscan_tf32_split_multi(int count, const float* const* x, float* const* hi, 
 
 int64_t vmscan_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return -VMSCAN_ERR_SHAPE;
-  return int64_t(gemm_plan(M, N, K).ws_bytes);
+  // enough for either operand layout of A (CTA pairs may split K differently)
+  return int64_t(std::max(gemm_plan(M, N, K, false).ws_bytes, gemm_plan(M, N, K, true).ws_bytes));
 }
 
 int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const float* a_lo, int64_t lda,
@@ -1145,8 +1181,9 @@ int vmscan_gemm_tf32x3(int64_t M, int64_t N, int64_t K, const float* a_hi, const
   // A(m, k): K-major a[m * lda + k] (rows M), MN-major a[k * lda + m] (rows K)
   const int64_t acols = a_mn_major ? M : K, arows = a_mn_major ? K : M;
   const int64_t bcols = b_mn_major ? N : K, brows = b_mn_major ? K : N;
-  const GemmPlan p = gemm_plan(M, N, K);
-  const int abox = a_mn_major ? 32 : GM_BM, bbox = b_mn_major ? 32 : p.bn;
+  const GemmPlan p = gemm_plan(M, N, K, a_mn_major != 0);
+  // B box: the rows of B one CTA loads (half the tile's columns for a CTA pair)
+  const int abox = a_mn_major ? 32 : GM_BM, bbox = b_mn_major ? 32 : (p.pair ? p.bn / 2 : p.bn);
   VM_TRY(encode_gemm_map(&ahi, "a_hi", a_hi, acols, arows, lda, abox, a_mn_major != 0));
   VM_TRY(encode_gemm_map(&alo, "a_lo", a_lo, acols, arows, lda, abox, a_mn_major != 0));
   VM_TRY(encode_gemm_map(&bhi, "b_hi", b_hi, bcols, brows, ldb, bbox, b_mn_major != 0));

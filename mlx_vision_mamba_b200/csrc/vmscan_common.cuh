@@ -219,15 +219,27 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// CL: acquire at cluster scope (a barrier that the other CTA of a cluster
+// arrives on).
+template <bool CL = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
-      : "memory");
+  if constexpr (CL)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+        : "memory");
   return ok != 0;
 }
 
@@ -236,11 +248,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // thread of the CTA already aborted.
 // BACKOFF: sleep kBackoffNs between polls (a producer waiting for a stage to
 // drain would otherwise spend issue slots its consumers need).
-template <bool BACKOFF = false>
+template <bool BACKOFF = false, bool CL = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                           uint32_t limit = kWaitLimit) {
   for (uint32_t it = 0; it < limit; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<CL>(bar, parity)) return true;
     if (*abort_flag) return false;
     if (BACKOFF) __nanosleep(kBackoffNs);
   }

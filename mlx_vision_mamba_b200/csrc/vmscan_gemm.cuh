@@ -54,11 +54,18 @@ constexpr int GM_EPI_WARPS = 8;
 #define VMSCAN_GEMM_PK 3
 #endif
 
-template <int BN>
+// Ring stages and shared-memory layout of one CTA.  PAIR: the CTA is one of
+// a cluster pair that computes a 256 x BN tile with cta_group::2 MMAs; each
+// CTA holds its own 128 rows of A but only its half (BN / 2 rows) of B, so a
+// stage is 48 KB instead of 64 KB and the ring gets 4 stages instead of 3.
+template <int BN, bool PAIR = false>
 struct GemmCfg {
   static_assert(BN == 32 || BN == 64 || BN == 128, "BN: 32, 64 or 128");
+  static_assert(!PAIR || BN == 128, "CTA pairs use 128-column tiles");
+  static constexpr int BM = PAIR ? 2 * GM_BM : GM_BM;  // output rows of a work item
+  static constexpr int BROWS = PAIR ? BN / 2 : BN;      // rows of B one CTA loads
   static constexpr int A_TILE_B = GM_BM * GM_BK * 4;  // 16 KB
-  static constexpr int B_TILE_B = BN * GM_BK * 4;
+  static constexpr int B_TILE_B = BROWS * GM_BK * 4;
   static constexpr int OFF_ALO = A_TILE_B, OFF_BHI = 2 * A_TILE_B, OFF_BLO = 2 * A_TILE_B + B_TILE_B;
   static constexpr int STAGE_B = 2 * A_TILE_B + 2 * B_TILE_B;
   static constexpr int NST = (196 * 1024) / STAGE_B < 6 ? (196 * 1024) / STAGE_B : 6;
@@ -95,10 +102,11 @@ __device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
-// Instruction descriptor: D fp32, A and B tf32, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(int n, bool a_mn, bool b_mn) {
+// Instruction descriptor: D fp32, A and B tf32, M = m (128, or 256 for a CTA
+// pair), N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int n, bool a_mn, bool b_mn, int m = GM_BM) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
-         (uint32_t(n >> 3) << 17) | (uint32_t(GM_BM >> 4) << 24);
+         (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -115,6 +123,74 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint6
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// ---- CTA-pair (cta_group::2) helpers ----
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at p in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+// Every thread of both CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Tiled load into this CTA's shared memory whose bytes are counted on the
+// barrier at shared::cluster address `bar` (the pair leader's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// One 256 x N x 8 MMA of the pair, issued by the leader: A rows 0..127 and B
+// columns 0..N/2-1 from the leader's shared memory, A rows 128..255 and B
+// columns N/2..N-1 from the peer's (same offsets), D rows split the same way
+// over the two CTAs' TMEM.
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once the
+// pair's MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(uint16_t(3))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t r[32]) {
@@ -180,18 +256,30 @@ __global__ void tf32_split_multi_kernel(const __grid_constant__ SplitTable t) {
 // (r0 + 32 j, k0), 4 KB apart; boxes that would lie wholly past the operand's
 // last row are not issued (their smem rows only feed outputs that are not
 // stored).  Boxes that straddle the edge are zero-filled by the TMA.
-template <int ROWS, bool MN>
+// PAIR: the bytes are counted on the pair leader's barrier (bar_c, its
+// shared::cluster address) instead of bar.
+template <bool PAIR>
+__device__ __forceinline__ void gemm_tma(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t bar_c, int c0,
+                                         int c1) {
+  if constexpr (PAIR)
+    tma_load_2d_pair(dst, map, bar_c, c0, c1);
+  else
+    tma_load_2d(dst, map, bar, c0, c1);
+}
+
+template <int ROWS, bool MN, bool PAIR = false>
 __device__ __forceinline__ void gemm_load_operand(unsigned char* hi_dst, unsigned char* lo_dst, const CUtensorMap* mhi,
-                                                  const CUtensorMap* mlo, uint64_t* bar, int r0, int k0, int nbox) {
+                                                  const CUtensorMap* mlo, uint64_t* bar, uint32_t bar_c, int r0,
+                                                  int k0, int nbox) {
   if (!MN) {
-    tma_load_2d(hi_dst, mhi, bar, k0, r0);
-    tma_load_2d(lo_dst, mlo, bar, k0, r0);
+    gemm_tma<PAIR>(hi_dst, mhi, bar, bar_c, k0, r0);
+    gemm_tma<PAIR>(lo_dst, mlo, bar, bar_c, k0, r0);
   } else {
 #pragma unroll
     for (int j = 0; j < ROWS / 32; ++j) {
       if (j < nbox) {
-        tma_load_2d(hi_dst + j * 4096, mhi, bar, r0 + 32 * j, k0);
-        tma_load_2d(lo_dst + j * 4096, mlo, bar, r0 + 32 * j, k0);
+        gemm_tma<PAIR>(hi_dst + j * 4096, mhi, bar, bar_c, r0 + 32 * j, k0);
+        gemm_tma<PAIR>(lo_dst + j * 4096, mlo, bar, bar_c, r0 + 32 * j, k0);
       }
     }
   }
@@ -201,7 +289,7 @@ __device__ __forceinline__ void gemm_load_operand(unsigned char* hi_dst, unsigne
 // least one row (all ROWS/32 for a K-major operand, which loads one box).
 template <int ROWS, bool MN>
 __device__ __forceinline__ int gemm_nbox(int r0, int rows) {
-  return MN ? min(ROWS / 32, (rows - r0 + 31) / 32) : ROWS / 32;
+  return MN ? max(0, min(ROWS / 32, (rows - r0 + 31) / 32)) : ROWS / 32;
 }
 
 // Descriptor of the kk-th K=8 step of an operand tile.  K-major: rows of
@@ -261,13 +349,13 @@ struct GemmItem {
   int m0, n0, split, kb0, nkb;
 };
 
-__device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int w, int bn, int tiles_n) {
+__device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int w, int bm, int bn, int tiles_n) {
   GemmItem it;
   const int splits = a.splits;
   it.split = w % splits;
   const int t = w / splits;
   it.n0 = (t % tiles_n) * bn;
-  it.m0 = (t / tiles_n) * GM_BM;
+  it.m0 = (t / tiles_n) * bm;
   const int nkb_total = (a.K + GM_BK - 1) / GM_BK;
   it.kb0 = it.split * a.kb_per_split;
   it.nkb = max(0, min(a.kb_per_split, nkb_total - it.kb0));
@@ -292,12 +380,22 @@ __device__ __forceinline__ GemmItem gemm_item(const GemmArgs& a, int w, int bn, 
 // Roles (GM_THREADS = 320): warp 0 lane 0 TMA producer, warp 1 TMEM owner and
 // (lane 0) MMA issuer, warps 2..9 epilogue: warp w reads TMEM lane quarter
 // w % 4 and column half (w - 2) / 4 of the tile.
-template <int BN, bool A_MN, bool B_MN>
+//
+// PAIR (launched as clusters of 2 CTAs): the pair walks 256 x BN work items,
+// item w for cluster blockIdx.x / 2.  Each CTA's producer loads its 128 A rows
+// and its BN / 2 rows of B into its own ring, counting the bytes on the
+// leader's (rank 0) full barrier; only the leader's MMA thread issues, with
+// cta_group::2 MMAs whose commits arrive on the barrier of both CTAs (stage
+// free, chain ready); both CTAs' epilogues read their own TMEM rows and
+// report a drained buffer on the leader's barriers (16 warps).
+template <int BN, bool A_MN, bool B_MN, bool PAIR = false>
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
                        const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
                        const GemmArgs args, int* __restrict__ status) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, PAIR>;
+  constexpr int BM = Cfg::BM, BROWS = Cfg::BROWS;
+  constexpr int EPI_ARRIVALS = GM_EPI_WARPS * (PAIR ? 2 : 1);
   constexpr int NST = Cfg::NST;
   constexpr int HC = BN / 2;  // columns per epilogue warp
   extern __shared__ unsigned char smem_raw[];
@@ -313,8 +411,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = (args.N + BN - 1) / BN;
-  const int tiles_m = (args.M + GM_BM - 1) / GM_BM;
+  const int tiles_m = (args.M + BM - 1) / BM;
   const int items = tiles_m * tiles_n * args.splits;
+  // this CTA's first work item and stride (a pair shares its items), its rank in the pair
+  const int w0 = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int wstep = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -323,17 +425,22 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], GM_EPI_WARPS);
+      mbar_init(&acce[b], EPI_ARRIVALS);
     }
-    for (int c = 0; c < 2; ++c) mbar_init(&sme[c], GM_EPI_WARPS);
+    for (int c = 0; c < 2; ++c) mbar_init(&sme[c], EPI_ARRIVALS);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    else
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     tmem_fence_before_sync();
   }
   __syncthreads();
+  // a pair: both CTAs' barriers are initialised before any commit or load reaches them
+  if constexpr (PAIR) cluster_sync_all();
   tmem_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   // TMEM columns: large-product buffers at 0 and BN, correction buffers at 2 BN and 3 BN
@@ -346,11 +453,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     prefetch_tmap(&tb_lo);
     int g = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < items && ok; w += gridDim.x) {
-      const GemmItem it = gemm_item(args, w, BN, tiles_n);
-      const int nba = gemm_nbox<GM_BM, A_MN>(it.m0, args.M), nbb = gemm_nbox<BN, B_MN>(it.n0, args.N);
-      // bytes landing per stage: hi + lo of every issued box (32 x 32 fp32 = 4 KB)
-      const uint32_t tx = 2u * 4096u * uint32_t(nba + nbb);
+    for (int w = w0; w < items && ok; w += wstep) {
+      const GemmItem it = gemm_item(args, w, BM, BN, tiles_n);
+      // this CTA's A rows and B rows
+      const int am0 = it.m0 + GM_BM * int(rank), bn0 = it.n0 + BROWS * int(rank);
+      const int nba = gemm_nbox<GM_BM, A_MN>(am0, args.M), nbb = gemm_nbox<BROWS, B_MN>(bn0, args.N);
+      // bytes landing per stage on the (leader's) full barrier: hi + lo of
+      // every box the pair issues (32 x 32 fp32 = 4 KB)
+      int boxes = nba + nbb;
+      if constexpr (PAIR)
+        boxes = gemm_nbox<GM_BM, A_MN>(it.m0, args.M) + gemm_nbox<GM_BM, A_MN>(it.m0 + GM_BM, args.M) +
+                gemm_nbox<BROWS, B_MN>(it.n0, args.N) + gemm_nbox<BROWS, B_MN>(it.n0 + BROWS, args.N);
+      const uint32_t tx = 2u * 4096u * uint32_t(boxes);
       for (int i = 0; i < it.nkb; ++i, ++g) {
         const int s = g % NST;
         if (g >= NST && !mbar_wait<true>(&empty[s], uint32_t((g / NST) - 1) & 1u, abort_flag, status)) {
@@ -358,20 +472,24 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           break;
         }
         unsigned char* st = smb + s * Cfg::STAGE_B;
-        mbar_arrive_expect_tx(&full[s], tx);
+        if (rank == 0) mbar_arrive_expect_tx(&full[s], tx);
+        const uint32_t full_c = PAIR ? cluster_addr(&full[s], 0) : 0u;
         const int k0 = (it.kb0 + i) * GM_BK;
-        gemm_load_operand<GM_BM, A_MN>(st, st + Cfg::OFF_ALO, &ta_hi, &ta_lo, &full[s], it.m0, k0, nba);
-        gemm_load_operand<BN, B_MN>(st + Cfg::OFF_BHI, st + Cfg::OFF_BLO, &tb_hi, &tb_lo, &full[s], it.n0, k0,
-                                    nbb);
+        gemm_load_operand<GM_BM, A_MN, PAIR>(st, st + Cfg::OFF_ALO, &ta_hi, &ta_lo, &full[s], full_c, am0, k0, nba);
+        gemm_load_operand<BROWS, B_MN, PAIR>(st + Cfg::OFF_BHI, st + Cfg::OFF_BLO, &tb_hi, &tb_lo, &full[s], full_c,
+                                             bn0, k0, nbb);
       }
     }
     // Drain: the last load of every stage has landed before the CTA may exit
-    // (on the normal path the MMA warp consumed them all already).
-    for (int i = max(0, g - NST); i < g; ++i)
-      (void)mbar_wait<true>(&full[i % NST], uint32_t(i / NST) & 1u, abort_flag, status);
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN);
+    // (on the normal path the MMA warp consumed them all already).  A pair's
+    // loads all count on the leader's barriers, so the leader drains for both
+    // (the final cluster barrier keeps the peer until then).
+    if (rank == 0)
+      for (int i = max(0, g - NST); i < g; ++i)
+        (void)mbar_wait<true>(&full[i % NST], uint32_t(i / NST) & 1u, abort_flag, status);
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---- MMA issuer (a pair's leader) ----
+    constexpr uint32_t idesc = umma_idesc_tf32(BN, A_MN, B_MN, BM);
     // Operand descriptors of stage 0, K step 0: a stage or K step moves only the
     // 14-bit start-address field (shared addresses < 256 KB, so the addition
     // never carries out of it), which saves rebuilding 4 descriptors per K step
@@ -382,16 +500,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     constexpr uint32_t KS_A = (A_MN ? 1024u : 32u) >> 4, KS_B = (B_MN ? 1024u : 32u) >> 4;
     int g = 0, cg = 0, j = 0;  // k-blocks, promotion chains, items so far
     bool ok = true;
-    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
-      const GemmItem it = gemm_item(args, w, BN, tiles_n);
+    for (int w = w0; w < items && ok; w += wstep, ++j) {
+      const GemmItem it = gemm_item(args, w, BM, BN, tiles_n);
       const int c = j & 1;
       // correction buffer c last held item j - 2: wait until the epilogue read it
-      if (j >= 2 && !mbar_wait(&sme[c], uint32_t((j >> 1) - 1) & 1u, abort_flag, status)) break;
+      if (j >= 2 && !mbar_wait<false, PAIR>(&sme[c], uint32_t((j >> 1) - 1) & 1u, abort_flag, status)) break;
       const uint32_t d_small = tmem_base + uint32_t((NB + c) * BN);
       for (int i = 0; i < it.nkb; ++i, ++g) {
         const int s = g % NST, b = cg % NB, ci = i % PK;
         // a chain's first k-block: buffer b last held chain cg - NB; wait until the epilogue read it
-        if (ci == 0 && cg >= NB && !mbar_wait(&acce[b], uint32_t((cg / NB) - 1) & 1u, abort_flag, status)) {
+        if (ci == 0 && cg >= NB &&
+            !mbar_wait<false, PAIR>(&acce[b], uint32_t((cg / NB) - 1) & 1u, abort_flag, status)) {
           ok = false;
           break;
         }
@@ -406,13 +525,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int kk = 0; kk < GM_BK / 8; ++kk) {
           const uint64_t ahi = D_ahi + so + kk * KS_A, alo = D_alo + so + kk * KS_A;
           const uint64_t bhi = D_bhi + so + kk * KS_B, blo = D_blo + so + kk * KS_B;
-          umma_tf32(d_big, ahi, bhi, idesc, (ci > 0 || kk > 0) ? 1u : 0u);
-          umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-          umma_tf32(d_small, alo, bhi, idesc, 1u);
+          if constexpr (PAIR) {
+            umma_tf32_pair(d_big, ahi, bhi, idesc, (ci > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32_pair(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32_pair(d_small, alo, bhi, idesc, 1u);
+          } else {
+            umma_tf32(d_big, ahi, bhi, idesc, (ci > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32(d_small, ahi, blo, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_tf32(d_small, alo, bhi, idesc, 1u);
+          }
         }
-        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        // the stage is free once these MMAs have read it
+        if constexpr (PAIR)
+          umma_commit_pair(&empty[s]);
+        else
+          umma_commit(&empty[s]);
         if (ci == PK - 1 || i == it.nkb - 1) {
-          umma_commit(&accf[b]);  // buffer b holds this chain's large products
+          // buffer b holds this chain's large products
+          if constexpr (PAIR)
+            umma_commit_pair(&accf[b]);
+          else
+            umma_commit(&accf[b]);
           ++cg;
         }
       }
@@ -426,8 +559,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                      (args.split_stride % 4 == 0);
     int cg = 0, j = 0;  // promotion chains, items so far
     bool ok = true;
-    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++j) {
-      const GemmItem it = gemm_item(args, w, BN, tiles_n);
+    for (int w = w0; w < items && ok; w += wstep, ++j) {
+      const GemmItem it = gemm_item(args, w, BM, BN, tiles_n);
       float acc[HC];
 #pragma unroll
       for (int x = 0; x < HC; ++x) acc[x] = 0.f;
@@ -443,7 +576,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         for (int x = 0; x < HC; ++x) acc[x] += __uint_as_float(r[x]);
         tmem_fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[b]);
+        if (lane == 0) {
+          if constexpr (PAIR)
+            mbar_arrive_cluster(cluster_addr(&acce[b], 0));  // the leader's
+          else
+            mbar_arrive(&acce[b]);
+        }
       }
       if (!ok || it.nkb == 0) break;
       // the item's last chain commit also covered all of its correction-product MMAs
@@ -452,8 +590,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
       tmem_load_cols<HC>(lane_addr + uint32_t((NB + c) * BN), r);
       tmem_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sme[c]);
-      const int row = it.m0 + 32 * q + lane;
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(cluster_addr(&sme[c], 0));
+        else
+          mbar_arrive(&sme[c]);
+      }
+      const int mrow0 = it.m0 + GM_BM * int(rank) + 32 * q;  // this warp's first output row
+      const int row = mrow0 + lane;
       float* tile = args.C + int64_t(it.split) * args.split_stride;
       const int col0 = it.n0 + h * HC;
       if (vec && col0 + HC <= args.N) {
@@ -483,7 +627,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           for (int i = 0; i < TPR; ++i) {
             const int rr = i * (32 / TPR) + lane / TPR;
             float4 v = reinterpret_cast<const float4*>(st + rr * SC)[k ^ ((rr / RPL) & (TPR - 1))];
-            const int grow = it.m0 + 32 * q + rr;
+            const int grow = mrow0 + rr;
             if (grow < args.M) {
               float4* dst = reinterpret_cast<float4*>(tile + int64_t(grow) * args.ldc + col0 + p + 4 * k);
               if (args.accumulate) {
@@ -512,9 +656,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
   }
   tmem_fence_before_sync();
   __syncthreads();
+  // a pair: the leader's MMAs read the peer's shared memory and write its
+  // TMEM, and the peer's loads and arrivals reach the leader's barriers; both
+  // stay until the other is done
+  if constexpr (PAIR) cluster_sync_all();
   if (warp == 1) {
     tmem_fence_after_sync();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

@@ -30,7 +30,11 @@ def _operand(rows, cols, mn, gen, scale=1.0):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("m,n,k", [(200, 96, 72), (128, 128, 32), (260, 160, 100), (1568, 512, 384)])
+@pytest.mark.parametrize("m,n,k", [(200, 96, 72), (128, 128, 32), (260, 160, 100), (1568, 512, 384),
+                                   # M a multiple of 256 with 128-column tiles: CTA pairs when A is
+                                   # MN-major (one item; the second tile's peer half of B partly /
+                                   # wholly past N; K split over the pairs)
+                                   (256, 128, 64), (512, 200, 100), (768, 132, 4096), (2048, 384, 768)])
 def test_gemm_layouts(m, n, k, a_mn, b_mn):
     from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
 
@@ -100,6 +104,29 @@ def test_tf32_split_exact():
     assert int((lo.view(torch.int32) & low13).abs().sum()) == 0
     err = (hi.double() + lo.double() - x.double()).abs()
     assert bool((err <= x.double().abs() * 2.0 ** -21).all())
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
+def test_gemm_pair_output_slice_and_accumulate(a_mn, b_mn):
+    """M 512 (CTA-pair tiles when A is MN-major) writing a column slice of a
+    wider output (ldc 200), then C += A B^T on it; the columns outside the
+    slice stay untouched."""
+    from mlx_vision_mamba_b200.linear import gemm_tf32x3, tf32_split
+
+    gen = torch.Generator().manual_seed(23 + a_mn)
+    dev = torch.device("cuda", 0)
+    m, n, k, ld = 512, 160, 96, 200
+    a, a_st = _operand(m, k, a_mn, gen)
+    b, b_st = _operand(n, k, b_mn, gen)
+    a_s, b_s = tf32_split(a_st.float().to(dev)), tf32_split(b_st.float().to(dev))
+    out = torch.full((m, ld), 3.0, device=dev)
+    gemm_tf32x3(a_s, a_mn, b_s, b_mn, m, n, k, out=out[:, :n])
+    exact = a.float().double() @ b.float().double().t()
+    assert_parity("pair gemm slice", out[:, :n].cpu(), exact, a.float() @ b.float().t())
+    gemm_tf32x3(a_s, a_mn, b_s, b_mn, m, n, k, out=out[:, :n], accumulate=True)
+    assert_parity("pair gemm slice accumulate", out[:, :n].cpu(), 2.0 * exact, 2.0 * (a.float() @ b.float().t()))
+    assert bool((out[:, n:] == 3.0).all()), "columns outside the output slice were written"
+    assert device_status(dev, clear=True) == 0, "a bounded device wait of the GEMM gave up"
 
 
 def test_gemm_skinny_slices_and_accumulate():
