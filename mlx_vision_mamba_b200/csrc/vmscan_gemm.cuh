@@ -625,6 +625,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
           }
           __syncwarp();
           const int k = lane % TPR;
+          // C += A B: the pass's old values are all loaded before its first
+          // store (a load placed after a store through the same pointer
+          // would wait for it: one global round trip per row piece)
+          float4 old[TPR];
+          if (args.accumulate) {
+#pragma unroll
+            for (int i = 0; i < TPR; ++i) {
+              const int grow = mrow0 + i * (32 / TPR) + lane / TPR;
+              old[i] = grow < args.M ? *reinterpret_cast<const float4*>(tile + int64_t(grow) * args.ldc + col0 + p +
+                                                                         4 * k)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
 #pragma unroll
           for (int i = 0; i < TPR; ++i) {
             const int rr = i * (32 / TPR) + lane / TPR;
@@ -633,11 +646,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             if (grow < args.M) {
               float4* dst = reinterpret_cast<float4*>(tile + int64_t(grow) * args.ldc + col0 + p + 4 * k);
               if (args.accumulate) {
-                const float4 o = *dst;
-                v.x += o.x;
-                v.y += o.y;
-                v.z += o.z;
-                v.w += o.w;
+                v.x += old[i].x;
+                v.y += old[i].y;
+                v.z += old[i].z;
+                v.w += old[i].w;
               }
               *dst = v;
             }
