@@ -390,7 +390,10 @@ int vmscan_layernorm_bwd(int64_t rows, int64_t dim, const float* x, int64_t ldx,
  * operand pointers 16-byte aligned.  accumulate != 0 adds the product to C
  * (C += A B^T).  When the output tiles would not fill the GPU, K is split and
  * the partials are summed in a fixed order; that needs
- * vmscan_gemm_workspace_bytes(M, N, K) bytes of workspace (0: none).
+ * vmscan_gemm_workspace_bytes(M, N, K) bytes of workspace (0: none; the size
+ * covers either operand layout).  With an MN-major A, N > 64 and M a
+ * multiple of 256 (the weight gradients) the kernel runs as clusters of two
+ * CTAs; the call stays stream-ordered, synchronisation- and allocation-free.
  */
 int vmscan_tf32_split(int64_t n, const float* x, float* hi, float* lo, vmscan_stream_t stream);
 /* The same split for up to 16 tensors in one launch (x[k], hi[k], lo[k] of

@@ -25,6 +25,13 @@
 // chunks swizzled) or MN-major (rows of M or N contiguous: 32-element column
 // blocks of 32 K rows each, 4 KB apart, 32-byte chunks swizzled).  Every wait is bounded: on time-out the kernel
 // records VMSCAN_ERR_TIMEOUT in the device status and drains.
+//
+// Weight gradients (MN-major A, 128-column tiles, M a multiple of 256) run
+// as CTA pairs instead: clusters of 2 CTAs compute 256 x 128 items with
+// cta_group::2 MMAs issued by the leader, each CTA holding its 128 rows of A
+// and half of B, so the ring has 4 stages of 48 KB instead of 3 of 64 KB.
+// The pairs' TMA loads carry no multicast (the same code runs on every GPU
+// of a multi-GPU job).
 #pragma once
 
 #include "vmscan_common.cuh"
