@@ -137,7 +137,7 @@ __device__ __forceinline__ float dbc_reduce_scatter(const float2 vb[4], const fl
 // dA and dD sum batch x L terms per element, which in a plain running sum
 // would cost accuracy at elements whose exact value cancels to near zero.
 // dD is summed with Kahan compensation every step (dDcomp).  dA is summed in
-// short partials (about four reverse steps) that are folded into the running total
+// short partials (about eight reverse steps) that are folded into the running total
 // by Fast2Sum; the rounding error of each fold starts the next partial
 // (dAerr carries it across boxes), so only the products' own roundings
 // remain.
@@ -345,7 +345,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
   __syncwarp();
 
   // ---- reverse adjoint over the box ----
-  // dA partials of about four steps at a time (every other step pair),
+  // dA partials of about eight steps at a time (every fourth step pair),
   // folded into the running totals (fold_dA); the first starts at the error
   // left by the previous box's last fold
   float2 dAbox[2][4];
@@ -381,7 +381,7 @@ __device__ __forceinline__ void bwd_box(BwdLane& L, const BwdStage<T>& S, float*
     tmem_ld16(taddr + 16 * max(s - 2, 0), XB);
     bwd_rev_math<T, HAS_Z>(L, hs, dAbox, XA, S, row(s - 1), c0l, pl, ka);
     bwd_rev_epilogue(kb, S, part, warp, pl, Down, du_b, dt_b, sdus, sdts, ev);
-    if (pairs & 1) fold_dA(L, dAbox);
+    if ((pairs & 3) == 3) fold_dA(L, dAbox);
     tmem_wait_ld16(XB);
   }
   if (s == 0) {
